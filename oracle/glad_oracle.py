@@ -1,0 +1,337 @@
+"""Numpy restatement of the qrt INT8 GLAD forward (test infrastructure only).
+
+Arithmetic follows PyTorch eager semantics of the reference on each op:
+fp16 tensors are rounded to fp16 after every op, fp32 where the reference
+promotes, int8 x int8 products accumulate exactly in int32. Summation order
+inside float dot products is whatever numpy's BLAS picks -- the reference's
+own order is unspecified as well -- so only integer results are expected to
+match bit for bit; float results match within rounding.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+f16, f32, i8, i32 = np.float16, np.float32, np.int8, np.int32
+H1, W1, C1 = 21, 33, 3        # conv1 input (NHWC)           qrt/qconv.py:32
+H2, W2, C2 = 11, 17, 16       # conv1 output / conv2 input    qrt/qconv.py:33
+P = H2 * W2                   # 187 tokens                    qrt/qconv.py:34
+N2 = 64                       # conv2 output channels         qrt/qconv.py:35
+K1, K2S = 128, 64             # packed K sizes                qrt/qconv.py:37-38
+MAP = H1 * W1 * C1            # 2079
+INV127 = f32(1.0 / 127.0)
+
+
+def _mm16(a, b):
+    """fp16 @ fp16 -> fp16 with fp32 accumulation (torch CPU half matmul)."""
+    return np.matmul(a.astype(f32), b.astype(f32)).astype(f16)
+
+
+def _softmax16(x, axis):
+    """torch.softmax on fp16: computed in fp32, result rounded to fp16."""
+    x = x.astype(f32)
+    e = np.exp(x - x.max(axis=axis, keepdims=True))
+    return (e / e.sum(axis=axis, keepdims=True)).astype(f16)
+
+
+def _elu16(x):
+    x32 = x.astype(f32)
+    return np.where(x32 > 0, x32, np.expm1(x32)).astype(f16)
+
+
+def round_half_away(z):
+    """``where(z>=0, floor(z+0.5), ceil(z-0.5))`` in fp32 (qrt/qconv.py:100)."""
+    z = z.astype(f32)
+    return np.where(z >= 0, np.floor(z + f32(0.5)), np.ceil(z - f32(0.5))).astype(f32)
+
+
+# -- weight quantisation ------------------------------------------------------
+def requant_qlinear(weight, bias, alpha=None, beta=None, s_z=1.0):
+    """``QuantLinear.requantize_`` (qrt/qlinear.py:84-102).
+
+    Returns ``w8 [Np,K] int8, dq_scale [Np], s_w [Np], b_prime [Np]`` with the
+    rows padded to a multiple of 8 (qrt/qlinear.py:56,76-80; pad rows keep the
+    constructor's values: w8 0, scales 1, bias 0).
+    """
+    W = np.asarray(weight).astype(f32)
+    N, K = W.shape
+    b = np.asarray(bias).astype(f32) if bias is not None else np.zeros(N, f32)
+    if alpha is not None:
+        W = W / np.asarray(alpha, f32)[None, :]
+        beta = np.asarray(beta, f32) if beta is not None else np.zeros(K, f32)
+        b = (b - (W * beta[None, :]).sum(axis=1, dtype=f32)).astype(f32)
+    s_w = (np.maximum(np.abs(W).max(axis=1), f32(1e-8)) / f32(127.0)).astype(f32)
+    w8 = np.clip(np.rint(W / s_w[:, None]), -128, 127).astype(i8)
+    Np = N + (-N) % 8
+    w8p = np.zeros((Np, K), i8)
+    w8p[:N] = w8
+    dq = np.ones(Np, f32)
+    dq[:N] = s_w * f32(s_z)
+    swp = np.ones(Np, f32)
+    swp[:N] = s_w
+    bp = np.zeros(Np, f32)
+    bp[:N] = b
+    return w8p, dq, swp, bp
+
+
+def bn_affine16(weight, bias, mean, var, eps=1e-5):
+    """Eval BatchNorm as ``a*x+c``, evaluated on the fp16 copy's tensors:
+    ``a`` is computed in fp16 then widened (qrt/qconv.py:252-255)."""
+    w, bb, mu, v = (np.asarray(t).astype(f16) for t in (weight, bias, mean, var))
+    a = (w / np.sqrt((v + f16(eps)).astype(f16)).astype(f16)).astype(f16).astype(f32)
+    c = (bb.astype(f32) - a * mu.astype(f32)).astype(f32)
+    return a, c
+
+
+def requant_qcnn(sd, s_z, prefix="map_cnn."):
+    """``QuantCNN.requantize_`` without LET (qrt/qconv.py:247-284).
+
+    ``sd`` maps the fp16 model's names (``map_cnn.0.weight``...) to arrays.
+    """
+    g = lambda k: np.asarray(sd[prefix + k])  # noqa: E731
+    a1, c1 = bn_affine16(g("2.weight"), g("2.bias"), g("2.running_mean"), g("2.running_var"))
+    a2, c2 = bn_affine16(g("5.weight"), g("5.bias"), g("5.running_mean"), g("5.running_var"))
+    s_z = f32(s_z)
+    W1 = g("0.weight").astype(f32)                                 # [16,3,5,5]
+    w1p = np.zeros((8, 16, C2), f32)
+    w1p[:5, :15, :] = W1.transpose(2, 3, 1, 0).reshape(5, 15, C2)
+    W2 = g("3.weight").astype(f32)                                 # [64,16,3,3]
+    Wp = W2.transpose(2, 3, 1, 0).reshape(3, 48, N2)
+    s_w = (np.maximum(np.abs(Wp).max(axis=(0, 1)), f32(1e-8)) / f32(127.0)).astype(f32)
+    w8 = np.zeros((3, K2S, N2), i8)
+    w8[:, :48, :] = np.clip(np.rint(Wp / s_w[None, None, :]), -128, 127).astype(i8)
+    return {
+        "w1p": w1p.reshape(K1, C2).astype(f16), "b1f": g("0.bias").astype(f32),
+        "qa": (a1 / s_z).astype(f32), "qc": (c1 / s_z).astype(f32),
+        "w8": w8, "dq": (s_w * s_z).astype(f32), "b2f": g("3.bias").astype(f32),
+        "a2": a2, "c2": c2,
+    }
+
+
+# -- conv chain ---------------------------------------------------------------
+def conv1_im2col(x_nhwc):
+    """``[B*187, 128]`` fp16 A tile of ``_k_conv1_fused_q`` (qrt/qconv.py:64-87)."""
+    x = np.asarray(x_nhwc).astype(f16)
+    B = x.shape[0]
+    xp = np.zeros((B, H1 + 4, W1 + 4, C1), f16)                   # pad 2 each side
+    xp[:, 2:2 + H1, 2:2 + W1, :] = x
+    A = np.zeros((B, H2, W2, 8, 16), f16)
+    for kh in range(5):
+        for kw in range(5):
+            patch = xp[:, kh:kh + 2 * H2:2, kw:kw + 2 * W2:2, :]   # [B,11,17,3]
+            A[:, :, :, kh, kw * 3:kw * 3 + 3] = patch
+    return A.reshape(B * P, K1)
+
+
+def conv1_fused_q(x_nhwc, w1p, b1, qa, qc, return_z=False):
+    """Op ``qrt::conv1_fused_q`` -> z8 ``[B*187,16]`` (qrt/qconv.py:54-103)."""
+    A = conv1_im2col(x_nhwc)
+    acc = np.matmul(A.astype(f32), np.asarray(w1p).astype(f32), dtype=f32)
+    z = np.maximum(acc + np.asarray(b1, f32)[None, :], f32(0.0)).astype(f32)
+    z = (z * np.asarray(qa, f32)[None, :] + np.asarray(qc, f32)[None, :]).astype(f32)
+    q = np.clip(round_half_away(z), -128.0, 127.0).astype(i8)
+    return (q, z) if return_z else q
+
+
+def conv2_acc(z8, w8):
+    """int32 accumulators of ``_k_conv2_int8_fused`` (qrt/qconv.py:135-153)."""
+    z = np.asarray(z8).astype(np.int64).reshape(-1, H2, W2, C2)
+    B = z.shape[0]
+    zp = np.zeros((B, H2 + 2, W2 + 2, C2), np.int64)
+    zp[:, 1:1 + H2, 1:1 + W2, :] = z
+    w = np.asarray(w8).astype(np.int64)                           # [3, 64(ks), 64(n)]
+    acc = np.zeros((B, H2, W2, N2), np.int64)
+    for kh in range(3):
+        for kw in range(3):
+            tap = zp[:, kh:kh + H2, kw:kw + W2, :]                 # [B,11,17,16]
+            acc += np.einsum("bhwc,cn->bhwn", tap, w[kh, kw * 16:kw * 16 + 16, :])
+    return acc.reshape(B * P, N2).astype(i32)
+
+
+def conv2_epilogue(acc, dq, b2, a2, c2):
+    """``acc*dq + b`` -> ReLU -> BN2 -> fp16 (qrt/qconv.py:155-163)."""
+    y = (acc.astype(f32) * np.asarray(dq, f32)[None, :] + np.asarray(b2, f32)[None, :]).astype(f32)
+    y = np.maximum(y, f32(0.0))
+    y = (y * np.asarray(a2, f32)[None, :] + np.asarray(c2, f32)[None, :]).astype(f32)
+    return y.astype(f16)
+
+
+def conv2_int8_fused(z8, w8, dq, b2, a2, c2, return_acc=False):
+    """Op ``qrt::conv2_int8_fused`` -> ``[B*187,64]`` fp16 (qrt/qconv.py:116-163)."""
+    acc = conv2_acc(z8, w8)
+    y = conv2_epilogue(acc, dq, b2, a2, c2)
+    return (y, acc) if return_acc else y
+
+
+# -- QuantLinear --------------------------------------------------------------
+def qlinear_forward(x, L, act_mode="dynamic", out_features=None, aux=None):
+    """``QuantLinear.forward`` inference branch (qrt/qlinear.py:111-138).
+
+    ``L`` holds ``w8, dq_scale, s_w, b_prime, s_z, inv_sz`` and optionally
+    ``alpha, beta``. Returns fp16 ``[M, out_features]``.
+    """
+    x = np.asarray(x).astype(f16)
+    has_let = L.get("alpha") is not None
+    if has_let:
+        z = (x.astype(f32) * np.asarray(L["alpha"], f32)[None, :]).astype(f32)
+        z = (z + np.asarray(L["beta"], f32)[None, :]).astype(f32)
+    else:
+        z = x                                    # stays fp16 (0-d scale does not promote)
+    zt = z.dtype.type
+    if act_mode == "dynamic":
+        amax = np.abs(z).max() if z.size else zt(0)
+        s_z = (np.maximum(amax, zt(1e-8)) * zt(1.0 / 127.0)).astype(zt)
+        q = np.clip(np.rint((z / s_z).astype(zt)), -128, 127).astype(i8)
+        scale = (np.asarray(L["s_w"], f32) * f32(s_z)).astype(f32)
+    elif act_mode == "static":
+        s_z = f32(L["s_z"])
+        q = np.clip(np.rint((z * zt(L["inv_sz"])).astype(zt)), -128, 127).astype(i8)
+        scale = np.asarray(L["dq_scale"], f32)
+    else:
+        raise ValueError(f"unknown act_mode: {act_mode}")
+    acc = np.matmul(q.astype(np.int64), np.asarray(L["w8"]).astype(np.int64).T).astype(i32)
+    y = (acc.astype(f32) * scale[None, :]).astype(f32)
+    y = (y + np.asarray(L["b_prime"], f32)[None, :]).astype(f32)
+    n = out_features or y.shape[1]
+    if aux is not None:
+        aux.update(q=q, acc=acc, s_z=f32(s_z))
+    return y[:, :n].astype(f16)
+
+
+def linear16(x, w, b):
+    """fp16 ``F.linear`` (addmm, fp32 accumulation, one rounding)."""
+    y = np.matmul(np.asarray(x).astype(f32), np.asarray(w).astype(f32).T)
+    if b is not None:
+        y = y + np.asarray(b).astype(f32)[None, :]
+    return y.astype(f16)
+
+
+# -- top-k ----------------------------------------------------------------------
+def topk_lowest_index(logits, k):
+    """Top-k indices ordered by value descending, ties by index ascending."""
+    lg = np.asarray(logits).astype(f32)
+    order = np.lexsort((np.broadcast_to(np.arange(lg.shape[-1]), lg.shape), -lg), axis=-1)
+    return order[..., :k].astype(np.int64)
+
+
+# -- model-level forward --------------------------------------------------------
+class GladWeights:
+    """fp16 inference-copy parameters + qrt quantised buffers by qrt name."""
+
+    QL = ("actor_proprio_embedding", "query_projector", "actor.0", "actor.2", "actor.4", "actor.6")
+
+    def __init__(self, sd):
+        self.sd = {k: np.asarray(v) for k, v in sd.items()}
+
+    def ql(self, name):
+        s = self.sd
+        d = {k: s[f"{name}.{k}"] for k in ("w8", "dq_scale", "s_w", "b_prime", "s_z", "inv_sz")}
+        d["alpha"] = s.get(f"{name}.alpha")
+        d["beta"] = s.get(f"{name}.beta")
+        d["out_features"] = s[f"{name}.weight"].shape[0]
+        return d
+
+    def cnn(self):
+        return {k: self.sd[f"map_cnn.{k}"] for k in ("w1p", "b1f", "qa", "qc", "w8", "dq", "b2f", "a2", "c2")}
+
+    def __getitem__(self, k):
+        return self.sd[k]
+
+
+def encode(obs, Wt: GladWeights, act_mode="dynamic", proprio="actor", noise=None, aux=None):
+    """``_encode_terrain_opt`` over QuantCNN / QuantLinear (qrt/encoder_opt.py:41-123).
+
+    ``obs`` is the observation group (fp32 or fp16); it is cast to fp16 first,
+    as ``update_distribution_qrt`` does (qrt/integration.py:206). ``noise`` is
+    an optional additive perturbation of the top-k logits (the Gumbel term of
+    train-mode rollouts, qrt/encoder_opt.py:87-91).
+    """
+    obs16 = np.asarray(obs).astype(f16)
+    B = obs16.shape[0]
+    x_nhwc = obs16[:, -MAP:].reshape(B, H1, W1, C1)
+    c = Wt.cnn()
+    z8 = conv1_fused_q(x_nhwc, c["w1p"], c["b1f"], c["qa"], c["qc"])
+    local = conv2_int8_fused(z8, c["w8"], c["dq"], c["b2f"], c["a2"], c["c2"]).reshape(B, P, N2)
+    prop = obs16[:, :-MAP]
+    if proprio == "actor":
+        pe_aux = {}
+        L = Wt.ql("actor_proprio_embedding")
+        emb = qlinear_forward(prop, L, act_mode, L["out_features"], pe_aux)
+    else:
+        emb = linear16(prop, Wt["critic_proprio_embedding.weight"], Wt["critic_proprio_embedding.bias"])
+        pe_aux = {}
+    D = N2
+    w2 = np.concatenate([Wt["global_pool_selector.weight"], Wt["topk_scorer.weight"][:, :D]], 0)
+    logits2 = _mm16(local.reshape(B * P, D), w2.T).reshape(B, P, 2)
+    gc_logits = (logits2[..., 0].astype(f32) + Wt["global_pool_selector.bias"].astype(f32)).astype(f16)
+    score_local = logits2[..., 1]
+    gc_w = _softmax16(gc_logits, axis=1)                                      # [B,N]
+    gc = np.einsum("bn,bnd->bd", gc_w.astype(f32), local.astype(f32)).astype(f16)
+    qp_aux = {}
+    L = Wt.ql("query_projector")
+    qin = np.concatenate([gc, emb], axis=1)
+    query = qlinear_forward(qin, L, act_mode, L["out_features"], qp_aux)
+    sq = _mm16(query, Wt["topk_scorer.weight"][:, D:].T)
+    score_query = (sq.astype(f32) + Wt["topk_scorer.bias"].astype(f32)).astype(f16)   # [B,1]
+    topk_logits = (score_local.astype(f32) + score_query.astype(f32)).astype(f16)
+    pert = topk_logits if noise is None else (topk_logits.astype(f32) + np.asarray(noise, f32)).astype(f16)
+    idx = topk_lowest_index(pert, 32)
+    sparse = np.take_along_axis(local, idx[..., None], axis=1)               # [B,32,D]
+    Win, bin_ = Wt["mha.in_proj_weight"], Wt["mha.in_proj_bias"]
+    q = linear16_2step(query, Win[:D], bin_[:D])
+    k = linear16_2step(sparse.reshape(-1, D), Win[D:2 * D], bin_[D:2 * D]).reshape(B, 32, D)
+    v = linear16_2step(sparse.reshape(-1, D), Win[2 * D:], bin_[2 * D:]).reshape(B, 32, D)
+    H, hd = 16, 4
+    qh = q.reshape(B, H, 1, hd)
+    kh = k.reshape(B, 32, H, hd).transpose(0, 2, 1, 3)
+    vh = v.reshape(B, 32, H, hd).transpose(0, 2, 1, 3)
+    scores = (_mm16(qh, kh.transpose(0, 1, 3, 2)).astype(f32) * f32(0.5)).astype(f16)
+    attn = _softmax16(scores, axis=-1)                                        # [B,H,1,32]
+    oh = _mm16(attn, vh)                                                      # [B,H,1,4]
+    foot = linear16_2step(oh.reshape(B, D), Wt["mha.out_proj.weight"], Wt["mha.out_proj.bias"])
+    attn_w = attn[:, :, 0, :].astype(f32).mean(axis=1, keepdims=True).astype(f16)
+    enc = np.concatenate([foot, gc, prop], axis=1)
+    if aux is not None:
+        aux.update(z8=z8, local=local, emb=emb, gc_logits=gc_logits, score_local=score_local,
+                   gc_w=gc_w, gc=gc, query=query, score_query=score_query,
+                   topk_logits=topk_logits, topk_idx=idx, foothold=foot, attn_weights=attn_w,
+                   enc=enc, s_pe=pe_aux.get("s_z"), s_qp=qp_aux.get("s_z"),
+                   q_pe=pe_aux.get("q"), acc_pe=pe_aux.get("acc"),
+                   q_qp=qp_aux.get("q"), acc_qp=qp_aux.get("acc"))
+    return enc
+
+
+def linear16_2step(x, w, b):
+    """``x @ W.t() + b`` in fp16 as two eager ops (matmul, then add)
+    (qrt/encoder_opt.py:108-118)."""
+    y = _mm16(np.asarray(x), np.asarray(w).T)
+    return (y.astype(f32) + np.asarray(b).astype(f32)[None, :]).astype(f16)
+
+
+def actor_forward(obs, Wt: GladWeights, act_mode="dynamic", noise=None, aux=None):
+    """Compiled ``f_act`` of qrt (qrt/integration.py:129-131): encoder + the
+    INT8 actor MLP (``actor.0/2/4/6`` with ELU between, rsl_rl/networks/mlp.py:59-83).
+    Returns the action mean ``[B, 29]`` in fp32 (``.float()``, integration.py:206)."""
+    h = encode(obs, Wt, act_mode, "actor", noise, aux)
+    names = ("actor.0", "actor.2", "actor.4", "actor.6")
+    for i, n in enumerate(names):
+        L = Wt.ql(n)
+        la = {}
+        h = qlinear_forward(h, L, act_mode, L["out_features"], la)
+        if aux is not None:
+            aux[f"{n}.q"], aux[f"{n}.acc"], aux[f"{n}.s_z"] = la["q"], la["acc"], la["s_z"]
+        if i < 3:
+            h = _elu16(h)
+        if aux is not None:
+            aux[f"{n}.out"] = h
+    return h.astype(f32)
+
+
+def critic_forward(obs, Wt: GladWeights, act_mode="dynamic", aux=None):
+    """Compiled ``f_val`` (qrt/integration.py:133-135): same encoder with the
+    fp16 critic proprio embedding, fp16 critic MLP. Returns ``[B,1]`` fp32."""
+    h = encode(obs, Wt, act_mode, "critic", None, aux)
+    for i, n in enumerate(("critic.0", "critic.2", "critic.4", "critic.6")):
+        h = linear16(h, Wt[f"{n}.weight"], Wt[f"{n}.bias"])
+        if i < 3:
+            h = _elu16(h)
+    return h.astype(f32)

@@ -1,0 +1,83 @@
+"""Pin the numpy oracle to the reference (golden vectors made by running qrt)."""
+import numpy as np
+import pytest
+
+from oracle import glad_oracle as O
+
+QL = O.GladWeights.QL
+
+
+def cos(a, b):
+    a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
+    return float((a @ b) / np.sqrt((a @ a) * (b @ b)))
+
+
+@pytest.mark.parametrize("name", QL)
+def test_requant_qlinear_matches_reference(golden_weights, name):
+    w = golden_weights
+    w8, dq, sw, bp = O.requant_qlinear(w[f"{name}.weight"], w[f"{name}.bias"],
+                                       w[f"{name}.alpha"], w[f"{name}.beta"], w[f"{name}.s_z"])
+    assert np.array_equal(w8, w[f"{name}.w8"])
+    assert np.array_equal(dq, w[f"{name}.dq_scale"])
+    assert np.array_equal(sw, w[f"{name}.s_w"])
+    np.testing.assert_allclose(bp, w[f"{name}.b_prime"], rtol=0, atol=1e-6)
+
+
+def test_requant_qcnn_matches_reference(golden_weights):
+    c = O.requant_qcnn(golden_weights, golden_weights["map_cnn.s_z"])
+    for k, v in c.items():
+        assert np.array_equal(v, golden_weights[f"map_cnn.{k}"]), k
+
+
+def test_conv_chain_matches_reference_kernels(golden_weights, golden_conv):
+    w, g = golden_weights, golden_conv
+    z8 = O.conv1_fused_q(g["x_nhwc"], w["map_cnn.w1p"], w["map_cnn.b1f"], w["map_cnn.qa"], w["map_cnn.qc"])
+    assert np.array_equal(z8, g["z8"])
+    feat, acc = O.conv2_int8_fused(g["z8"], w["map_cnn.w8"], w["map_cnn.dq"], w["map_cnn.b2f"],
+                                   w["map_cnn.a2"], w["map_cnn.c2"], return_acc=True)
+    assert np.array_equal(feat, g["feat"])
+    assert np.abs(acc).max() < 2 ** 24
+
+
+def test_conv1_quant_error_bound(golden_weights, golden_conv):
+    """The reference's own kernel-1 bound (qrt/bench/_test_qconv.py:57-67)."""
+    s_z = float(golden_weights["map_cnn.s_z"])
+    z8 = O.conv1_fused_q(golden_conv["x_nhwc"], *(golden_weights[f"map_cnn.{k}"] for k in ("w1p", "b1f", "qa", "qc")))
+    z = z8.astype(np.float32).reshape(4, 11, 17, 16).transpose(0, 3, 1, 2) * s_z
+    ref = golden_conv["ref_bn1_fp32"]
+    inr = np.abs(ref) < 126.0 * s_z
+    assert np.abs(z - ref)[inr].max() < 2.0 * s_z + 1e-3
+
+
+def test_conv_chain_cosine_vs_fp32(golden_conv):
+    feat = golden_conv["feat"].astype(np.float32).reshape(4, 11, 17, 64).transpose(0, 3, 1, 2)
+    assert cos(feat, golden_conv["ref_chain_fp32"]) > 0.9995
+
+
+@pytest.mark.parametrize("B", [1, 3, 16])
+@pytest.mark.parametrize("mode", ["dynamic", "static"])
+def test_actor_forward_matches_reference(golden_weights, golden_fwd, B, mode):
+    d = golden_fwd[B]
+    aux = {}
+    mean = O.actor_forward(d["policy_obs"], O.GladWeights(golden_weights), mode, aux=aux)
+    ref = d[f"{mode}.mean"]
+    assert np.abs(mean - ref).max() <= 1e-3
+    assert cos(mean, ref) >= 0.99999
+    for a, b in zip(aux["topk_idx"], d[f"{mode}.topk_idx"]):
+        assert set(a.tolist()) == set(b.tolist())
+    assert np.array_equal(aux["emb"], d[f"{mode}.actor_proprio_embedding.out"])
+    # INT8 path stays close to the fp32 eager model (random init, README.md:240 style)
+    assert cos(mean, d["fp32.mean"]) > 0.999
+
+
+@pytest.mark.parametrize("B", [3, 16])
+def test_critic_forward_matches_reference(golden_weights, golden_fwd, B):
+    d = golden_fwd[B]
+    v = O.critic_forward(d["critic_obs"], O.GladWeights(golden_weights), "dynamic")
+    assert np.abs(v - d["dynamic.value"]).max() <= 1e-3
+
+
+def test_topk_tie_rule():
+    lg = np.array([[1.0, 3.0, 3.0, 2.0, 3.0]], np.float16)
+    assert O.topk_lowest_index(lg, 3).tolist() == [[1, 2, 4]]
+    assert O.topk_lowest_index(lg, 2).tolist() == [[1, 2]]
