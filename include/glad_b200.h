@@ -1,0 +1,197 @@
+/*
+ * glad_b200.h -- C ABI of the B200 (sm_100a) GLAD rollout forward.
+ *
+ * Plain pointers and sizes only. Every device pointer is a CUDA device
+ * address owned by the caller; `stream` is a cudaStream_t passed as void*.
+ * Functions return GLAD_OK (0) or a negative GLAD_ERR_* code; no exception
+ * crosses the ABI and glad_last_error() returns a message for the calling
+ * thread's last failure. Launches are asynchronous on `stream` and allocate
+ * nothing: scratch memory is the caller's `workspace`.
+ *
+ * Data types: "f16" = IEEE binary16, "f32" = binary32, "i8" = int8.
+ * Tensor layouts are the ones of the reference's qrt package (RL_Quant).
+ */
+#ifndef GLAD_B200_H_
+#define GLAD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLAD_OK 0
+#define GLAD_ERR_INVALID_ARG (-1)  /* bad pointer, size, alignment or mode */
+#define GLAD_ERR_CUDA (-2)         /* a CUDA runtime call failed            */
+#define GLAD_ERR_DEVICE (-3)       /* a kernel reported a device-side error */
+#define GLAD_ERR_UNSUPPORTED (-4)  /* no sm_100 device / feature not built   */
+#define GLAD_ERR_WORKSPACE (-5)    /* workspace missing or too small         */
+
+#define GLAD_DTYPE_F32 0
+#define GLAD_DTYPE_F16 1
+
+#define GLAD_ACT_STATIC 0   /* qrt QuantLinear act_mode="static"  (qrt/qlinear.py:132-135) */
+#define GLAD_ACT_DYNAMIC 1  /* qrt QuantLinear act_mode="dynamic" (qrt/qlinear.py:125-131) */
+
+/* Last error message of the calling thread ("" when none). */
+const char* glad_last_error(void);
+
+/* ABI version (major * 100 + minor). */
+int glad_abi_version(void);
+
+/* ---- weights ---------------------------------------------------------------
+ * QuantCNN buffers (qrt/qconv.py:236-244, filled by requantize_ :247-284):
+ *   w1p [128,16] f16 (k = kh*16 + kw*3 + c), b1f/qa/qc [16] f32,
+ *   w8 [3,64,64] i8 (kh; ks = kw*16 + c; n), dq/b2f/a2/c2 [64] f32.        */
+typedef struct GladConvWeights {
+  const void* w1p;
+  const float* b1f;
+  const float* qa;
+  const float* qc;
+  const int8_t* w8;
+  const float* dq;
+  const float* b2f;
+  const float* a2;
+  const float* c2;
+} GladConvWeights;
+
+/* QuantLinear buffers (qrt/qlinear.py:58-81): w8 [Np,K] i8 row-major,
+ * dq_scale/s_w/b_prime [Np] f32, alpha/beta [K] f32 (NULL without LET),
+ * s_z/inv_sz 0-d f32. Np = out_features rounded up to a multiple of 8.     */
+typedef struct GladQLinear {
+  const int8_t* w8;
+  const float* dq_scale;
+  const float* s_w;
+  const float* b_prime;
+  const float* alpha;
+  const float* beta;
+  const float* s_z;
+  const float* inv_sz;
+  int32_t in_features;
+  int32_t out_features;
+} GladQLinear;
+
+/* Every tensor the fused actor forward reads (qrt full mode: QuantCNN,
+ * LET W8A8 on actor_proprio_embedding, query_projector, actor.0/2/4/6;
+ * fp16 GPS selector, top-k scorer and MHA, qrt/integration.py:42-43).     */
+typedef struct GladActorWeights {
+  GladConvWeights conv;          /* map_cnn (QuantCNN)                      */
+  GladQLinear proprio_emb;       /* actor_proprio_embedding, 96 -> 64        */
+  GladQLinear query_proj;        /* query_projector, 128 -> 64               */
+  const void* gps_w;             /* global_pool_selector.weight f16 [1,64]   */
+  const void* gps_b;             /* global_pool_selector.bias   f16 [1]      */
+  const void* scorer_w;          /* topk_scorer.weight f16 [1,128]           */
+  const void* scorer_b;          /* topk_scorer.bias   f16 [1]               */
+  const void* mha_in_w;          /* mha.in_proj_weight f16 [192,64]          */
+  const void* mha_in_b;          /* mha.in_proj_bias   f16 [192]             */
+  const void* mha_out_w;         /* mha.out_proj.weight f16 [64,64]          */
+  const void* mha_out_b;         /* mha.out_proj.bias   f16 [64]             */
+  GladQLinear mlp[4];            /* actor.0 224->512, .2 ->256, .4 ->128, .6 ->29 */
+} GladActorWeights;
+
+/* Optional per-call outputs of the fused forward (any field may be NULL). */
+typedef struct GladActorAux {
+  int8_t* z8;            /* [B*187,16] i8   conv1 output (QuantCNN z8)          */
+  void* local;           /* [B,187,64] f16  local features (conv2 output)       */
+  void* gc_weights;      /* [B,187]   f16   global softmax pool weights         */
+  void* score_local;     /* [B,187]   f16   scorer logits of the local half     */
+  void* topk_logits;     /* [B,187]   f16   score_local + score_query           */
+  int64_t* topk_idx;     /* [B,32]    i64   value desc, ties by lower index     */
+  void* attn_weights;    /* [B,32]    f16   head-mean attention weights         */
+  void* encoded;         /* [B,224]   f16   cat(foothold, gc, proprio)          */
+  float* act_scales;     /* [6]       f32   per-layer s_z used by this call     */
+} GladActorAux;
+
+/* ---- qrt operator replacements -------------------------------------------- */
+
+/* torch.ops.qrt.conv1_fused_q (qrt/qconv.py:170-183, kernel :54-103):
+ * x_nhwc f16 [B,21,33,3] -> z8 i8 [B*187,16]. conv1 5x5/s2/p2 + bias + ReLU +
+ * BN1 + quantisation (round half away from zero, clamp to [-128,127]).     */
+int glad_conv1_fused_q(const void* x_nhwc, int64_t B, const GladConvWeights* w,
+                       int8_t* z8_out, void* stream);
+
+/* torch.ops.qrt.conv2_int8_fused (qrt/qconv.py:186-198, kernel :116-163):
+ * z8 i8 [B*187,16] -> f16 [B*187,64]. int8 x int8 -> int32 implicit GEMM,
+ * acc*dq + b, ReLU, BN2. `acc_out` (NULL or i32 [B*187,64]) receives the
+ * int32 accumulators.                                                     */
+int glad_conv2_int8_fused(const int8_t* z8, int64_t B, const GladConvWeights* w,
+                          void* feat_out, int32_t* acc_out, void* stream);
+
+/* QuantCNN.forward eval branch (qrt/qconv.py:297-303): both ops in one
+ * kernel; z8 never leaves the SM unless `z8_out` is non-NULL.              */
+int glad_conv_chain(const void* x_nhwc, int64_t B, const GladConvWeights* w,
+                    void* feat_out, int8_t* z8_out, void* stream);
+
+/* QuantLinear.forward inference branch (qrt/qlinear.py:111-138):
+ * x [M,K] (f16 or f32, row stride ldx elements) -> y f16 [M,N] (stride ldy).
+ * act_mode GLAD_ACT_STATIC uses the calibrated inv_sz; GLAD_ACT_DYNAMIC
+ * computes s_z = absmax(alpha*x+beta)/127 over the whole input first.
+ * `s_z_out` (NULL or f32 [1]) receives the scale used.                     */
+size_t glad_qlinear_workspace_size(void);
+int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int x_dtype,
+                         int64_t M, int64_t ldx, void* y, int64_t ldy, float* s_z_out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- fused rollout forward ---------------------------------------------------
+ * The compiled actor function of qrt full mode (qrt/integration.py:129-131;
+ * runtime.py:98-99): _encode_terrain_opt (qrt/encoder_opt.py:41-123) over
+ * QuantCNN/QuantLinear, then the INT8 actor MLP. obs [B, 96+2079] (f32 or
+ * f16, row stride ld_obs elements) -> mean f32 [B,29].
+ * `topk_noise` (NULL or f32 [B,187]) is added to the top-k logits before
+ * selection (the Gumbel term of train-mode rollouts, qrt/encoder_opt.py:87-91). */
+size_t glad_actor_workspace_size(int64_t B);
+int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                       int64_t ld_obs, int act_mode, const float* topk_noise, float* mean_out,
+                       const GladActorAux* aux, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Device-side status word of the last launches that used `workspace`
+ * (0 = fine; bits = a bounded wait ran out). Synchronises `stream`.        */
+int glad_workspace_status(const void* workspace, uint32_t* status, void* stream);
+
+/* ---- weight refresh (qrt/runtime.py:195-271) ------------------------------- */
+
+/* QuantLinear.requantize_ (qrt/qlinear.py:84-102) in place, for `n` layers in
+ * one launch. Source weights are the module's fp16 (or f32) parameters.     */
+typedef struct GladQLinearSrc {
+  const void* weight;   /* [N,K] */
+  const void* bias;     /* [N] or NULL */
+  int32_t w_dtype;      /* GLAD_DTYPE_F16 / F32, for weight and bias */
+  int32_t N, K, Np;
+  const float* alpha;   /* [K] or NULL */
+  const float* beta;    /* [K] or NULL */
+  const float* s_z;     /* 0-d */
+  int8_t* w8;           /* [Np,K] out */
+  float* dq_scale;      /* [Np] out   */
+  float* s_w;           /* [Np] out   */
+  float* b_prime;       /* [Np] out   */
+} GladQLinearSrc;
+int glad_requant_qlinear(const GladQLinearSrc* layers, int n, void* stream);
+
+/* QuantCNN.requantize_ without LET (qrt/qconv.py:247-284) in place. All
+ * parameters are the fp16 inference copy's (conv weights/biases, BN
+ * weight/bias/running stats); s_z 0-d f32; eps the BatchNorm eps.         */
+typedef struct GladQCNNSrc {
+  const void* conv1_w; const void* conv1_b;
+  const void* bn1_w; const void* bn1_b; const void* bn1_mean; const void* bn1_var;
+  const void* conv2_w; const void* conv2_b;
+  const void* bn2_w; const void* bn2_b; const void* bn2_mean; const void* bn2_var;
+  const float* s_z;
+  float eps1, eps2;
+  void* w1p; float* b1f; float* qa; float* qc;
+  int8_t* w8; float* dq; float* b2f; float* a2; float* c2;
+} GladQCNNSrc;
+int glad_requant_qcnn(const GladQCNNSrc* src, void* stream);
+
+/* The cast-copy half of sync_weights_from (qrt/runtime.py:251-253): n
+ * element-wise copies with dtype conversion in one launch.                  */
+typedef struct GladCastCopy {
+  const void* src; void* dst; int64_t n; int32_t src_dtype; int32_t dst_dtype;
+} GladCastCopy;
+int glad_cast_copy(const GladCastCopy* items, int n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GLAD_B200_H_ */

@@ -1,0 +1,502 @@
+// C-ABI entry points (include/glad_b200.h): argument checks, workspace
+// carve-up and launch order. No allocation happens here; every buffer is the
+// caller's.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "glad_common.cuh"
+
+namespace glad {
+size_t front_smem_bytes();
+template <int MODE>
+cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st);
+size_t tail_smem_bytes();
+cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st);
+template <int NT>
+cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st);
+size_t qgemm_smem_bytes(int K, int NT);
+cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
+                          const float* alpha, const float* beta, int round16, float* slot,
+                          int num_sms, cudaStream_t st);
+cudaError_t launch_act_scales(const float* slots, int act_mode, const float* const s_z[6],
+                              const int let[6], float* out, cudaStream_t st);
+cudaError_t launch_requant_qlinear(const GladQLinearSrc* layers, int n, cudaStream_t st);
+cudaError_t launch_requant_qcnn(const GladQCNNSrc& s, cudaStream_t st);
+cudaError_t launch_cast_copy(const GladCastCopy* items, int n, cudaStream_t st);
+}  // namespace glad
+
+using namespace glad;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(GLAD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define GLAD_CHECK_CUDA(expr, what)              \
+  do {                                           \
+    cudaError_t e_ = (expr);                     \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+};
+
+// Per-device properties, queried once per device.
+int device_info(DeviceInfo* out) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  static bool have[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(GLAD_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!have[dev]) {
+    DeviceInfo d;
+    e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(CC major)");
+    cache[dev] = d;
+    have[dev] = true;
+  }
+  if (cache[dev].major != 10)
+    return fail(GLAD_ERR_UNSUPPORTED, "device %d is sm_%d0; this library is built for sm_100a",
+                dev, cache[dev].major);
+  *out = cache[dev];
+  return GLAD_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_conv(const GladConvWeights* w, bool c1, bool c2) {
+  if (!w) return fail(GLAD_ERR_INVALID_ARG, "conv weights are NULL");
+  if (c1 && (!w->w1p || !w->b1f || !w->qa || !w->qc))
+    return fail(GLAD_ERR_INVALID_ARG, "conv1 buffers (w1p, b1f, qa, qc) must be set");
+  if (c2 && (!w->w8 || !w->dq || !w->b2f || !w->a2 || !w->c2))
+    return fail(GLAD_ERR_INVALID_ARG, "conv2 buffers (w8, dq, b2f, a2, c2) must be set");
+  return GLAD_OK;
+}
+
+// `gemm`: the layer runs through the tcgen05 GEMM (in_features % 8 == 0,
+// qrt/qlinear.py:52-53); otherwise it is the front kernel's dp4a embedding
+// (in_features % 4 == 0, <= 128).
+int check_ql(const GladQLinear* L, const char* name, int K, int N, bool gemm = true) {
+  if (!L->w8 || !L->dq_scale || !L->s_w || !L->b_prime || !L->s_z || !L->inv_sz)
+    return fail(GLAD_ERR_INVALID_ARG, "%s: QuantLinear buffers must be set", name);
+  if ((L->alpha == nullptr) != (L->beta == nullptr))
+    return fail(GLAD_ERR_INVALID_ARG, "%s: alpha and beta must both be set or both NULL", name);
+  if (K > 0 && L->in_features != K)
+    return fail(GLAD_ERR_INVALID_ARG, "%s: in_features %d, expected %d", name, L->in_features, K);
+  if (N > 0 && L->out_features != N)
+    return fail(GLAD_ERR_INVALID_ARG, "%s: out_features %d, expected %d", name, L->out_features, N);
+  if (gemm && (L->in_features <= 0 || L->in_features % 8 != 0 || L->in_features > 1024))
+    return fail(GLAD_ERR_INVALID_ARG, "%s: in_features %d must be a multiple of 8 in [8, 1024]",
+                name, L->in_features);
+  if (!gemm && (L->in_features <= 0 || L->in_features % 4 != 0 || L->in_features > 128))
+    return fail(GLAD_ERR_INVALID_ARG, "%s: in_features %d must be a multiple of 4 in [4, 128]",
+                name, L->in_features);
+  if (L->out_features <= 0) return fail(GLAD_ERR_INVALID_ARG, "%s: out_features must be > 0", name);
+  if (!aligned(L->w8, 16))
+    return fail(GLAD_ERR_INVALID_ARG, "%s: w8 must be 16-byte aligned", name);
+  return GLAD_OK;
+}
+
+int front_grid(int64_t B, const DeviceInfo& d, int per_sm) {
+  int64_t g = (int64_t)d.sms * per_sm;
+  return (int)(B < g ? B : g);
+}
+
+// Fused-forward workspace layout.
+struct ActorWs {
+  float* slots;
+  int8_t* z8;
+  __half* score_local;
+  __half* pe;
+  __half* enc;
+  __half* h1;
+  __half* h2;
+  __half* h3;
+  size_t bytes;
+};
+
+size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+ActorWs actor_ws(void* base, int64_t B) {
+  ActorWs w;
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += up256(n);
+    return r;
+  };
+  w.slots = reinterpret_cast<float*>(take(kSlotsBytes));
+  w.z8 = reinterpret_cast<int8_t*>(take((size_t)B * kTok * 16));
+  w.score_local = reinterpret_cast<__half*>(take((size_t)B * kTok * 2));
+  w.pe = reinterpret_cast<__half*>(take((size_t)B * kD * 2));
+  w.enc = reinterpret_cast<__half*>(take((size_t)B * kEnc * 2));
+  w.h1 = reinterpret_cast<__half*>(take((size_t)B * 512 * 2));
+  w.h2 = reinterpret_cast<__half*>(take((size_t)B * 256 * 2));
+  w.h3 = reinterpret_cast<__half*>(take((size_t)B * 128 * 2));
+  w.bytes = off;
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* glad_last_error(void) { return g_err; }
+
+int glad_abi_version(void) { return 100; }
+
+int glad_conv1_fused_q(const void* x_nhwc, int64_t B, const GladConvWeights* w, int8_t* z8_out,
+                       void* stream) {
+  g_err[0] = 0;
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (B == 0) return GLAD_OK;
+  if (!x_nhwc || !z8_out) return fail(GLAD_ERR_INVALID_ARG, "x_nhwc and z8_out must be set");
+  if (!aligned(x_nhwc, 4) || !aligned(z8_out, 16))
+    return fail(GLAD_ERR_INVALID_ARG, "x_nhwc must be 4-byte and z8_out 16-byte aligned");
+  int rc = check_conv(w, true, false);
+  if (rc) return rc;
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  FrontParams p{};
+  p.in = x_nhwc;
+  p.ld = kMap;
+  p.in_dtype = GLAD_DTYPE_F16;
+  p.B = B;
+  p.conv = *w;
+  p.z8_out = z8_out;
+  GLAD_CHECK_CUDA(launch_front<kModeConv1>(p, front_grid(B, d, 4), (cudaStream_t)stream),
+                  "conv1 launch");
+  return GLAD_OK;
+}
+
+int glad_conv2_int8_fused(const int8_t* z8, int64_t B, const GladConvWeights* w, void* feat_out,
+                          int32_t* acc_out, void* stream) {
+  g_err[0] = 0;
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (B == 0) return GLAD_OK;
+  if (!z8 || !feat_out) return fail(GLAD_ERR_INVALID_ARG, "z8 and feat_out must be set");
+  if (!aligned(z8, 16) || !aligned(feat_out, 16) || (acc_out && !aligned(acc_out, 16)))
+    return fail(GLAD_ERR_INVALID_ARG, "z8, feat_out and acc_out must be 16-byte aligned");
+  int rc = check_conv(w, false, true);
+  if (rc) return rc;
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  FrontParams p{};
+  p.in = z8;
+  p.ld = kTok * 16;
+  p.in_dtype = GLAD_DTYPE_F16;
+  p.B = B;
+  p.conv = *w;
+  p.feat_out = reinterpret_cast<__half*>(feat_out);
+  p.acc_out = acc_out;
+  GLAD_CHECK_CUDA(launch_front<kModeConv2>(p, front_grid(B, d, 4), (cudaStream_t)stream),
+                  "conv2 launch");
+  return GLAD_OK;
+}
+
+int glad_conv_chain(const void* x_nhwc, int64_t B, const GladConvWeights* w, void* feat_out,
+                    int8_t* z8_out, void* stream) {
+  g_err[0] = 0;
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (B == 0) return GLAD_OK;
+  if (!x_nhwc || !feat_out) return fail(GLAD_ERR_INVALID_ARG, "x_nhwc and feat_out must be set");
+  if (!aligned(x_nhwc, 4) || !aligned(feat_out, 16) || (z8_out && !aligned(z8_out, 16)))
+    return fail(GLAD_ERR_INVALID_ARG, "x_nhwc 4-byte, feat_out/z8_out 16-byte alignment required");
+  int rc = check_conv(w, true, true);
+  if (rc) return rc;
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  FrontParams p{};
+  p.in = x_nhwc;
+  p.ld = kMap;
+  p.in_dtype = GLAD_DTYPE_F16;
+  p.B = B;
+  p.conv = *w;
+  p.feat_out = reinterpret_cast<__half*>(feat_out);
+  p.z8_out = z8_out;
+  GLAD_CHECK_CUDA(launch_front<kModeChain>(p, front_grid(B, d, 4), (cudaStream_t)stream),
+                  "conv chain launch");
+  return GLAD_OK;
+}
+
+size_t glad_qlinear_workspace_size(void) { return kSlotsBytes; }
+
+int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int x_dtype, int64_t M,
+                         int64_t ldx, void* y, int64_t ldy, float* s_z_out, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!L) return fail(GLAD_ERR_INVALID_ARG, "layer is NULL");
+  int rc = check_ql(L, "qlinear", 0, 0);
+  if (rc) return rc;
+  if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown act_mode %d", act_mode);
+  if (x_dtype != GLAD_DTYPE_F16 && x_dtype != GLAD_DTYPE_F32)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown x dtype %d", x_dtype);
+  if (M < 0) return fail(GLAD_ERR_INVALID_ARG, "M must be >= 0");
+  if (M == 0) return GLAD_OK;
+  if (!x || !y) return fail(GLAD_ERR_INVALID_ARG, "x and y must be set");
+  if (ldx < L->in_features || ldy < L->out_features)
+    return fail(GLAD_ERR_INVALID_ARG, "row strides smaller than the row length");
+  if (!workspace || workspace_bytes < kSlotsBytes)
+    return fail(GLAD_ERR_WORKSPACE, "workspace of %zu bytes required", (size_t)kSlotsBytes);
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  float* slots = reinterpret_cast<float*>(workspace);
+  GLAD_CHECK_CUDA(cudaMemsetAsync(slots, 0, kSlotsBytes, st), "workspace reset");
+  if (act_mode == GLAD_ACT_DYNAMIC)
+    GLAD_CHECK_CUDA(launch_absmax(x, x_dtype, M, ldx, L->in_features, L->alpha, L->beta, 0,
+                                  &slots[0], d.sms, st),
+                    "absmax launch");
+  GemmParams p{};
+  p.L = *L;
+  p.act_mode = act_mode;
+  p.slot = 0;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.M = M;
+  p.ldx = ldx;
+  if (x_dtype == GLAD_DTYPE_F16) {
+    p.y = reinterpret_cast<__half*>(y);
+    p.ldy = ldy;
+  } else {
+    p.y32 = reinterpret_cast<float*>(y);
+    p.ldy32 = ldy;
+  }
+  p.next_slot = -1;
+  p.slots = slots;
+  const size_t smem128 = qgemm_smem_bytes(L->in_features, 128);
+  if (smem128 <= 220 * 1024)
+    GLAD_CHECK_CUDA(launch_qgemm<128>(p, st), "qlinear launch");
+  else
+    GLAD_CHECK_CUDA(launch_qgemm<32>(p, st), "qlinear launch");
+  if (s_z_out) {
+    const float* sz[6] = {L->s_z, L->s_z, L->s_z, L->s_z, L->s_z, L->s_z};
+    const int let[6] = {L->alpha != nullptr, 0, 0, 0, 0, 0};
+    GLAD_CHECK_CUDA(launch_act_scales(slots, act_mode, sz, let, s_z_out, st), "scale launch");
+  }
+  return GLAD_OK;
+}
+
+size_t glad_actor_workspace_size(int64_t B) { return actor_ws(nullptr, B < 0 ? 0 : B).bytes; }
+
+int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                       int64_t ld_obs, int act_mode, const float* topk_noise, float* mean_out,
+                       const GladActorAux* aux, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  g_err[0] = 0;
+  if (!w) return fail(GLAD_ERR_INVALID_ARG, "weights are NULL");
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown act_mode %d", act_mode);
+  if (obs_dtype != GLAD_DTYPE_F16 && obs_dtype != GLAD_DTYPE_F32)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown obs dtype %d", obs_dtype);
+  const int P = w->proprio_emb.in_features;
+  if (P != 96)
+    return fail(GLAD_ERR_INVALID_ARG, "actor proprio width %d; the fused path is built for 96", P);
+  if (ld_obs < P + kMap) return fail(GLAD_ERR_INVALID_ARG, "ld_obs %lld < %d", (long long)ld_obs, P + kMap);
+  if (B == 0) return GLAD_OK;
+  if (!obs || !mean_out) return fail(GLAD_ERR_INVALID_ARG, "obs and mean_out must be set");
+  if (!aligned(obs, obs_dtype == GLAD_DTYPE_F32 ? 4 : 2))
+    return fail(GLAD_ERR_INVALID_ARG, "obs is not element-aligned");
+  int rc = check_conv(&w->conv, true, true);
+  if (rc) return rc;
+  if ((rc = check_ql(&w->proprio_emb, "actor_proprio_embedding", 96, 64, false))) return rc;
+  if ((rc = check_ql(&w->query_proj, "query_projector", 128, 64))) return rc;
+  const int mk[4] = {224, 512, 256, 128}, mn[4] = {512, 256, 128, kActions};
+  for (int i = 0; i < 4; ++i)
+    if ((rc = check_ql(&w->mlp[i], "actor MLP layer", mk[i], mn[i]))) return rc;
+  if (!w->gps_w || !w->gps_b || !w->scorer_w || !w->scorer_b || !w->mha_in_w || !w->mha_in_b ||
+      !w->mha_out_w || !w->mha_out_b)
+    return fail(GLAD_ERR_INVALID_ARG, "fp16 encoder weights must be set");
+  if (!aligned(w->mha_in_w, 16) || !aligned(w->mha_out_w, 16) || !aligned(w->query_proj.w8, 16))
+    return fail(GLAD_ERR_INVALID_ARG, "MHA / query_projector weights must be 16-byte aligned");
+  const ActorWs ws = actor_ws(workspace, B);
+  if (!workspace || workspace_bytes < ws.bytes)
+    return fail(GLAD_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", ws.bytes,
+                workspace_bytes);
+  if (!aligned(workspace, 256)) return fail(GLAD_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const GladActorAux none{};
+  const GladActorAux& ax = aux ? *aux : none;
+  int8_t* z8 = ax.z8 ? ax.z8 : ws.z8;
+  __half* score_local = ax.score_local ? reinterpret_cast<__half*>(ax.score_local) : ws.score_local;
+  __half* enc = ax.encoded ? reinterpret_cast<__half*>(ax.encoded) : ws.enc;
+  if (!aligned(z8, 16) || !aligned(enc, 16))
+    return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded must be 16-byte aligned");
+
+  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
+  if (act_mode == GLAD_ACT_DYNAMIC)
+    GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb.alpha,
+                                  w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st),
+                    "absmax launch");
+  FrontParams fp{};
+  fp.in = obs;
+  fp.ld = ld_obs;
+  fp.in_dtype = obs_dtype;
+  fp.prop_dim = P;
+  fp.B = B;
+  fp.conv = w->conv;
+  fp.gps_w = reinterpret_cast<const __half*>(w->gps_w);
+  fp.gps_b = reinterpret_cast<const __half*>(w->gps_b);
+  fp.scorer_w = reinterpret_cast<const __half*>(w->scorer_w);
+  fp.pe = w->proprio_emb;
+  fp.qp = w->query_proj;
+  fp.act_mode = act_mode;
+  fp.z8_out = z8;
+  fp.feat_out = reinterpret_cast<__half*>(ax.local);
+  fp.score_local = score_local;
+  fp.gc_w_out = reinterpret_cast<__half*>(ax.gc_weights);
+  fp.enc = enc;
+  fp.pe_out = ws.pe;
+  fp.slots = ws.slots;
+  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 4), st), "front launch");
+
+  TailParams tp{};
+  tp.B = B;
+  tp.conv = w->conv;
+  tp.qp = w->query_proj;
+  tp.scorer_w = reinterpret_cast<const __half*>(w->scorer_w);
+  tp.scorer_b = reinterpret_cast<const __half*>(w->scorer_b);
+  tp.in_w = reinterpret_cast<const __half*>(w->mha_in_w);
+  tp.in_b = reinterpret_cast<const __half*>(w->mha_in_b);
+  tp.out_w = reinterpret_cast<const __half*>(w->mha_out_w);
+  tp.out_b = reinterpret_cast<const __half*>(w->mha_out_b);
+  tp.a0_alpha = w->mlp[0].alpha;
+  tp.a0_beta = w->mlp[0].beta;
+  tp.act_mode = act_mode;
+  tp.noise = topk_noise;
+  tp.z8 = z8;
+  tp.score_local = score_local;
+  tp.pe = ws.pe;
+  tp.enc = enc;
+  tp.topk_logits_out = reinterpret_cast<__half*>(ax.topk_logits);
+  tp.topk_idx_out = ax.topk_idx;
+  tp.attn_w_out = reinterpret_cast<__half*>(ax.attn_weights);
+  tp.slots = ws.slots;
+  const int64_t groups = (B + 3) / 4;
+  const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
+  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st), "tail launch");
+
+  __half* hs[4] = {enc, ws.h1, ws.h2, ws.h3};
+  for (int i = 0; i < 4; ++i) {
+    GemmParams g{};
+    g.L = w->mlp[i];
+    g.act_mode = act_mode;
+    g.slot = 2 + i;
+    g.x = hs[i];
+    g.x_dtype = GLAD_DTYPE_F16;
+    g.M = B;
+    g.ldx = mk[i];
+    g.slots = ws.slots;
+    if (i < 3) {
+      g.y = hs[i + 1];
+      g.ldy = mn[i];
+      g.elu = 1;
+      g.next_alpha = w->mlp[i + 1].alpha;
+      g.next_beta = w->mlp[i + 1].beta;
+      g.next_let = w->mlp[i + 1].alpha != nullptr;
+      g.next_slot = 3 + i;
+      GLAD_CHECK_CUDA(launch_qgemm<128>(g, st), "actor MLP launch");
+    } else {
+      g.y32 = mean_out;
+      g.ldy32 = kActions;
+      g.next_slot = -1;
+      GLAD_CHECK_CUDA(launch_qgemm<32>(g, st), "actor head launch");
+    }
+  }
+  if (ax.act_scales) {
+    const float* sz[6] = {w->proprio_emb.s_z, w->query_proj.s_z, w->mlp[0].s_z,
+                          w->mlp[1].s_z, w->mlp[2].s_z, w->mlp[3].s_z};
+    const int let[6] = {w->proprio_emb.alpha != nullptr, w->query_proj.alpha != nullptr,
+                        w->mlp[0].alpha != nullptr, w->mlp[1].alpha != nullptr,
+                        w->mlp[2].alpha != nullptr, w->mlp[3].alpha != nullptr};
+    GLAD_CHECK_CUDA(launch_act_scales(ws.slots, act_mode, sz, let, ax.act_scales, st),
+                    "scale launch");
+  }
+  return GLAD_OK;
+}
+
+int glad_workspace_status(const void* workspace, uint32_t* status, void* stream) {
+  g_err[0] = 0;
+  if (!workspace || !status) return fail(GLAD_ERR_INVALID_ARG, "workspace and status must be set");
+  cudaStream_t st = (cudaStream_t)stream;
+  const float* slots = reinterpret_cast<const float*>(workspace);
+  GLAD_CHECK_CUDA(cudaMemcpyAsync(status, slots + kSlotStatus, sizeof(uint32_t),
+                                  cudaMemcpyDeviceToHost, st),
+                  "status copy");
+  GLAD_CHECK_CUDA(cudaStreamSynchronize(st), "status sync");
+  return *status ? fail(GLAD_ERR_DEVICE, "device status 0x%x", *status) : GLAD_OK;
+}
+
+int glad_requant_qlinear(const GladQLinearSrc* layers, int n, void* stream) {
+  g_err[0] = 0;
+  if (n < 0 || n > 16) return fail(GLAD_ERR_INVALID_ARG, "between 0 and 16 layers per call");
+  if (n == 0) return GLAD_OK;
+  if (!layers) return fail(GLAD_ERR_INVALID_ARG, "layers is NULL");
+  for (int i = 0; i < n; ++i) {
+    const GladQLinearSrc& l = layers[i];
+    if (!l.weight || !l.w8 || !l.dq_scale || !l.s_w || !l.b_prime || !l.s_z)
+      return fail(GLAD_ERR_INVALID_ARG, "layer %d: buffers must be set", i);
+    if (l.N <= 0 || l.K <= 0 || l.Np < l.N)
+      return fail(GLAD_ERR_INVALID_ARG, "layer %d: bad sizes N=%d K=%d Np=%d", i, l.N, l.K, l.Np);
+    if (l.w_dtype != GLAD_DTYPE_F16 && l.w_dtype != GLAD_DTYPE_F32)
+      return fail(GLAD_ERR_INVALID_ARG, "layer %d: unknown dtype", i);
+  }
+  GLAD_CHECK_CUDA(launch_requant_qlinear(layers, n, (cudaStream_t)stream), "requant launch");
+  return GLAD_OK;
+}
+
+int glad_requant_qcnn(const GladQCNNSrc* s, void* stream) {
+  g_err[0] = 0;
+  if (!s || !s->conv1_w || !s->conv1_b || !s->bn1_w || !s->bn1_b || !s->bn1_mean || !s->bn1_var ||
+      !s->conv2_w || !s->conv2_b || !s->bn2_w || !s->bn2_b || !s->bn2_mean || !s->bn2_var ||
+      !s->s_z || !s->w1p || !s->b1f || !s->qa || !s->qc || !s->w8 || !s->dq || !s->b2f || !s->a2 ||
+      !s->c2)
+    return fail(GLAD_ERR_INVALID_ARG, "QuantCNN requant: every buffer must be set");
+  GLAD_CHECK_CUDA(launch_requant_qcnn(*s, (cudaStream_t)stream), "requant launch");
+  return GLAD_OK;
+}
+
+int glad_cast_copy(const GladCastCopy* items, int n, void* stream) {
+  g_err[0] = 0;
+  if (n < 0) return fail(GLAD_ERR_INVALID_ARG, "n must be >= 0");
+  if (n == 0) return GLAD_OK;
+  if (!items) return fail(GLAD_ERR_INVALID_ARG, "items is NULL");
+  for (int i = 0; i < n; ++i) {
+    const GladCastCopy& c = items[i];
+    if ((!c.src || !c.dst) && c.n > 0) return fail(GLAD_ERR_INVALID_ARG, "item %d: NULL pointer", i);
+    if ((c.src_dtype != GLAD_DTYPE_F16 && c.src_dtype != GLAD_DTYPE_F32) ||
+        (c.dst_dtype != GLAD_DTYPE_F16 && c.dst_dtype != GLAD_DTYPE_F32))
+      return fail(GLAD_ERR_INVALID_ARG, "item %d: unknown dtype", i);
+  }
+  GLAD_CHECK_CUDA(launch_cast_copy(items, n, (cudaStream_t)stream), "cast-copy launch");
+  return GLAD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,226 @@
+// Shared definitions of the GLAD kernels: shapes, parameter blocks and the
+// element-wise arithmetic that must agree with the reference's qrt semantics.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+#include "../../include/glad_b200.h"
+#include "tc05.cuh"
+
+namespace glad {
+
+// GLAD shapes (qrt/qconv.py:32-38, rsl_rl actor_critic_encoder.py:33-38).
+constexpr int kH1 = 21, kW1 = 33, kC1 = 3;      // height map, NHWC
+constexpr int kH2 = 11, kW2 = 17, kC2 = 16;     // conv1 output
+constexpr int kTok = kH2 * kW2;                 // 187 tokens
+constexpr int kD = 64;                          // embedding / conv2 channels
+constexpr int kMap = kH1 * kW1 * kC1;           // 2079
+constexpr int kTopK = 32;
+constexpr int kHeads = 16;
+constexpr int kEnc = 224;                       // cat(foothold, gc, proprio[96])
+constexpr int kActions = 29;
+
+// ---- fused-forward workspace slots --------------------------------------------
+// slots[0..5] : running absmax of each quantised layer's input z (dynamic s_z)
+//   0 actor_proprio_embedding, 1 query_projector, 2 actor.0, 3 actor.2,
+//   4 actor.4, 5 actor.6
+// slots[8]    : device status word (DeviceError bits)
+constexpr int kSlotStatus = 8;
+constexpr int kSlotsBytes = 256;
+
+__device__ __forceinline__ float fp16r(float x) { return __half2float(__float2half_rn(x)); }
+
+// Activation quantisation of QuantLinear (qrt/qlinear.py:123-133).
+//  with LET: z = x*alpha + beta in fp32 (two roundings), q = rint(z/s) (dynamic)
+//            or rint(z*inv_sz) (static);
+//  without : z stays fp16 and the scaled value is rounded to fp16 before rint.
+struct ActQuant {
+  bool let;
+  bool dyn;
+  float s;      // dynamic scale (fp32 with LET; fp16-valued without)
+  float inv;    // static inv_sz (fp32 with LET; fp16-valued without)
+  __device__ __forceinline__ int quant(float x, float alpha, float beta) const {
+    float v;
+    if (let) {
+      float z = __fadd_rn(__fmul_rn(x, alpha), beta);
+      v = dyn ? __fdiv_rn(z, s) : __fmul_rn(z, inv);
+    } else {
+      v = fp16r(dyn ? __fdiv_rn(x, s) : __fmul_rn(x, inv));
+    }
+    int q = __float2int_rn(v);
+    return q < -128 ? -128 : (q > 127 ? 127 : q);
+  }
+  // |z| of one input element (what the dynamic absmax reduces).
+  __device__ __forceinline__ float absz(float x, float alpha, float beta) const {
+    return let ? fabsf(__fadd_rn(__fmul_rn(x, alpha), beta)) : fabsf(x);
+  }
+};
+
+// Scale of a dynamic layer from its reduced absmax:
+//   s_z = absmax.clamp_min(1e-8) * (1/127)      (qrt/qlinear.py:128)
+__device__ __forceinline__ float dyn_scale(float amax, bool let) {
+  if (let) return __fmul_rn(fmaxf(amax, 1e-8f), (float)(1.0 / 127.0));
+  // fp16 tensor: 1e-8 rounds to 0 in fp16; product rounded to fp16.
+  return fp16r(__fmul_rn(fmaxf(amax, 0.0f), (float)(1.0 / 127.0)));
+}
+
+__device__ __forceinline__ ActQuant make_act_quant(const GladQLinear& L, int act_mode,
+                                                   const float* slots, int slot) {
+  ActQuant a;
+  a.let = L.alpha != nullptr;
+  a.dyn = act_mode == GLAD_ACT_DYNAMIC;
+  a.s = a.dyn ? dyn_scale(slots[slot], a.let) : 1.0f;
+  a.inv = a.let ? *L.inv_sz : fp16r(*L.inv_sz);
+  return a;
+}
+
+// Output scale of row n: s_w*s_z (dynamic) or dq_scale (static) (qlinear.py:130,135).
+__device__ __forceinline__ float out_scale(const GladQLinear& L, const ActQuant& a, int n) {
+  return a.dyn ? __fmul_rn(L.s_w[n], a.s) : L.dq_scale[n];
+}
+
+// int32 accumulator -> fp16 output: y = acc*scale + b' in fp32, then fp16.
+__device__ __forceinline__ __half qlinear_out(int32_t acc, float scale, float bprime) {
+  return __float2half_rn(__fadd_rn(__fmul_rn((float)acc, scale), bprime));
+}
+
+// ELU on an fp16 value (computed in fp32, rounded to fp16).
+__device__ __forceinline__ __half elu16(__half h) {
+  float x = __half2float(h);
+  return __float2half_rn(x > 0.0f ? x : expm1f(x));
+}
+
+// conv2 epilogue (qrt/qconv.py:159-161): ((acc*dq + b) relu) * a2 + c2 -> fp16.
+__device__ __forceinline__ __half conv2_out(int32_t acc, float dq, float b, float a2, float c2) {
+  float y = __fadd_rn(__fmul_rn(i2f_small(acc), dq), b);
+  y = fmaxf(y, 0.0f);
+  return __float2half_rn(__fadd_rn(__fmul_rn(y, a2), c2));
+}
+
+// conv1 epilogue (qrt/qconv.py:96-101): relu(acc+b)*qa + qc, round half away
+// from zero, clamp to int8.
+__device__ __forceinline__ int conv1_quant(float acc, float b, float qa, float qc) {
+  float z = fmaxf(__fadd_rn(acc, b), 0.0f);
+  z = __fadd_rn(__fmul_rn(z, qa), qc);
+  float q = z >= 0.0f ? floorf(__fadd_rn(z, 0.5f)) : ceilf(__fsub_rn(z, 0.5f));
+  q = fminf(fmaxf(q, -128.0f), 127.0f);
+  return (int)q;
+}
+
+// ---- 64-wide cross-lane reduction -----------------------------------------------
+// On return lane L holds the warp sums of channels c0 and c0+1 with
+// c0 = 32*b4 + 16*b3 + 8*b2 + 4*b1 + 2*b0 (b_i = bit i of L) in v[0], v[1].
+__device__ __forceinline__ void warp_reduce64(float (&v)[64], int lane) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const bool up = lane & 16;
+    float send = up ? v[i] : v[i + 32];
+    float keep = up ? v[i + 32] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const bool up = lane & 8;
+    float send = up ? v[i] : v[i + 16];
+    float keep = up ? v[i + 16] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 4;
+    float send = up ? v[i] : v[i + 8];
+    float keep = up ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 2;
+    float send = up ? v[i] : v[i + 4];
+    float keep = up ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 1;
+    float send = up ? v[i] : v[i + 2];
+    float keep = up ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+  }
+}
+__device__ __forceinline__ int reduce64_channel(int lane) {
+  return ((lane >> 4) & 1) * 32 + ((lane >> 3) & 1) * 16 + ((lane >> 2) & 1) * 8 +
+         ((lane >> 1) & 1) * 4 + (lane & 1) * 2;
+}
+
+// ---- kernel parameter blocks -------------------------------------------------------
+enum FrontMode : int { kModeConv1 = 0, kModeConv2 = 1, kModeChain = 2, kModeFront = 3 };
+
+struct FrontParams {
+  const void* in;          // obs / x_nhwc rows (kModeConv2: z8)
+  int64_t ld;              // row stride in elements
+  int in_dtype;            // GLAD_DTYPE_*
+  int prop_dim;            // columns before the map (0 for the conv operators)
+  int64_t B;
+  GladConvWeights conv;
+  // kModeFront only
+  const __half* gps_w;
+  const __half* gps_b;
+  const __half* scorer_w;
+  GladQLinear pe;
+  GladQLinear qp;          // only alpha/beta are read (absmax of its input)
+  int act_mode;
+  // outputs
+  int8_t* z8_out;          // [B*187,16]
+  __half* feat_out;        // [B*187,64]
+  int32_t* acc_out;        // [B*187,64]
+  __half* score_local;     // [B,187]
+  __half* gc_w_out;        // [B,187]
+  __half* enc;             // [B,224]: writes columns 64..223 (gc, proprio)
+  __half* pe_out;          // [B,64]
+  float* slots;
+};
+
+struct TailParams {
+  int64_t B;
+  GladConvWeights conv;
+  GladQLinear qp;          // query_projector
+  const __half* scorer_w;  // [128]
+  const __half* scorer_b;  // [1]
+  const __half* in_w;      // [192,64]
+  const __half* in_b;      // [192]
+  const __half* out_w;     // [64,64]
+  const __half* out_b;     // [64]
+  const float* a0_alpha;   // actor.0 LET (absmax of its input), may be null
+  const float* a0_beta;
+  int act_mode;
+  const float* noise;      // [B,187] or null
+  const int8_t* z8;        // [B*187,16]
+  const __half* score_local;
+  const __half* pe;        // [B,64]
+  __half* enc;             // [B,224]: reads 64..223, writes 0..63
+  __half* topk_logits_out; // [B,187] or null
+  int64_t* topk_idx_out;   // [B,32] or null
+  __half* attn_w_out;      // [B,32] or null
+  float* slots;
+};
+
+struct GemmParams {
+  GladQLinear L;
+  int act_mode;
+  int slot;                // slot of this layer's absmax (dynamic)
+  const void* x;           // [M,K]
+  int x_dtype;
+  int64_t M, ldx;
+  __half* y;               // [M,ldy] f16 output (or null)
+  int64_t ldy;
+  float* y32;              // [M,ldy32] f32 output (or null)
+  int64_t ldy32;
+  int elu;                 // apply ELU to the fp16 output
+  const float* next_alpha; // LET of the consumer layer (absmax of its input)
+  const float* next_beta;
+  int next_let;
+  int next_slot;           // -1: no absmax for a consumer
+  float* slots;
+};
+
+}  // namespace glad

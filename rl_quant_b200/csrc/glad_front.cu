@@ -1,0 +1,504 @@
+// Encoder front: conv1 (fp16 tcgen05) -> conv2 (int8 tcgen05) and, in the
+// fused mode, the global softmax pool, the scorer's local logits and the
+// proprio embedding, one environment at a time per CTA.
+//
+// Reference: qrt/qconv.py:54-163 (the two Triton kernels), qrt/encoder_opt.py:
+// 41-77 (GPS + scorer-local merged GEMM, softmax pool), qrt/qlinear.py:111-138
+// (actor_proprio_embedding).
+//
+// Shared-memory operand layouts (no swizzle, K-major core matrices of
+// 8 rows x 16 bytes). Neither GEMM materialises an im2col matrix: the A
+// operand descriptors point into layouts in which consecutive GEMM rows are
+// 16 bytes apart, so one descriptor per K chunk walks the whole tile.
+//
+// conv1 planes (fp16): input rows split by parity, each pixel padded to four
+//   halves (x,y,z,0). Plane p, row r holds input row ih = 2r-2+p; pixel slot
+//   s holds column iw = s-2; a row is 38 slots = 304 bytes. GEMM row
+//   m = oh*19 + ow (ow < 17 valid). The 16-byte chunk (kh, j) of row m (pixels
+//   kw = 2j, 2j+1) sits at plane(kh&1) + (kh>>1)*304 + j*16 + m*16.
+// conv2 strip (int8): z8 at padded position (oh+1)*18 + (ow+1), 16 channels =
+//   16 bytes per position; row 0 / column 0 are zero halo and column 18 wraps
+//   onto the next row's halo. GEMM row m = oh*18 + ow; tap (kh,kw) of row m
+//   sits at (m + kh*18 + kw)*16.
+// Each environment owns two M=128 tiles per GEMM (conv1: 209 rows, conv2:
+// 198 rows); rows outside the 11x17 grid are computed and discarded.
+#include <cuda_runtime.h>
+
+#include "glad_common.cuh"
+
+namespace glad {
+
+constexpr int kRowBytes = 304;                  // 38 slots x 8 bytes
+constexpr int kPlaneRows = 16;
+constexpr int kPlaneBytes = kPlaneRows * kRowBytes;   // 4864
+constexpr int kPlanesBytes = 2 * kPlaneBytes;          // 9728
+constexpr int kW1sBytes = 8 * 512;                     // 8 MMA K-steps x (2 chunks x 16 n x 16 B)
+constexpr int kStripCols = 18;
+constexpr int kStripBytes = 4736;                      // >= (255 + 2*18 + 2 + 1 + 1) * 16
+constexpr int kW2sBytes = 5 * 2048;                    // 5 K-steps x (2 chunks x 64 n x 16 B)
+constexpr int kStageBytes = 8864;                      // (128 + 2079) * 4 rounded up + 16
+constexpr int kTmemCols = 128;
+
+struct __align__(128) FrontSmem {
+  uint8_t planes[kPlanesBytes];
+  uint8_t w1s[kW1sBytes];
+  uint8_t strip[kStripBytes];
+  uint8_t w2s[kW2sBytes];
+  uint8_t stage[2][kStageBytes];
+  float b1[16], qa[16], qc[16];
+  float dq[64], b2[64], a2[64], c2[64];
+  float wg[64], ws[64];                 // GPS weight, scorer weight (local half)
+  float red[8][64];                     // pooling partial sums
+  float wmax[4], wsum[4];
+  __half prop16[128];                   // proprio (fp16)
+  __half pe16[64];
+  __half gc16[64];
+  alignas(16) int8_t q8[128];           // quantised proprio
+  uint64_t mbar;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// K-chunk q (0..15) of the conv1 GEMM: byte offset inside the planes for GEMM row 0.
+__device__ __forceinline__ uint32_t conv1_chunk_off(int q) {
+  if (q >= 15) return conv1_chunk_off(14) + 16;        // zero-weight filler chunk
+  const int kh = q / 3, j = q % 3;
+  return (kh & 1) * kPlaneBytes + (kh >> 1) * kRowBytes + j * 16;
+}
+// Tap q (0..9) of the conv2 GEMM: position offset of GEMM row 0 in the strip.
+__device__ __forceinline__ int conv2_tap_off(int q) {
+  if (q >= 9) return 2 * kStripCols + 2 + 1;           // zero-weight filler tap
+  return (q / 3) * kStripCols + (q % 3);
+}
+
+// One observation row lives partly in shared memory: the 16-byte aligned
+// body arrives by cp.async, the ragged head/tail bytes are read from global.
+struct RowStage {
+  const uint8_t* src;    // first byte of the row in global memory
+  uint32_t body_lo;      // first staged byte (relative to src)
+  uint32_t body_hi;      // one past the last staged byte
+  const uint8_t* stage;  // shared copy of [body_lo, body_hi)
+};
+
+__device__ __forceinline__ RowStage row_stage(const void* base, int64_t row, int64_t ld,
+                                              int esz, int nelem, uint8_t* stage) {
+  RowStage r;
+  r.src = reinterpret_cast<const uint8_t*>(base) + row * ld * esz;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(r.src);
+  const uintptr_t lo = (a + 15) & ~uintptr_t(15);
+  const uintptr_t hi = (a + (uintptr_t)nelem * esz) & ~uintptr_t(15);
+  r.body_lo = (uint32_t)(lo - a);
+  r.body_hi = hi > lo ? (uint32_t)(hi - a) : r.body_lo;
+  r.stage = stage;
+  return r;
+}
+
+__device__ __forceinline__ void row_issue(const RowStage& r, int tid, int nthr) {
+  const uint32_t n16 = (r.body_hi - r.body_lo) >> 4;
+  for (uint32_t i = tid; i < n16; i += nthr)
+    cp_async16((void*)(r.stage + i * 16), r.src + r.body_lo + i * 16);
+}
+
+template <int ESZ>
+__device__ __forceinline__ float row_elem(const RowStage& r, int i) {
+  const uint32_t b = (uint32_t)i * ESZ;
+  const uint8_t* p = (b >= r.body_lo && b < r.body_hi) ? r.stage + (b - r.body_lo) : r.src + b;
+  if (ESZ == 4) return *reinterpret_cast<const float*>(p);
+  return __half2float(*reinterpret_cast<const __half*>(p));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ FrontParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  FrontSmem& s = *reinterpret_cast<FrontSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr bool kConv1 = MODE != kModeConv2;
+  constexpr bool kConv2 = MODE != kModeConv1;
+  constexpr bool kFront = MODE == kModeFront;
+
+  // ---- one-time set-up ------------------------------------------------------
+  if (warp == 0) tmem_alloc(&s.tmem_base, kTmemCols);
+  if (tid == 0) {
+    mbar_init(&s.mbar, 1);
+    fence_mbar_init();
+    s.abort_flag = 0;
+  }
+  {
+    uint4 z = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < kPlanesBytes / 16; i += 128) reinterpret_cast<uint4*>(s.planes)[i] = z;
+    for (int i = tid; i < kStripBytes / 16; i += 128) reinterpret_cast<uint4*>(s.strip)[i] = z;
+  }
+  if (kConv1) {
+    const __half* w1p = reinterpret_cast<const __half*>(p.conv.w1p);
+    __half* dst = reinterpret_cast<__half*>(s.w1s);
+    for (int idx = tid; idx < kW1sBytes / 2; idx += 128) {
+      const int pr = idx >> 8, c = (idx >> 7) & 1, n = (idx >> 3) & 15, e = idx & 7;
+      const int q = 2 * pr + c;
+      __half v = __float2half(0.0f);
+      if (q < 15) {
+        const int kh = q / 3, kw = 2 * (q % 3) + (e >> 2), ch = e & 3;
+        if (kw < 5 && ch < 3) v = w1p[(kh * 16 + kw * 3 + ch) * 16 + n];
+      }
+      dst[idx] = v;
+    }
+    if (tid < 16) {
+      s.b1[tid] = p.conv.b1f[tid];
+      s.qa[tid] = p.conv.qa[tid];
+      s.qc[tid] = p.conv.qc[tid];
+    }
+  }
+  if (kConv2) {
+    for (int idx = tid; idx < kW2sBytes; idx += 128) {
+      const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
+      const int q = 2 * pr + c;
+      int8_t v = 0;
+      if (q < 9) v = p.conv.w8[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n];
+      s.w2s[idx] = (uint8_t)v;
+    }
+    if (tid < 64) {
+      s.dq[tid] = p.conv.dq[tid];
+      s.b2[tid] = p.conv.b2f[tid];
+      s.a2[tid] = p.conv.a2[tid];
+      s.c2[tid] = p.conv.c2[tid];
+      if (kFront) {
+        s.wg[tid] = __half2float(p.gps_w[tid]);
+        s.ws[tid] = __half2float(p.scorer_w[tid]);
+      }
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  uint32_t phase = 0;
+
+  // Front-mode constants.
+  ActQuant aq_pe{};
+  ActQuant aq_qp{};
+  float gb = 0.0f;
+  float zmax_qp = 0.0f;
+  if (kFront) {
+    aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
+    aq_qp.let = p.qp.alpha != nullptr;
+    gb = __half2float(p.gps_b[0]);
+  }
+
+  const int esz = (MODE == kModeConv2) ? 1 : (p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2);
+  const int row_elems = (MODE == kModeConv2) ? kTok * kC2 : p.prop_dim + kMap;
+  int buf = 0;
+  int64_t env = blockIdx.x;
+  if (env < p.B) {
+    RowStage r0 = row_stage(p.in, env, p.ld, esz, row_elems, s.stage[0]);
+    row_issue(r0, tid, 128);
+  }
+  cp_async_commit();
+
+  for (; env < p.B; env += gridDim.x) {
+    cp_async_wait_all();
+    __syncthreads();
+    const RowStage rs = row_stage(p.in, env, p.ld, esz, row_elems, s.stage[buf]);
+    const int64_t nxt = env + gridDim.x;
+    if (nxt < p.B) {
+      RowStage rn = row_stage(p.in, nxt, p.ld, esz, row_elems, s.stage[buf ^ 1]);
+      row_issue(rn, tid, 128);
+    }
+    cp_async_commit();
+
+    if (kConv1) {
+      // ---- input -> conv1 planes (fp16) -------------------------------------------
+      const int moff = p.prop_dim;
+      for (int px = tid; px < kH1 * kW1; px += 128) {
+        const int ih = px / kW1, iw = px - ih * kW1;
+        float v0, v1, v2;
+        if (esz == 4) {
+          v0 = row_elem<4>(rs, moff + px * 3);
+          v1 = row_elem<4>(rs, moff + px * 3 + 1);
+          v2 = row_elem<4>(rs, moff + px * 3 + 2);
+        } else {
+          v0 = row_elem<2>(rs, moff + px * 3);
+          v1 = row_elem<2>(rs, moff + px * 3 + 1);
+          v2 = row_elem<2>(rs, moff + px * 3 + 2);
+        }
+        const int pl = ih & 1, r = ((ih - pl) >> 1) + 1, slot = iw + 2;
+        __half2 h01 = __floats2half2_rn(v0, v1);
+        __half2 h2z = __floats2half2_rn(v2, 0.0f);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&h01);
+        pk.y = *reinterpret_cast<uint32_t*>(&h2z);
+        *reinterpret_cast<uint2*>(s.planes + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
+      }
+      if (kFront) {
+        for (int k = tid; k < p.prop_dim; k += 128)
+          s.prop16[k] = __float2half_rn(esz == 4 ? row_elem<4>(rs, k) : row_elem<2>(rs, k));
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t pb = smem_u32(s.planes), wb = smem_u32(s.w1s);
+        constexpr uint32_t idesc = idesc_f16(128, 16);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+#pragma unroll
+          for (int pr = 0; pr < 8; ++pr) {
+            const uint32_t c0 = conv1_chunk_off(2 * pr), c1 = conv1_chunk_off(2 * pr + 1);
+            const uint64_t ad = smem_desc(pb + c0 + t * 128 * 16, c1 - c0, 128);
+            const uint64_t bd = smem_desc(wb + pr * 512, 256, 128);
+            mma_f16(tmem + t * 16, ad, bd, idesc, pr > 0 ? 1u : 0u);
+          }
+        }
+        mma_commit(&s.mbar);
+      }
+
+      if (kFront) {
+        // proprio embedding while the tensor core runs (qrt/qlinear.py:123-138)
+        const int P = p.prop_dim;
+        for (int k = tid; k < P; k += 128) {
+          const float a = aq_pe.let ? p.pe.alpha[k] : 0.0f;
+          const float b = aq_pe.let ? p.pe.beta[k] : 0.0f;
+          s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[k]), a, b);
+        }
+        __syncthreads();
+        if (tid < kD) {
+          const int n = tid;
+          const int* wrow = reinterpret_cast<const int*>(p.pe.w8 + (int64_t)n * P);
+          const int* qw = reinterpret_cast<const int*>(s.q8);
+          int acc = 0;
+          for (int k4 = 0; k4 < P / 4; ++k4) acc = __dp4a(qw[k4], __ldg(wrow + k4), acc);
+          s.pe16[n] = qlinear_out(acc, out_scale(p.pe, aq_pe, n), p.pe.b_prime[n]);
+        }
+      }
+
+      const bool ok = mbar_wait_bounded(&s.mbar, phase);
+      phase ^= 1;
+      if (!ok) s.abort_flag = 1;
+      tc_fence_after();
+      __syncthreads();
+      if (s.abort_flag) break;
+
+      // ---- conv1 epilogue: TMEM -> int8 z8 -> strip / global --------------------------
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + t * 16, r);
+        tmem_ld_wait();
+        const int m = t * 128 + 32 * warp + lane;
+        const int oh = m / 19, ow = m - oh * 19;
+        if (oh < kH2 && ow < kW2) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const int c = w4 * 4 + b;
+              const int q = conv1_quant(__uint_as_float(r[c]), s.b1[c], s.qa[c], s.qc[c]);
+              word |= ((uint32_t)(q & 0xFF)) << (8 * b);
+            }
+            pk[w4] = word;
+          }
+          const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          if (kConv2)
+            *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
+          if (p.z8_out)
+            reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;
+        }
+      }
+      tc_fence_before();
+    }
+
+    if (kConv2) {
+      if (MODE == kModeConv2) {
+        // z8 rows of this environment -> strip
+        for (int t = tid; t < kTok; t += 128) {
+          const int oh = t / kW2, ow = t - oh * kW2;
+          const uint32_t b = (uint32_t)t * 16;
+          const uint8_t* src = (b >= rs.body_lo && b + 16 <= rs.body_hi) ? rs.stage + (b - rs.body_lo)
+                                                                          : rs.src + b;
+          *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) =
+              *reinterpret_cast<const uint4*>(src);
+        }
+      }
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t sb = smem_u32(s.strip), wb = smem_u32(s.w2s);
+        constexpr uint32_t idesc = idesc_i8(128, 64);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+#pragma unroll
+          for (int pr = 0; pr < 5; ++pr) {
+            const int o0 = conv2_tap_off(2 * pr), o1 = conv2_tap_off(2 * pr + 1);
+            const uint64_t ad = smem_desc(sb + (t * 128 + o0) * 16, (o1 - o0) * 16, 128);
+            const uint64_t bd = smem_desc(wb + pr * 2048, 1024, 128);
+            mma_i8(tmem + t * 64, ad, bd, idesc, pr > 0 ? 1u : 0u);
+          }
+        }
+        mma_commit(&s.mbar);
+      }
+      const bool ok = mbar_wait_bounded(&s.mbar, phase);
+      phase ^= 1;
+      if (!ok) s.abort_flag = 1;
+      tc_fence_after();
+      __syncthreads();
+      if (s.abort_flag) break;
+
+      // ---- conv2 epilogue, pass 1 -------------------------------------------------------
+      float my_logit[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int m = t * 128 + 32 * warp + lane;
+        const int oh = m / kStripCols, ow = m - oh * kStripCols;
+        const bool valid = oh < kH2 && ow < kW2;
+        const int tok = oh * kW2 + ow;
+        float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
+          tmem_ld_wait();
+          __half h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int c = cb * 16 + j;
+            h[j] = conv2_out((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]);
+          }
+          if (kFront) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float f = __half2float(h[j]);
+              l0 = fmaf(f, s.wg[cb * 16 + j], l0);
+              l1 = fmaf(f, s.ws[cb * 16 + j], l1);
+            }
+          }
+          if (valid && p.feat_out) {
+            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + tok) * kD + cb * 16);
+            dst[0] = *reinterpret_cast<uint4*>(&h[0]);
+            dst[1] = *reinterpret_cast<uint4*>(&h[8]);
+          }
+          if (valid && p.acc_out) {
+            int4* dst = reinterpret_cast<int4*>(p.acc_out + (env * kTok + tok) * kD + cb * 16);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2], (int)r[4 * j + 3]);
+          }
+        }
+        if (kFront) {
+          // logits2 = local @ [w_gps; w_s[:, :D]]^T, rounded to fp16 (qrt/encoder_opt.py:69-73)
+          const float g = fp16r(__fadd_rn(fp16r(l0), gb));
+          my_logit[t] = valid ? g : -INFINITY;
+          if (valid) p.score_local[env * kTok + tok] = __float2half_rn(l1);
+        }
+      }
+
+      if (kFront) {
+        // ---- softmax over the 187 tokens (qrt/encoder_opt.py:75) ------------------------
+        float mx = warp_max(fmaxf(my_logit[0], my_logit[1]));
+        if (lane == 0) s.wmax[warp] = mx;
+        __syncthreads();
+        mx = fmaxf(fmaxf(s.wmax[0], s.wmax[1]), fmaxf(s.wmax[2], s.wmax[3]));
+        float e[2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) e[t] = my_logit[t] == -INFINITY ? 0.0f : expf(my_logit[t] - mx);
+        float sm = warp_sum(e[0] + e[1]);
+        if (lane == 0) s.wsum[warp] = sm;
+        __syncthreads();
+        sm = (s.wsum[0] + s.wsum[1]) + (s.wsum[2] + s.wsum[3]);
+
+        // ---- pass 2: gc = sum_i w_i * local_i (qrt/encoder_opt.py:76-77) ---------------
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int m = t * 128 + 32 * warp + lane;
+          const int oh = m / kStripCols, ow = m - oh * kStripCols;
+          const bool valid = oh < kH2 && ow < kW2;
+          const __half wh = __float2half_rn(__fdiv_rn(e[t], sm));
+          if (valid && p.gc_w_out) p.gc_w_out[env * kTok + oh * kW2 + ow] = wh;
+          const float wt = valid ? __half2float(wh) : 0.0f;
+          float v[64];
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb) {
+            uint32_t r[16];
+            tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int c = cb * 16 + j;
+              v[c] = wt * __half2float(conv2_out((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]));
+            }
+          }
+          warp_reduce64(v, lane);
+          const int c0 = reduce64_channel(lane);
+          s.red[t * 4 + warp][c0] = v[0];
+          s.red[t * 4 + warp][c0 + 1] = v[1];
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (tid < kD) {
+          float g = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) g += s.red[j][tid];
+          const __half gh = __float2half_rn(g);
+          s.gc16[tid] = gh;
+          p.enc[env * kEnc + 64 + tid] = gh;
+          p.pe_out[env * kD + tid] = s.pe16[tid];
+        }
+        for (int k = tid; k < p.prop_dim; k += 128) p.enc[env * kEnc + 128 + k] = s.prop16[k];
+        __syncthreads();
+        if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
+          // |alpha*cat(gc, pe) + beta| for the query projector's dynamic s_z
+          const float x = __half2float(tid < kD ? s.gc16[tid] : s.pe16[tid - kD]);
+          const float a = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
+          const float b = aq_qp.let ? p.qp.beta[tid] : 0.0f;
+          zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, a, b));
+        }
+      } else {
+        tc_fence_before();
+      }
+    }
+    buf ^= 1;
+  }
+
+  // ---- teardown --------------------------------------------------------------------------
+  cp_async_wait_all();
+  if (s.abort_flag) {
+    // give an MMA still in flight one more bounded wait before TMEM is released
+    mbar_wait_bounded(&s.mbar, phase);
+  }
+  if (kFront && p.act_mode == GLAD_ACT_DYNAMIC) {
+    const float m = warp_max(zmax_qp);
+    if (lane == 0 && m > 0.0f) atomic_max_nonneg(&p.slots[1], m);
+  }
+  if (s.abort_flag && tid == 0 && p.slots)
+    atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrMmaTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+size_t front_smem_bytes() { return sizeof(FrontSmem) + 128; }
+
+template <int MODE>
+cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st) {
+  const size_t smem = front_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(front_kernel<MODE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  front_kernel<MODE><<<grid, 128, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_front<kModeConv1>(const FrontParams&, int, cudaStream_t);
+template cudaError_t launch_front<kModeConv2>(const FrontParams&, int, cudaStream_t);
+template cudaError_t launch_front<kModeChain>(const FrontParams&, int, cudaStream_t);
+template cudaError_t launch_front<kModeFront>(const FrontParams&, int, cudaStream_t);
+
+}  // namespace glad

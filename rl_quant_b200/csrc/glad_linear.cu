@@ -1,0 +1,414 @@
+// W8A8 QuantLinear as a tcgen05 int8 GEMM, plus the small kernels of the
+// forward (dynamic absmax) and of the weight refresh (requantisation,
+// batched cast-copies).
+//
+// Reference: qrt/qlinear.py:84-138 (QuantLinear), qrt/qconv.py:247-284
+// (QuantCNN.requantize_), qrt/runtime.py:224-271 (sync_weights_from).
+#include <cuda_runtime.h>
+
+#include "glad_common.cuh"
+
+namespace glad {
+
+// ---- tcgen05 int8 GEMM --------------------------------------------------------------
+// CTA = 128 rows x NT columns; A (activations) is quantised on the way into
+// shared memory, B is the layer's int8 weight rows. Both K-major, no swizzle:
+//   A: [K/16 chunks][128 rows][16 B]   (LBO = 2048, SBO = 128)
+//   B: [K/16 chunks][NT rows][16 B]    (LBO = NT*16, SBO = 128)
+template <int NT>
+__global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int K = p.L.in_features;
+  const int Kp = (K + 31) & ~31;         // K padded to the MMA K-step (zero fill)
+  uint8_t* As = base;
+  uint8_t* Bs = As + (size_t)Kp * 128;
+  float* cscale = reinterpret_cast<float*>(Bs + (size_t)Kp * NT);
+  float* cbias = cscale + NT;
+  float* calpha = cbias + NT;
+  float* cbeta = calpha + NT;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(cbeta + NT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t m0 = (int64_t)blockIdx.x * 128;
+  const int n0 = blockIdx.y * NT;
+  const int N = p.L.out_features;
+  const int Np = (N + 7) & ~7;
+  constexpr uint32_t kCols = NT < 32 ? 32 : NT;
+
+  if (warp == 0) tmem_alloc(tmem_slot, kCols);
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    fence_mbar_init();
+    *abort_flag = 0;
+  }
+  const ActQuant aq = make_act_quant(p.L, p.act_mode, p.slots, p.slot);
+  // weights: rows n0..n0+NT of w8 (zero past Np)
+  const int kc16 = Kp / 16;
+  const bool rows16 = (K & 15) == 0;
+  for (int idx = tid; idx < NT * kc16; idx += 128) {
+    const int c = idx / NT, n = idx - c * NT;
+    uint8_t* dst = Bs + c * (NT * 16) + n * 16;
+    const int8_t* src = p.L.w8 + (int64_t)(n0 + n) * K + c * 16;
+    if (n0 + n < Np && c * 16 + 16 <= K && rows16) {
+      cp_async16(dst, src);
+    } else {
+      uint2 lo = make_uint2(0, 0), hi = make_uint2(0, 0);
+      if (n0 + n < Np && c * 16 + 8 <= K) lo = *reinterpret_cast<const uint2*>(src);
+      if (n0 + n < Np && c * 16 + 16 <= K) hi = *reinterpret_cast<const uint2*>(src + 8);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+    }
+  }
+  cp_async_commit();
+  for (int j = tid; j < NT; j += 128) {
+    const int n = n0 + j;
+    const bool in = n < N;
+    cscale[j] = in ? out_scale(p.L, aq, n) : 0.0f;
+    cbias[j] = in ? p.L.b_prime[n] : 0.0f;
+    calpha[j] = (in && p.next_let) ? p.next_alpha[n] : 0.0f;
+    cbeta[j] = (in && p.next_let) ? p.next_beta[n] : 0.0f;
+  }
+  // activations: quantise 8 elements at a time
+  const int k8n = Kp / 8, k8real = K / 8;
+  const bool f32in = p.x_dtype == GLAD_DTYPE_F32;
+  for (int idx = tid; idx < 128 * k8n; idx += 128) {
+    const int r = idx / k8n, k8 = idx - r * k8n;
+    const int64_t m = m0 + r;
+    uint2 out = make_uint2(0, 0);
+    if (m < p.M && k8 < k8real) {
+      float x[8];
+      if (f32in) {
+        const float* src = reinterpret_cast<const float*>(p.x) + m * p.ldx + k8 * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = src[e];
+      } else {
+        const __half* src = reinterpret_cast<const __half*>(p.x) + m * p.ldx + k8 * 8;
+        if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src);
+          const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = __half2float(h[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = __half2float(src[e]);
+        }
+      }
+      uint32_t w[2] = {0, 0};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int k = k8 * 8 + e;
+        const float a = aq.let ? __ldg(p.L.alpha + k) : 0.0f;
+        const float b = aq.let ? __ldg(p.L.beta + k) : 0.0f;
+        w[e >> 2] |= (uint32_t)(aq.quant(x[e], a, b) & 0xFF) << (8 * (e & 3));
+      }
+      out = make_uint2(w[0], w[1]);
+    }
+    *reinterpret_cast<uint2*>(As + (k8 >> 1) * 2048 + r * 16 + (k8 & 1) * 8) = out;
+  }
+  cp_async_wait_all();
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    const uint32_t ab = smem_u32(As), bb = smem_u32(Bs);
+    constexpr uint32_t idesc = idesc_i8(128, NT);
+    for (int kc = 0; kc < Kp / 32; ++kc) {
+      const uint64_t ad = smem_desc(ab + kc * 2 * 2048, 2048, 128);
+      const uint64_t bd = smem_desc(bb + kc * 2 * NT * 16, NT * 16, 128);
+      mma_i8(tmem, ad, bd, idesc, kc > 0 ? 1u : 0u);
+    }
+    mma_commit(mbar);
+  }
+  const bool ok = mbar_wait_bounded(mbar, 0);
+  if (!ok) *abort_flag = 1;
+  tc_fence_after();
+  __syncthreads();
+
+  float zmax = 0.0f;
+  if (!*abort_flag) {
+    const int64_t m = m0 + 32 * warp + lane;
+    const bool row_ok = m < p.M;
+    ActQuant nq{};
+    nq.let = p.next_let != 0;
+#pragma unroll 1
+    for (int cb = 0; cb < NT / 16; ++cb) {
+      uint32_t rr[16];
+      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + cb * 16, rr);
+      tmem_ld_wait();
+      __half h[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int jj = cb * 16 + j;
+        h[j] = qlinear_out((int32_t)rr[j], cscale[jj], cbias[jj]);
+        if (p.elu) h[j] = elu16(h[j]);
+      }
+      if (row_ok) {
+        const int nb = n0 + cb * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = nb + j;
+          if (n < N) {
+            if (p.y) p.y[m * p.ldy + n] = h[j];
+            if (p.y32) p.y32[m * p.ldy32 + n] = __half2float(h[j]);
+            if (p.next_slot >= 0)
+              zmax = fmaxf(zmax, nq.absz(__half2float(h[j]), calpha[cb * 16 + j], cbeta[cb * 16 + j]));
+          }
+        }
+      }
+    }
+  }
+  if (p.next_slot >= 0 && p.act_mode == GLAD_ACT_DYNAMIC) {
+    const float mm = warp_max(zmax);
+    if (lane == 0 && mm > 0.0f) atomic_max_nonneg(&p.slots[p.next_slot], mm);
+  }
+  if (*abort_flag) {
+    mbar_wait_bounded(mbar, 0);
+    if (tid == 0 && p.slots)
+      atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrMmaTimeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+size_t qgemm_smem_bytes(int K, int NT) {
+  const size_t Kp = (size_t)((K + 31) & ~31);
+  return Kp * 128 + Kp * NT + 4 * NT * sizeof(float) + 64 + 128;
+}
+
+template <int NT>
+cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st) {
+  const size_t smem = qgemm_smem_bytes(p.L.in_features, NT);
+  cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<NT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int Np = (p.L.out_features + 7) & ~7;
+  dim3 grid((unsigned)((p.M + 127) / 128), (unsigned)((Np + NT - 1) / NT));
+  qgemm_kernel<NT><<<grid, 128, smem, st>>>(p);
+  return cudaGetLastError();
+}
+template cudaError_t launch_qgemm<128>(const GemmParams&, cudaStream_t);
+template cudaError_t launch_qgemm<64>(const GemmParams&, cudaStream_t);
+template cudaError_t launch_qgemm<32>(const GemmParams&, cudaStream_t);
+
+// ---- dynamic absmax of alpha*x + beta over [M, K] ---------------------------------------
+// `round16`: the input is first rounded to fp16 (the .half() cast in front of
+// the compiled actor, qrt/integration.py:206).
+__global__ void absmax_kernel(const void* x, int dtype, int64_t M, int64_t ld, int K,
+                              const float* alpha, const float* beta, int round16,
+                              float* slot) {
+  ActQuant q{};
+  q.let = alpha != nullptr;
+  float m = 0.0f;
+  const int64_t total = M * (int64_t)K;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K;
+    const int k = (int)(i - r * K);
+    float v = dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(x)[r * ld + k]
+                                      : __half2float(reinterpret_cast<const __half*>(x)[r * ld + k]);
+    if (round16) v = fp16r(v);
+    m = fmaxf(m, q.absz(v, q.let ? alpha[k] : 0.0f, q.let ? beta[k] : 0.0f));
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0 && m > 0.0f) atomic_max_nonneg(slot, m);
+}
+
+cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
+                          const float* alpha, const float* beta, int round16, float* slot,
+                          int num_sms, cudaStream_t st) {
+  const int64_t total = M * (int64_t)K;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 4LL * num_sms) blocks = 4LL * num_sms;
+  if (blocks < 1) blocks = 1;
+  absmax_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, dtype, M, ld, K, alpha, beta, round16, slot);
+  return cudaGetLastError();
+}
+
+// Per-layer scales reported through GladActorAux::act_scales.
+struct ScaleArgs {
+  const float* s_z[6];
+  int let[6];
+};
+__global__ void act_scales_kernel2(const float* slots, int act_mode, ScaleArgs a, float* out) {
+  const int i = threadIdx.x;
+  if (i < 6) out[i] = act_mode == GLAD_ACT_DYNAMIC ? dyn_scale(slots[i], a.let[i] != 0) : *a.s_z[i];
+}
+cudaError_t launch_act_scales(const float* slots, int act_mode, const float* const s_z[6],
+                              const int let[6], float* out, cudaStream_t st) {
+  ScaleArgs a;
+  for (int i = 0; i < 6; ++i) {
+    a.s_z[i] = s_z[i];
+    a.let[i] = let[i];
+  }
+  act_scales_kernel2<<<1, 32, 0, st>>>(slots, act_mode, a, out);
+  return cudaGetLastError();
+}
+
+// ---- QuantLinear.requantize_ (qrt/qlinear.py:84-102) ---------------------------------
+// One warp per output row; blockIdx.y = layer.
+constexpr int kMaxRequantLayers = 16;
+struct RequantTable {
+  GladQLinearSrc l[kMaxRequantLayers];
+  int n;
+};
+
+__device__ __forceinline__ float load_w(const void* p, int dtype, int64_t i) {
+  return dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(p)[i]
+                                 : __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+__global__ void requant_qlinear_kernel(const __grid_constant__ RequantTable t) {
+  const GladQLinearSrc& L = t.l[blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (n >= L.N) return;
+  const int K = L.K;
+  float amax = 0.0f, bsum = 0.0f;
+  for (int k = lane; k < K; k += 32) {
+    float w = load_w(L.weight, L.w_dtype, (int64_t)n * K + k);
+    if (L.alpha) w = __fdiv_rn(w, L.alpha[k]);
+    amax = fmaxf(amax, fabsf(w));
+    if (L.alpha && L.beta) bsum += __fmul_rn(w, L.beta[k]);
+  }
+  amax = warp_max(amax);
+  bsum = warp_sum(bsum);
+  const float s_w = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+  for (int k = lane; k < K; k += 32) {
+    float w = load_w(L.weight, L.w_dtype, (int64_t)n * K + k);
+    if (L.alpha) w = __fdiv_rn(w, L.alpha[k]);
+    int q = __float2int_rn(__fdiv_rn(w, s_w));
+    q = q < -128 ? -128 : (q > 127 ? 127 : q);
+    L.w8[(int64_t)n * K + k] = (int8_t)q;
+  }
+  if (lane == 0) {
+    const float b = L.bias ? load_w(L.bias, L.w_dtype, n) : 0.0f;
+    L.dq_scale[n] = __fmul_rn(s_w, *L.s_z);
+    L.s_w[n] = s_w;
+    L.b_prime[n] = (L.alpha && L.beta) ? __fsub_rn(b, bsum) : b;
+  }
+}
+
+cudaError_t launch_requant_qlinear(const GladQLinearSrc* layers, int n, cudaStream_t st) {
+  RequantTable t;
+  t.n = n;
+  int maxN = 0;
+  for (int i = 0; i < n; ++i) {
+    t.l[i] = layers[i];
+    if (layers[i].N > maxN) maxN = layers[i].N;
+  }
+  dim3 grid((unsigned)((maxN + 7) / 8), (unsigned)n);
+  requant_qlinear_kernel<<<grid, 256, 0, st>>>(t);
+  return cudaGetLastError();
+}
+
+// ---- QuantCNN.requantize_ (qrt/qconv.py:247-284), no LET -------------------------------
+__device__ __forceinline__ float h2f(const void* p, int i) {
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+__global__ void requant_qcnn_kernel(const __grid_constant__ GladQCNNSrc s) {
+  const int tid = threadIdx.x;
+  const float sz = *s.s_z;
+  // BN affine evaluated in fp16 (the inference copy is fp16), then widened.
+  auto bn = [](const void* w, const void* b, const void* mu, const void* var, float eps, int c,
+               float& a, float& cc) {
+    const float den = fp16r(sqrtf(fp16r(__fadd_rn(h2f(var, c), fp16r(eps)))));
+    a = fp16r(__fdiv_rn(h2f(w, c), den));
+    cc = __fsub_rn(h2f(b, c), __fmul_rn(a, h2f(mu, c)));
+  };
+  if (tid < 16) {
+    float a1, c1;
+    bn(s.bn1_w, s.bn1_b, s.bn1_mean, s.bn1_var, s.eps1, tid, a1, c1);
+    s.qa[tid] = __fdiv_rn(a1, sz);
+    s.qc[tid] = __fdiv_rn(c1, sz);
+    s.b1f[tid] = h2f(s.conv1_b, tid);
+  }
+  // w1p [128,16]: k = kh*16 + kw*3 + c for kh<5, kw*3+c<15
+  for (int idx = tid; idx < 128 * 16; idx += blockDim.x) {
+    const int k = idx >> 4, n = idx & 15;
+    const int kh = k >> 4, r = k & 15;
+    __half v = __float2half(0.0f);
+    if (kh < 5 && r < 15) {
+      const int kw = r / 3, c = r % 3;
+      v = reinterpret_cast<const __half*>(s.conv1_w)[((n * 3 + c) * 5 + kh) * 5 + kw];
+    }
+    reinterpret_cast<__half*>(s.w1p)[idx] = v;
+  }
+  if (tid < 64) {
+    const int n = tid;
+    float amax = 0.0f;
+    for (int i = 0; i < 144; ++i) amax = fmaxf(amax, fabsf(h2f(s.conv2_w, n * 144 + i)));
+    const float s_w = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    // conv2_w [64][16][3][3]; w8[kh][kw*16 + c][n]
+    for (int kh = 0; kh < 3; ++kh)
+      for (int ks = 0; ks < 64; ++ks) {
+        int q = 0;
+        if (ks < 48) {
+          const int kw = ks >> 4, c = ks & 15;
+          const float w = h2f(s.conv2_w, ((n * 16 + c) * 3 + kh) * 3 + kw);
+          q = __float2int_rn(__fdiv_rn(w, s_w));
+          q = q < -128 ? -128 : (q > 127 ? 127 : q);
+        }
+        s.w8[(kh * 64 + ks) * 64 + n] = (int8_t)q;
+      }
+    s.dq[n] = __fmul_rn(s_w, sz);
+    s.b2f[n] = h2f(s.conv2_b, n);
+    float a2, c2;
+    bn(s.bn2_w, s.bn2_b, s.bn2_mean, s.bn2_var, s.eps2, n, a2, c2);
+    s.a2[n] = a2;
+    s.c2[n] = c2;
+  }
+}
+
+cudaError_t launch_requant_qcnn(const GladQCNNSrc& s, cudaStream_t st) {
+  requant_qcnn_kernel<<<1, 256, 0, st>>>(s);
+  return cudaGetLastError();
+}
+
+// ---- batched cast-copy (qrt/runtime.py:251-253) ----------------------------------------
+constexpr int kMaxCast = 96;
+struct CastTable {
+  GladCastCopy it[kMaxCast];
+};
+__global__ void cast_copy_kernel(const __grid_constant__ CastTable t) {
+  const GladCastCopy& c = t.it[blockIdx.y];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = c.src_dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(c.src)[i]
+                                                  : __half2float(reinterpret_cast<const __half*>(c.src)[i]);
+    if (c.dst_dtype == GLAD_DTYPE_F32)
+      reinterpret_cast<float*>(c.dst)[i] = v;
+    else
+      reinterpret_cast<__half*>(c.dst)[i] = __float2half_rn(v);
+  }
+}
+
+cudaError_t launch_cast_copy(const GladCastCopy* items, int n, cudaStream_t st) {
+  for (int b = 0; b < n; b += kMaxCast) {
+    CastTable t;
+    const int cnt = (n - b) < kMaxCast ? (n - b) : kMaxCast;
+    int64_t maxn = 1;
+    for (int i = 0; i < cnt; ++i) {
+      t.it[i] = items[b + i];
+      if (items[b + i].n > maxn) maxn = items[b + i].n;
+    }
+    int64_t blocks = (maxn + 255) / 256;
+    if (blocks > 256) blocks = 256;
+    cast_copy_kernel<<<dim3((unsigned)blocks, (unsigned)cnt), 256, 0, st>>>(t);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace glad

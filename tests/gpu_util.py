@@ -1,0 +1,84 @@
+"""Helpers of the GPU tests: golden/oracle weights -> CUDA tensors -> C-ABI structs."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from rl_quant_b200 import _native as N
+
+QL_NAMES = ("actor_proprio_embedding", "query_projector", "actor.0", "actor.2", "actor.4", "actor.6")
+
+
+class DeviceWeights:
+    """Every tensor of the golden state dict on the GPU (kept alive here)."""
+
+    def __init__(self, sd: dict, device="cuda"):
+        self.t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device) for k, v in sd.items()
+                  if isinstance(v, np.ndarray) and v.dtype != np.int64}
+        self.keep = []
+
+    def __getitem__(self, k):
+        return self.t[k]
+
+    def conv(self) -> N.GladConvWeights:
+        g = lambda k: self.t[f"map_cnn.{k}"]  # noqa: E731
+        return N.conv_weights(g("w1p"), g("b1f"), g("qa"), g("qc"), g("w8"), g("dq"), g("b2f"), g("a2"), g("c2"))
+
+    def ql(self, name: str) -> N.GladQLinear:
+        t = self.t
+        w = t[f"{name}.weight"]
+        alpha = t.get(f"{name}.alpha")
+        beta = t.get(f"{name}.beta")
+        return N.GladQLinear(N.ptr(t[f"{name}.w8"]), N.ptr(t[f"{name}.dq_scale"]), N.ptr(t[f"{name}.s_w"]),
+                             N.ptr(t[f"{name}.b_prime"]), N.ptr(alpha), N.ptr(beta), N.ptr(t[f"{name}.s_z"]),
+                             N.ptr(t[f"{name}.inv_sz"]), int(w.shape[1]), int(w.shape[0]))
+
+    def actor(self) -> N.GladActorWeights:
+        t = self.t
+        w = N.GladActorWeights()
+        w.conv = self.conv()
+        w.proprio_emb = self.ql("actor_proprio_embedding")
+        w.query_proj = self.ql("query_projector")
+        w.gps_w, w.gps_b = N.ptr(t["global_pool_selector.weight"]), N.ptr(t["global_pool_selector.bias"])
+        w.scorer_w, w.scorer_b = N.ptr(t["topk_scorer.weight"]), N.ptr(t["topk_scorer.bias"])
+        w.mha_in_w, w.mha_in_b = N.ptr(t["mha.in_proj_weight"]), N.ptr(t["mha.in_proj_bias"])
+        w.mha_out_w, w.mha_out_b = N.ptr(t["mha.out_proj.weight"]), N.ptr(t["mha.out_proj.bias"])
+        for i, n in enumerate(("actor.0", "actor.2", "actor.4", "actor.6")):
+            w.mlp[i] = self.ql(n)
+        return w
+
+
+def actor_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, noise=None, with_aux=True):
+    """Run glad_actor_forward; returns (mean, aux dict of tensors)."""
+    B = obs.shape[0]
+    dev = obs.device
+    mean = torch.empty(B, 29, dtype=torch.float32, device=dev)
+    aux_t = {}
+    aux = N.GladActorAux()
+    if with_aux:
+        aux_t = {
+            "z8": torch.empty(B * 187, 16, dtype=torch.int8, device=dev),
+            "local": torch.empty(B, 187, 64, dtype=torch.float16, device=dev),
+            "gc_weights": torch.empty(B, 187, dtype=torch.float16, device=dev),
+            "score_local": torch.empty(B, 187, dtype=torch.float16, device=dev),
+            "topk_logits": torch.empty(B, 187, dtype=torch.float16, device=dev),
+            "topk_idx": torch.empty(B, 32, dtype=torch.int64, device=dev),
+            "attn_weights": torch.empty(B, 32, dtype=torch.float16, device=dev),
+            "encoded": torch.empty(B, 224, dtype=torch.float16, device=dev),
+            "act_scales": torch.empty(6, dtype=torch.float32, device=dev),
+        }
+        for k, v in aux_t.items():
+            setattr(aux, k, v.data_ptr())
+    lib = N.load()
+    ws_bytes = lib.glad_actor_workspace_size(B)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    w = dw.actor()
+    dtype = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
+    rc = lib.glad_actor_forward(w, obs.data_ptr(), dtype, B, obs.stride(0), N.ACT_MODES[act_mode],
+                                N.ptr(noise), mean.data_ptr(), aux, ws.data_ptr(), ws_bytes,
+                                N.stream_handle())
+    N.check(rc, "glad_actor_forward")
+    st = N.c_uint32(0)
+    N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
+    torch.cuda.synchronize()
+    return mean, aux_t

@@ -1,0 +1,95 @@
+"""conv operators (qrt::conv1_fused_q / conv2_int8_fused / chain) vs the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import glad_oracle as O
+from rl_quant_b200 import _native as N
+from rl_quant_b200.synthetic import glad_obs
+
+from gpu_util import DeviceWeights
+
+pytestmark = pytest.mark.gpu
+
+
+def _x_nhwc(B, seed):
+    return glad_obs(B, seed)[:, 96:].half().reshape(B, 21, 33, 3).contiguous()
+
+
+def _conv1(dw, x):
+    z8 = torch.empty(x.shape[0] * 187, 16, dtype=torch.int8, device="cuda")
+    N.check(N.load().glad_conv1_fused_q(x.data_ptr(), x.shape[0], dw.conv(), z8.data_ptr(), N.stream_handle()))
+    torch.cuda.synchronize()
+    return z8
+
+
+def _conv2(dw, z8):
+    B = z8.shape[0] // 187
+    feat = torch.empty(B * 187, 64, dtype=torch.float16, device="cuda")
+    acc = torch.empty(B * 187, 64, dtype=torch.int32, device="cuda")
+    N.check(N.load().glad_conv2_int8_fused(z8.data_ptr(), B, dw.conv(), feat.data_ptr(), acc.data_ptr(),
+                                           N.stream_handle()))
+    torch.cuda.synchronize()
+    return feat, acc
+
+
+@pytest.fixture(scope="module")
+def dw(golden_weights):
+    return DeviceWeights(golden_weights)
+
+
+@pytest.mark.parametrize("B", [1, 3, 4, 37, 600])
+def test_conv2_int32_accumulators_bit_exact(dw, golden_weights, B):
+    rng = np.random.default_rng(B)
+    z8 = rng.integers(-128, 128, size=(B * 187, 16), dtype=np.int8)
+    feat, acc = _conv2(dw, torch.from_numpy(z8).cuda())
+    w = golden_weights
+    ref_acc = O.conv2_acc(z8, w["map_cnn.w8"])
+    assert np.array_equal(acc.cpu().numpy(), ref_acc)
+    ref_feat = O.conv2_epilogue(ref_acc, w["map_cnn.dq"], w["map_cnn.b2f"], w["map_cnn.a2"], w["map_cnn.c2"])
+    assert np.array_equal(feat.cpu().numpy(), ref_feat)
+
+
+def test_conv1_matches_reference_kernel(dw, golden_conv):
+    x = torch.from_numpy(golden_conv["x_nhwc"]).cuda()
+    z8 = _conv1(dw, x).cpu().numpy().astype(np.int16)
+    ref = golden_conv["z8"].astype(np.int16)
+    diff = np.abs(z8 - ref)
+    assert diff.max() <= 1
+    assert (diff > 0).mean() < 1e-3
+
+
+@pytest.mark.parametrize("B", [1, 5, 300])
+def test_conv1_vs_oracle(dw, golden_weights, B):
+    x = _x_nhwc(B, 100 + B)
+    z8 = _conv1(dw, x.cuda()).cpu().numpy().astype(np.int16)
+    w = golden_weights
+    ref = O.conv1_fused_q(x.numpy(), w["map_cnn.w1p"], w["map_cnn.b1f"], w["map_cnn.qa"], w["map_cnn.qc"])
+    diff = np.abs(z8 - ref.astype(np.int16))
+    assert diff.max() <= 1          # only rounding ties may flip, by one step
+    assert (diff > 0).mean() < 1e-3
+
+
+@pytest.mark.parametrize("B", [2, 129])
+def test_conv_chain_equals_two_ops(dw, golden_weights, B):
+    x = _x_nhwc(B, 7 + B).cuda()
+    feat = torch.empty(B * 187, 64, dtype=torch.float16, device="cuda")
+    z8 = torch.empty(B * 187, 16, dtype=torch.int8, device="cuda")
+    N.check(N.load().glad_conv_chain(x.data_ptr(), B, dw.conv(), feat.data_ptr(), z8.data_ptr(),
+                                     N.stream_handle()))
+    torch.cuda.synchronize()
+    z8_op = _conv1(dw, x)
+    assert torch.equal(z8, z8_op)
+    feat_op, _ = _conv2(dw, z8_op)
+    assert torch.equal(feat, feat_op)
+    w = golden_weights
+    ref = O.conv2_int8_fused(z8.cpu().numpy(), w["map_cnn.w8"], w["map_cnn.dq"], w["map_cnn.b2f"],
+                             w["map_cnn.a2"], w["map_cnn.c2"])
+    assert np.array_equal(feat.cpu().numpy(), ref)
+
+
+def test_conv_rejects_bad_arguments(dw):
+    lib = N.load()
+    with pytest.raises(ValueError):
+        N.check(lib.glad_conv1_fused_q(None, 4, dw.conv(), None, N.stream_handle()))
+    assert lib.glad_conv1_fused_q(None, 0, dw.conv(), None, N.stream_handle()) == 0
