@@ -1,0 +1,333 @@
+#!/usr/bin/env python
+"""GLAD actor rollout forward benchmark on B200 (qrt full mode: INT8 QuantCNN
++ LET W8A8 linears, dynamic activation scales), env-obs/s at B=4096 per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU runs are launched by torchrun, one process per GPU; each rank owns
+its own 4096 environments (weak scaling, no data-path collective), the step
+time is the max over ranks.
+
+Timing: device time with CUDA events around K graph replays of the fused
+forward, inputs rotating over 8 observation buffers (8 x 35.6 MB > 126 MB L2)
+resident in HBM. ``e2e`` repeats the step through the public
+``InferenceRunner.act`` call with the observations copied in from pinned host
+memory and the action means copied back every step.
+
+``--impl reference`` times the reference's own CPU implementation of the
+GLAD forward (FP32 eager, rsl_rl actor_critic_encoder.py:342-350, restated in
+oracle/cpu_fp32.py) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import copy
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "GLAD actor fwd env-obs/sec & ms/step at B=4096 (INT8 LET), 1/2/4/8 B200"
+UNIT = "env-obs/s"
+INT8_PATHS = ["actor.0", "actor.2", "actor.4", "actor.6", "actor_proprio_embedding", "query_projector"]
+BYTES_PER_ENV_FWD = 8816          # obs read (fp32) + action mean write, fused ideal
+MACS_PER_ENV = 2.55e6             # conv1 .. actor MLP (int8 2.02 M + fp16 0.53 M)
+OBS_BYTES_PER_ENV = 2175 * 4      # what the front kernel must read per env
+N_STAGES = ("absmax", "front", "tail", "actor.0", "actor.2", "actor.4", "actor.6")
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--batch", type=int, default=4096)
+    p.add_argument("--act-mode", choices=("dynamic", "static"), default="dynamic")
+    p.add_argument("--nbuf", type=int, default=8)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def rank_info():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of one GPU while the timed work runs."""
+
+    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
+              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.lines: list[str] = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            gid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.cmd = ["nvidia-smi", "-i", gid, f"--query-gpu={','.join(self.FIELDS)}",
+                        "--format=csv,noheader,nounits", "-lms", "50"]
+        except Exception:  # noqa: BLE001
+            self.cmd = None
+
+    def start(self):
+        if self.cmd:
+            try:
+                self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                             text=True)
+            except OSError:
+                self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) != len(self.FIELDS):
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+def build_inference_copy(device, act_mode: str):
+    """GLAD seed-0 model -> fp16 copy -> LET calibration (200 Adam steps, 512
+    obs from seed 1) -> QuantLinear swap -> QuantCNN -> encoder rewrite, all
+    through the package's public API (qrt/integration.py:100-126)."""
+    from rl_quant_b200 import calib, calib_cnn_scale, patch_encoder, swap, swap_cnn
+    from rl_quant_b200.glad_model import build_glad
+    from rl_quant_b200.synthetic import glad_obs
+
+    model = build_glad(seed=0, critic_seed=2, dtype=torch.float32, device=device)
+    infer = copy.deepcopy(model).half().eval()
+    cal = glad_obs(512, seed=1).half().to(device)
+    batches = [{"policy_obs": cal[i * 64:(i + 1) * 64]} for i in range(8)]
+
+    def fn_factory():
+        it = iter(batches * 64)
+        return lambda: next(it)
+
+    plan = calib.make_plan(infer, INT8_PATHS, obs_fn=fn_factory(), n_calib=8, use_let=True,
+                           let_steps=200, act_mode=act_mode, verbose=False, seed=0)
+    swap.apply(infer, plan)
+    swap_cnn(infer, calib_cnn_scale(infer, fn_factory(), n_batches=8))
+    patch_encoder(infer)
+    return model, infer.eval()
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from rl_quant_b200 import InferenceRunner, _native as N
+    from rl_quant_b200.fused import FusedActor
+    from rl_quant_b200.synthetic import glad_obs
+
+    rank, local, world = rank_info()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B = args.batch
+    _, infer = build_inference_copy(device, args.act_mode)
+    fused = FusedActor(infer)
+    if fused.act_mode != args.act_mode:
+        raise RuntimeError("calibrated model has the wrong act_mode")
+
+    # inputs resident in HBM, rotated so successive steps miss L2
+    obs = [glad_obs(B, seed=1000 + 97 * rank + i).to(device) for i in range(args.nbuf)]
+    means = [torch.empty(B, 29, dtype=torch.float32, device=device) for _ in range(args.nbuf)]
+    for i in range(args.nbuf):          # warm, allocate the workspace outside capture
+        fused.run(obs[i], means[i])
+    torch.cuda.synchronize()
+    graphs = []
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for i in range(args.nbuf):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                fused.run(obs[i], means[i])
+            graphs.append(g)
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize()
+    st = N.c_uint32(0)
+    N.check(N.load().glad_workspace_status(fused.workspace(B, device).data_ptr(), st,
+                                           N.stream_handle(device)), "device status")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    clocks = ClockSampler(device)
+    clocks.start()
+    for k in range(args.warmup):
+        graphs[k % args.nbuf].replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(args.steps):
+        graphs[k % args.nbuf].replay()
+    e1.record()
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = B * world / (ms_step / 1e3)
+
+    # per-stage device time of the same forward (CUDA events between launches)
+    n_st = len(N_STAGES) + 1
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_st)]
+    for e in evs:                       # materialise the driver events
+        e.record()
+    torch.cuda.synchronize(device)
+    arr = (N.c_void_p * n_st)(*[e.cuda_event for e in evs])
+    stage_ms = [0.0] * len(N_STAGES)
+    reps = max(20, min(args.steps, 400))
+    N.check(N.load().glad_actor_stage_events(arr, n_st), "stage events")
+    try:
+        for k in range(reps):
+            fused.run(obs[k % args.nbuf], means[k % args.nbuf])
+            torch.cuda.synchronize(device)
+            for s in range(len(N_STAGES)):
+                stage_ms[s] += evs[s].elapsed_time(evs[s + 1])
+    finally:
+        N.load().glad_actor_stage_events(None, 0)
+    stage_ms = [x / reps for x in stage_ms]
+
+    # end to end through InferenceRunner.act with host buffers
+    runner = InferenceRunner(infer, mode="manual-graph")
+    host = [o.cpu().pin_memory() for o in obs[:2]]
+    dev_in = torch.empty_like(obs[0])
+    out_host = torch.empty(B, 29, dtype=torch.float32).pin_memory()
+    for k in range(5):
+        dev_in.copy_(host[k % 2], non_blocking=True)
+        out_host.copy_(runner.act(dev_in), non_blocking=True)
+    barrier()
+    k_e2e = max(10, min(args.steps, 300))
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for k in range(k_e2e):
+        dev_in.copy_(host[k % 2], non_blocking=True)
+        out_host.copy_(runner.act(dev_in), non_blocking=True)
+    e3.record()
+    barrier()
+    ms_e2e = e2.elapsed_time(e3)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_value = B * world / (ms_e2e / k_e2e / 1e3)
+
+    if rank == 0:
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+        peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+        dom = max(range(len(N_STAGES)), key=lambda i: stage_ms[i])
+        dom_name = N_STAGES[dom]
+        alg_bytes = {"front": OBS_BYTES_PER_ENV * B}.get(dom_name)
+        achieved = (alg_bytes / (stage_ms[dom] / 1e3) / 1e9) if alg_bytes else None
+        fwd_gbs = BYTES_PER_ENV_FWD * B / (ms_step / 1e3) / 1e9
+        tops = MACS_PER_ENV * 2 * B / (ms_step / 1e3) / 1e12
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle.cpu_fp32 import time_fp32_forward
+            r = time_fp32_forward(batch=256, budget_s=12.0)
+            cpu = {"value": r["obs_per_s"], "unit": UNIT, "cores": r["threads"], "kind": "port",
+                   "sample": f"FP32 eager GLAD actor forward on the host CPU, B=256 per step, "
+                             f"median of {r['reps']} steps ({r['sec_per_step'] * 1e3:.1f} ms/step)"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"GLAD actor forward, qrt full mode (INT8 QuantCNN + LET W8A8 "
+                                   f"linears, {args.act_mode} s_z), B={B} per GPU",
+                       "batch_per_gpu": B, "act_mode": args.act_mode, "obs_dtype": "fp32",
+                       "weights": "seed-0 default init, LET calibrated 200 Adam steps on 512 obs (seed 1)",
+                       "l2": f"{args.nbuf} rotating obs buffers ({args.nbuf * B * OBS_BYTES_PER_ENV / 1e6:.0f} MB) > 126 MB L2",
+                       "launch": "CUDA graph per step (memset + 7 kernels)"},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * 2175 * 4,
+                    "d2h_bytes_per_step": B * 29 * 4},
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": (achieved / hbm_peak) if achieved else None,
+                         "traffic": None, "peak_source": peak_src,
+                         "algorithmic_bytes_per_env": OBS_BYTES_PER_ENV if alg_bytes else None},
+            "forward_roofline": {"bytes_per_env": BYTES_PER_ENV_FWD, "achieved_gbs": fwd_gbs,
+                                 "frac_hbm": fwd_gbs / hbm_peak, "macs_per_env": MACS_PER_ENV,
+                                 "achieved_tops": tops},
+            "stage_ms": dict(zip(N_STAGES, stage_ms)),
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps * (7 if args.act_mode == "dynamic" else 6),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del graphs
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank, _, world = rank_info()
+    if rank != 0:
+        return
+    from oracle.cpu_fp32 import time_fp32_forward
+
+    per_step_budget = 60.0 / max(args.steps + args.warmup, 1)
+    r0 = time_fp32_forward(batch=256, budget_s=0.0, min_reps=2, max_reps=2)
+    steps = args.steps
+    if r0["sec_per_step"] > per_step_budget:
+        steps = max(3, int(60.0 / r0["sec_per_step"]))
+    r = time_fp32_forward(batch=256, budget_s=0.0, min_reps=steps, max_reps=steps)
+    v = r["obs_per_s"]
+    line = {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": r["reps"],
+        "warmup": 2, "ms_per_step": r["sec_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"GLAD actor forward (FP32 eager, reference CPU path), B=256 sample per "
+                               f"step of the B={args.batch} workload", "batch_per_step": 256},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": r["threads"], "kind": "port",
+                         "sample": f"B=256 per step, median of {r['reps']} steps"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

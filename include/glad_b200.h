@@ -96,7 +96,7 @@ typedef struct GladActorAux {
   void* local;           /* [B,187,64] f16  local features (conv2 output)       */
   void* gc_weights;      /* [B,187]   f16   global softmax pool weights         */
   void* score_local;     /* [B,187]   f16   scorer logits of the local half     */
-  void* topk_logits;     /* [B,187]   f16   score_local + score_query           */
+  void* topk_logits;     /* [B,187]   f16   logits the top-32 ran on (+noise)   */
   int64_t* topk_idx;     /* [B,32]    i64   value desc, ties by lower index     */
   void* attn_weights;    /* [B,32]    f16   head-mean attention weights         */
   void* encoded;         /* [B,224]   f16   cat(foothold, gc, proprio)          */
@@ -137,7 +137,8 @@ int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int 
  * The compiled actor function of qrt full mode (qrt/integration.py:129-131;
  * runtime.py:98-99): _encode_terrain_opt (qrt/encoder_opt.py:41-123) over
  * QuantCNN/QuantLinear, then the INT8 actor MLP. obs [B, 96+2079] (f32 or
- * f16, row stride ld_obs elements) -> mean f32 [B,29].
+ * f16, row stride ld_obs elements) -> mean f32 [B,29]. With mean_out NULL
+ * only the encoder runs (aux->encoded must then be set).
  * `topk_noise` (NULL or f32 [B,187]) is added to the top-k logits before
  * selection (the Gumbel term of train-mode rollouts, qrt/encoder_opt.py:87-91). */
 size_t glad_actor_workspace_size(int64_t B);
@@ -145,6 +146,13 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
                        int64_t ld_obs, int act_mode, const float* topk_noise, float* mean_out,
                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/* Diagnostics: record CUDA events (cudaEvent_t, passed as void*) between the
+ * stages of the following glad_actor_forward calls on this host thread:
+ * events[0] before the first launch, then one after each stage (absmax, front,
+ * tail, actor.0, actor.2, actor.4, actor.6), so n = 8 covers a dynamic-mode
+ * call. n = 0 switches recording off. Not part of the reference interface.  */
+int glad_actor_stage_events(void* const* events, int n);
 
 /* Device-side status word of the last launches that used `workspace`
  * (0 = fine; bits = a bounded wait ran out). Synchronises `stream`.        */
@@ -169,9 +177,10 @@ typedef struct GladQLinearSrc {
 } GladQLinearSrc;
 int glad_requant_qlinear(const GladQLinearSrc* layers, int n, void* stream);
 
-/* QuantCNN.requantize_ without LET (qrt/qconv.py:247-284) in place. All
- * parameters are the fp16 inference copy's (conv weights/biases, BN
- * weight/bias/running stats); s_z 0-d f32; eps the BatchNorm eps.         */
+/* QuantCNN.requantize_ (qrt/qconv.py:247-284) in place. Parameters are the
+ * inference copy's (conv weights/biases, BN weight/bias/running stats) in
+ * `dtype`; the BN affine is evaluated in that dtype as the reference does.
+ * s_z 0-d f32; eps the BatchNorm eps.                                       */
 typedef struct GladQCNNSrc {
   const void* conv1_w; const void* conv1_b;
   const void* bn1_w; const void* bn1_b; const void* bn1_mean; const void* bn1_var;
@@ -181,6 +190,9 @@ typedef struct GladQCNNSrc {
   float eps1, eps2;
   void* w1p; float* b1f; float* qa; float* qc;
   int8_t* w8; float* dq; float* b2f; float* a2; float* c2;
+  int32_t dtype;          /* GLAD_DTYPE_F16 (fp16 copy) or F32, for every parameter */
+  const float* alpha;     /* [16] LET of conv2's input, or NULL (qrt/qconv.py:256-258,271-272) */
+  const float* beta;      /* [16] or NULL */
 } GladQCNNSrc;
 int glad_requant_qcnn(const GladQCNNSrc* src, void* stream);
 

@@ -77,7 +77,9 @@ def bn_affine16(weight, bias, mean, var, eps=1e-5):
     """Eval BatchNorm as ``a*x+c``, evaluated on the fp16 copy's tensors:
     ``a`` is computed in fp16 then widened (qrt/qconv.py:252-255)."""
     w, bb, mu, v = (np.asarray(t).astype(f16) for t in (weight, bias, mean, var))
-    a = (w / np.sqrt((v + f16(eps)).astype(f16)).astype(f16)).astype(f16).astype(f32)
+    # fp16 tensor + python float: computed in fp32, rounded to fp16
+    den = np.sqrt((v.astype(f32) + f32(eps)).astype(f16)).astype(f16)
+    a = (w / den).astype(f16).astype(f32)
     c = (bb.astype(f32) - a * mu.astype(f32)).astype(f32)
     return a, c
 

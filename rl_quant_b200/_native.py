@@ -59,7 +59,8 @@ class GladQCNNSrc(Structure):
         "conv1_w", "conv1_b", "bn1_w", "bn1_b", "bn1_mean", "bn1_var",
         "conv2_w", "conv2_b", "bn2_w", "bn2_b", "bn2_mean", "bn2_var", "s_z")] + [
         ("eps1", c_float), ("eps2", c_float)] + [
-        (n, c_void_p) for n in ("w1p", "b1f", "qa", "qc", "w8", "dq", "b2f", "a2", "c2")]
+        (n, c_void_p) for n in ("w1p", "b1f", "qa", "qc", "w8", "dq", "b2f", "a2", "c2")] + [
+        ("dtype", c_int32), ("alpha", c_void_p), ("beta", c_void_p)]
 
 
 class GladCastCopy(Structure):
@@ -80,6 +81,7 @@ SIGNATURES = {
     "glad_actor_workspace_size": (c_size_t, [c_int64]),
     "glad_actor_forward": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int, c_void_p,
                                    c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
+    "glad_actor_stage_events": (c_int, [POINTER(c_void_p), c_int]),
     "glad_workspace_status": (c_int, [c_void_p, POINTER(c_uint32), c_void_p]),
     "glad_requant_qlinear": (c_int, [POINTER(GladQLinearSrc), c_int, c_void_p]),
     "glad_requant_qcnn": (c_int, [POINTER(GladQCNNSrc), c_void_p]),

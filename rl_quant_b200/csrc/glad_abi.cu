@@ -34,6 +34,13 @@ using namespace glad;
 namespace {
 
 thread_local char g_err[512] = "";
+thread_local cudaEvent_t g_stage_ev[16];
+thread_local int g_stage_n = 0;
+
+// Record stage event `i` (if diagnostics are on) on `st`.
+void stage_mark(int i, cudaStream_t st) {
+  if (i < g_stage_n) cudaEventRecord(g_stage_ev[i], st);
+}
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -319,7 +326,9 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
     return fail(GLAD_ERR_INVALID_ARG, "actor proprio width %d; the fused path is built for 96", P);
   if (ld_obs < P + kMap) return fail(GLAD_ERR_INVALID_ARG, "ld_obs %lld < %d", (long long)ld_obs, P + kMap);
   if (B == 0) return GLAD_OK;
-  if (!obs || !mean_out) return fail(GLAD_ERR_INVALID_ARG, "obs and mean_out must be set");
+  if (!obs) return fail(GLAD_ERR_INVALID_ARG, "obs must be set");
+  if (!mean_out && !(aux && aux->encoded))
+    return fail(GLAD_ERR_INVALID_ARG, "encoder-only call (mean_out NULL) needs aux->encoded");
   if (!aligned(obs, obs_dtype == GLAD_DTYPE_F32 ? 4 : 2))
     return fail(GLAD_ERR_INVALID_ARG, "obs is not element-aligned");
   int rc = check_conv(&w->conv, true, true);
@@ -350,11 +359,13 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   if (!aligned(z8, 16) || !aligned(enc, 16))
     return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded must be 16-byte aligned");
 
+  stage_mark(0, st);
   GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
   if (act_mode == GLAD_ACT_DYNAMIC)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb.alpha,
                                   w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st),
                     "absmax launch");
+  stage_mark(1, st);
   FrontParams fp{};
   fp.in = obs;
   fp.ld = ld_obs;
@@ -376,6 +387,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
   GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 4), st), "front launch");
+  stage_mark(2, st);
 
   TailParams tp{};
   tp.B = B;
@@ -402,9 +414,10 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   const int64_t groups = (B + 3) / 4;
   const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
   GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st), "tail launch");
+  stage_mark(3, st);
 
   __half* hs[4] = {enc, ws.h1, ws.h2, ws.h3};
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < (mean_out ? 4 : 0); ++i) {
     GemmParams g{};
     g.L = w->mlp[i];
     g.act_mode = act_mode;
@@ -426,9 +439,11 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
     } else {
       g.y32 = mean_out;
       g.ldy32 = kActions;
+      g.y32_round16 = 1;                   // mean = fp16 output .float() (integration.py:206)
       g.next_slot = -1;
       GLAD_CHECK_CUDA(launch_qgemm<32>(g, st), "actor head launch");
     }
+    stage_mark(4 + i, st);
   }
   if (ax.act_scales) {
     const float* sz[6] = {w->proprio_emb.s_z, w->query_proj.s_z, w->mlp[0].s_z,
@@ -439,6 +454,15 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
     GLAD_CHECK_CUDA(launch_act_scales(ws.slots, act_mode, sz, let, ax.act_scales, st),
                     "scale launch");
   }
+  return GLAD_OK;
+}
+
+int glad_actor_stage_events(void* const* events, int n) {
+  g_err[0] = 0;
+  if (n < 0 || n > 16 || (n > 0 && !events))
+    return fail(GLAD_ERR_INVALID_ARG, "0..16 events required");
+  for (int i = 0; i < n; ++i) g_stage_ev[i] = reinterpret_cast<cudaEvent_t>(events[i]);
+  g_stage_n = n;
   return GLAD_OK;
 }
 
@@ -474,6 +498,10 @@ int glad_requant_qlinear(const GladQLinearSrc* layers, int n, void* stream) {
 
 int glad_requant_qcnn(const GladQCNNSrc* s, void* stream) {
   g_err[0] = 0;
+  if (s && s->dtype != GLAD_DTYPE_F16 && s->dtype != GLAD_DTYPE_F32)
+    return fail(GLAD_ERR_INVALID_ARG, "QuantCNN requant: unknown dtype %d", s->dtype);
+  if (s && (s->alpha == nullptr) != (s->beta == nullptr))
+    return fail(GLAD_ERR_INVALID_ARG, "QuantCNN requant: alpha and beta must both be set or NULL");
   if (!s || !s->conv1_w || !s->conv1_b || !s->bn1_w || !s->bn1_b || !s->bn1_mean || !s->bn1_var ||
       !s->conv2_w || !s->conv2_b || !s->bn2_w || !s->bn2_b || !s->bn2_mean || !s->bn2_var ||
       !s->s_z || !s->w1p || !s->b1f || !s->qa || !s->qc || !s->w8 || !s->dq || !s->b2f || !s->a2 ||

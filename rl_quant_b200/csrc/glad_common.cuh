@@ -79,9 +79,13 @@ __device__ __forceinline__ float out_scale(const GladQLinear& L, const ActQuant&
   return a.dyn ? __fmul_rn(L.s_w[n], a.s) : L.dq_scale[n];
 }
 
-// int32 accumulator -> fp16 output: y = acc*scale + b' in fp32, then fp16.
+// int32 accumulator -> output: y = acc*scale + b' in fp32 (qrt/qlinear.py:135).
+__device__ __forceinline__ float qlinear_out32(int32_t acc, float scale, float bprime) {
+  return __fadd_rn(__fmul_rn((float)acc, scale), bprime);
+}
+// ... then cast to the fp16 input dtype (qrt/qlinear.py:138).
 __device__ __forceinline__ __half qlinear_out(int32_t acc, float scale, float bprime) {
-  return __float2half_rn(__fadd_rn(__fmul_rn((float)acc, scale), bprime));
+  return __float2half_rn(qlinear_out32(acc, scale, bprime));
 }
 
 // ELU on an fp16 value (computed in fp32, rounded to fp16).
@@ -215,6 +219,7 @@ struct GemmParams {
   int64_t ldy;
   float* y32;              // [M,ldy32] f32 output (or null)
   int64_t ldy32;
+  int y32_round16;         // y32 holds float(fp16(y)) instead of the fp32 y
   int elu;                 // apply ELU to the fp16 output
   const float* next_alpha; // LET of the consumer layer (absmax of its input)
   const float* next_beta;

@@ -54,6 +54,10 @@ struct __align__(128) FrontSmem {
   __half pe16[64];
   __half gc16[64];
   alignas(16) int8_t q8[128];           // quantised proprio
+  alignas(16) int8_t pe_w8[64 * 128];   // actor_proprio_embedding int8 rows (K <= 128)
+  float pe_a[128], pe_b[128];           // its LET alpha / beta
+  float pe_scale[64], pe_bp[64];        // its output scale and bias
+  float qp_a[128], qp_b[128];           // query_projector LET (absmax of its input)
   uint64_t mbar;
   uint32_t tmem_base;
   int abort_flag;
@@ -184,6 +188,20 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
     aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
     aq_qp.let = p.qp.alpha != nullptr;
     gb = __half2float(p.gps_b[0]);
+    const int P = p.prop_dim;
+    for (int i = tid; i < kD * P / 4; i += 128)
+      reinterpret_cast<int*>(s.pe_w8)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
+    for (int k = tid; k < P; k += 128) {
+      s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
+      s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;
+    }
+    if (tid < kD) {
+      s.pe_scale[tid] = out_scale(p.pe, aq_pe, tid);
+      s.pe_bp[tid] = p.pe.b_prime[tid];
+    }
+    s.qp_a[tid] = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
+    s.qp_b[tid] = aq_qp.let ? p.qp.beta[tid] : 0.0f;
+    __syncthreads();
   }
 
   const int esz = (MODE == kModeConv2) ? 1 : (p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2);
@@ -258,19 +276,16 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
       if (kFront) {
         // proprio embedding while the tensor core runs (qrt/qlinear.py:123-138)
         const int P = p.prop_dim;
-        for (int k = tid; k < P; k += 128) {
-          const float a = aq_pe.let ? p.pe.alpha[k] : 0.0f;
-          const float b = aq_pe.let ? p.pe.beta[k] : 0.0f;
-          s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[k]), a, b);
-        }
+        for (int k = tid; k < P; k += 128)
+          s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[k]), s.pe_a[k], s.pe_b[k]);
         __syncthreads();
         if (tid < kD) {
           const int n = tid;
-          const int* wrow = reinterpret_cast<const int*>(p.pe.w8 + (int64_t)n * P);
+          const int* wrow = reinterpret_cast<const int*>(s.pe_w8 + n * P);
           const int* qw = reinterpret_cast<const int*>(s.q8);
           int acc = 0;
-          for (int k4 = 0; k4 < P / 4; ++k4) acc = __dp4a(qw[k4], __ldg(wrow + k4), acc);
-          s.pe16[n] = qlinear_out(acc, out_scale(p.pe, aq_pe, n), p.pe.b_prime[n]);
+          for (int k4 = 0; k4 < P / 4; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
+          s.pe16[n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
         }
       }
 
@@ -351,6 +366,7 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
 
       // ---- conv2 epilogue, pass 1 -------------------------------------------------------
       float my_logit[2];
+      uint32_t pend[16];
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         const int m = t * 128 + 32 * warp + lane;
@@ -360,9 +376,15 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
         float l0 = 0.0f, l1 = 0.0f;
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
-          uint32_t r[16];
-          tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
-          tmem_ld_wait();
+          uint32_t r[16], r_next[16];
+          if ((cb & 1) == 0) {
+            tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
+            tmem_ld16(tmem + lane_base + t * 64 + cb * 16 + 16, r_next);
+            tmem_ld_wait();
+            for (int j = 0; j < 16; ++j) pend[j] = r_next[j];
+          } else {
+            for (int j = 0; j < 16; ++j) r[j] = pend[j];
+          }
           __half h[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -422,14 +444,17 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
           const float wt = valid ? __half2float(wh) : 0.0f;
           float v[64];
 #pragma unroll
-          for (int cb = 0; cb < 4; ++cb) {
-            uint32_t r[16];
+          for (int cb = 0; cb < 4; cb += 2) {
+            uint32_t r[16], r2[16];
             tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
+            tmem_ld16(tmem + lane_base + t * 64 + cb * 16 + 16, r2);
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int c = cb * 16 + j;
               v[c] = wt * __half2float(conv2_out((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]));
+              v[c + 16] = wt * __half2float(conv2_out((int32_t)r2[j], s.dq[c + 16], s.b2[c + 16],
+                                                      s.a2[c + 16], s.c2[c + 16]));
             }
           }
           warp_reduce64(v, lane);
@@ -453,9 +478,7 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
         if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
           // |alpha*cat(gc, pe) + beta| for the query projector's dynamic s_z
           const float x = __half2float(tid < kD ? s.gc16[tid] : s.pe16[tid - kD]);
-          const float a = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
-          const float b = aq_qp.let ? p.qp.beta[tid] : 0.0f;
-          zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, a, b));
+          zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, s.qp_a[tid], s.qp_b[tid]));
         }
       } else {
         tc_fence_before();
@@ -489,8 +512,8 @@ size_t front_smem_bytes() { return sizeof(FrontSmem) + 128; }
 template <int MODE>
 cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st) {
   const size_t smem = front_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(front_kernel<MODE>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static bool done[64] = {false};
+  cudaError_t e = allow_max_smem((const void*)front_kernel<MODE>, done);
   if (e != cudaSuccess) return e;
   front_kernel<MODE><<<grid, 128, smem, st>>>(p);
   return cudaGetLastError();

@@ -142,10 +142,12 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
       tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + cb * 16, rr);
       tmem_ld_wait();
       __half h[16];
+      float f[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int jj = cb * 16 + j;
-        h[j] = qlinear_out((int32_t)rr[j], cscale[jj], cbias[jj]);
+        f[j] = qlinear_out32((int32_t)rr[j], cscale[jj], cbias[jj]);
+        h[j] = __float2half_rn(f[j]);
         if (p.elu) h[j] = elu16(h[j]);
       }
       if (row_ok) {
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
           const int n = nb + j;
           if (n < N) {
             if (p.y) p.y[m * p.ldy + n] = h[j];
-            if (p.y32) p.y32[m * p.ldy32 + n] = __half2float(h[j]);
+            if (p.y32) p.y32[m * p.ldy32 + n] = p.y32_round16 ? __half2float(h[j]) : f[j];
             if (p.next_slot >= 0)
               zmax = fmaxf(zmax, nq.absz(__half2float(h[j]), calpha[cb * 16 + j], cbeta[cb * 16 + j]));
           }
@@ -188,8 +190,8 @@ size_t qgemm_smem_bytes(int K, int NT) {
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st) {
   const size_t smem = qgemm_smem_bytes(p.L.in_features, NT);
-  cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<NT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static bool done[64] = {false};
+  cudaError_t e = allow_max_smem((const void*)qgemm_kernel<NT>, done);
   if (e != cudaSuccess) return e;
   const int Np = (p.L.out_features + 7) & ~7;
   dim3 grid((unsigned)((p.M + 127) / 128), (unsigned)((Np + NT - 1) / NT));
@@ -312,57 +314,74 @@ cudaError_t launch_requant_qlinear(const GladQLinearSrc* layers, int n, cudaStre
 }
 
 // ---- QuantCNN.requantize_ (qrt/qconv.py:247-284), no LET -------------------------------
-__device__ __forceinline__ float h2f(const void* p, int i) {
-  return __half2float(reinterpret_cast<const __half*>(p)[i]);
-}
-
 __global__ void requant_qcnn_kernel(const __grid_constant__ GladQCNNSrc s) {
   const int tid = threadIdx.x;
   const float sz = *s.s_z;
-  // BN affine evaluated in fp16 (the inference copy is fp16), then widened.
-  auto bn = [](const void* w, const void* b, const void* mu, const void* var, float eps, int c,
-               float& a, float& cc) {
-    const float den = fp16r(sqrtf(fp16r(__fadd_rn(h2f(var, c), fp16r(eps)))));
-    a = fp16r(__fdiv_rn(h2f(w, c), den));
-    cc = __fsub_rn(h2f(b, c), __fmul_rn(a, h2f(mu, c)));
+  const int dt = s.dtype;
+  const bool h16 = dt == GLAD_DTYPE_F16;
+  auto rd = [dt](const void* p, int i) { return load_w(p, dt, i); };
+  // BN affine y = a*x + c evaluated in the parameters' dtype, then widened
+  // (qrt/qconv.py:252-255).
+  auto bn = [&](const void* w, const void* b, const void* mu, const void* var, float eps, int c,
+                float& a, float& cc) {
+    if (h16) {
+      const float den = fp16r(sqrtf(fp16r(__fadd_rn(rd(var, c), eps))));
+      a = fp16r(__fdiv_rn(rd(w, c), den));
+    } else {
+      a = __fdiv_rn(rd(w, c), sqrtf(__fadd_rn(rd(var, c), eps)));
+    }
+    cc = __fsub_rn(rd(b, c), __fmul_rn(a, rd(mu, c)));
   };
   if (tid < 16) {
     float a1, c1;
     bn(s.bn1_w, s.bn1_b, s.bn1_mean, s.bn1_var, s.eps1, tid, a1, c1);
+    if (s.alpha) {                        // LET folded into BN1 (qrt/qconv.py:256-258)
+      a1 = __fmul_rn(a1, s.alpha[tid]);
+      c1 = __fadd_rn(__fmul_rn(c1, s.alpha[tid]), s.beta ? s.beta[tid] : 0.0f);
+    }
     s.qa[tid] = __fdiv_rn(a1, sz);
     s.qc[tid] = __fdiv_rn(c1, sz);
-    s.b1f[tid] = h2f(s.conv1_b, tid);
+    s.b1f[tid] = rd(s.conv1_b, tid);
   }
   // w1p [128,16]: k = kh*16 + kw*3 + c for kh<5, kw*3+c<15
   for (int idx = tid; idx < 128 * 16; idx += blockDim.x) {
     const int k = idx >> 4, n = idx & 15;
     const int kh = k >> 4, r = k & 15;
-    __half v = __float2half(0.0f);
+    float v = 0.0f;
     if (kh < 5 && r < 15) {
       const int kw = r / 3, c = r % 3;
-      v = reinterpret_cast<const __half*>(s.conv1_w)[((n * 3 + c) * 5 + kh) * 5 + kw];
+      v = rd(s.conv1_w, ((n * 3 + c) * 5 + kh) * 5 + kw);
     }
-    reinterpret_cast<__half*>(s.w1p)[idx] = v;
+    reinterpret_cast<__half*>(s.w1p)[idx] = __float2half_rn(v);
   }
   if (tid < 64) {
     const int n = tid;
-    float amax = 0.0f;
-    for (int i = 0; i < 144; ++i) amax = fmaxf(amax, fabsf(h2f(s.conv2_w, n * 144 + i)));
+    // conv2_w [64][16][3][3] -> W' = W/alpha per input channel (LET, qconv.py:271-272)
+    auto w2 = [&](int c, int kh, int kw) {
+      const float w = rd(s.conv2_w, ((n * 16 + c) * 3 + kh) * 3 + kw);
+      return s.alpha ? __fdiv_rn(w, s.alpha[c]) : w;
+    };
+    float amax = 0.0f, bsum = 0.0f;
+    for (int c = 0; c < 16; ++c)
+      for (int kh = 0; kh < 3; ++kh)
+        for (int kw = 0; kw < 3; ++kw) {
+          const float w = w2(c, kh, kw);
+          amax = fmaxf(amax, fabsf(w));
+          if (s.alpha && s.beta) bsum += __fmul_rn(w, s.beta[c]);
+        }
     const float s_w = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
-    // conv2_w [64][16][3][3]; w8[kh][kw*16 + c][n]
+    // w8[kh][kw*16 + c][n]
     for (int kh = 0; kh < 3; ++kh)
       for (int ks = 0; ks < 64; ++ks) {
         int q = 0;
         if (ks < 48) {
-          const int kw = ks >> 4, c = ks & 15;
-          const float w = h2f(s.conv2_w, ((n * 16 + c) * 3 + kh) * 3 + kw);
-          q = __float2int_rn(__fdiv_rn(w, s_w));
+          q = __float2int_rn(__fdiv_rn(w2(ks & 15, kh, ks >> 4), s_w));
           q = q < -128 ? -128 : (q > 127 ? 127 : q);
         }
         s.w8[(kh * 64 + ks) * 64 + n] = (int8_t)q;
       }
     s.dq[n] = __fmul_rn(s_w, sz);
-    s.b2f[n] = h2f(s.conv2_b, n);
+    s.b2f[n] = __fsub_rn(rd(s.conv2_b, n), bsum);   // b' = b - sum W'*beta (qconv.py:280-281)
     float a2, c2;
     bn(s.bn2_w, s.bn2_b, s.bn2_mean, s.bn2_var, s.eps2, n, a2, c2);
     s.a2[n] = a2;

@@ -369,8 +369,8 @@ size_t tail_smem_bytes() { return sizeof(TailSmem) + 128; }
 
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st) {
   const size_t smem = tail_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  static bool done[64] = {false};
+  cudaError_t e = allow_max_smem((const void*)tail_kernel, done);
   if (e != cudaSuccess) return e;
   tail_kernel<<<grid, 128, smem, st>>>(p);
   return cudaGetLastError();

@@ -7,6 +7,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 
 namespace glad {
 
@@ -190,6 +191,23 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Raise a kernel's dynamic shared-memory limit to the opt-in maximum, once per
+// device (`done` is the caller's per-kernel flag array). The limit is a
+// per-function attribute shared by every launch and every captured graph
+// node, so it is never lowered.
+inline cudaError_t allow_max_smem(const void* kernel, bool (&done)[64]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  int optin = 0;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+  return e;
 }
 
 // atomicMax on a non-negative float stored as its bit pattern.

@@ -1,0 +1,120 @@
+"""Driver of the fused GLAD forward (``glad_actor_forward``).
+
+``FusedActor`` reads the quantised model in place: the C weight struct holds
+pointers to the modules' own buffers and parameters (QuantCNN, QuantLinear,
+fp16 GPS selector / scorer / MHA), so ``requantize_`` / ``sync_weights_from``
+updates are seen by the next call and by captured CUDA graphs.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _native as N
+from .qconv import QuantCNN
+from .qlinear import QuantLinear
+
+MLP_PATHS = ("actor.0", "actor.2", "actor.4", "actor.6")
+
+
+class FusedUnsupported(NotImplementedError):
+    pass
+
+
+def _fp16(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+        raise FusedUnsupported(f"{name} must be a contiguous fp16 CUDA tensor (the inference copy is .half())")
+    return t
+
+
+def model_act_mode(model: nn.Module) -> str:
+    modes = {m.act_mode for m in model.modules() if isinstance(m, QuantLinear)}
+    if len(modes) != 1 or not modes <= {"static", "dynamic"}:
+        raise FusedUnsupported(f"fused path needs one act_mode in {{static, dynamic}}, model has {sorted(modes)}")
+    return modes.pop()
+
+
+class FusedActor:
+    """The fused encoder (+ INT8 actor MLP) of one GLAD inference copy."""
+
+    def __init__(self, model: nn.Module, need_mlp: bool = True):
+        self.model = model
+        self.check(model, need_mlp)
+        self.act_mode = model_act_mode(model)
+        self._ws: dict[tuple, torch.Tensor] = {}
+
+    @staticmethod
+    def check(model: nn.Module, need_mlp: bool = True) -> None:
+        if not isinstance(model.map_cnn, QuantCNN):
+            raise FusedUnsupported("map_cnn is not a QuantCNN (swap_cnn first)")
+        for p in ("actor_proprio_embedding", "query_projector") + (MLP_PATHS if need_mlp else ()):
+            if not isinstance(model.get_submodule(p), QuantLinear):
+                raise FusedUnsupported(f"{p} is not a QuantLinear (swap.apply the qrt INT8 paths)")
+        if model.actor_proprio_embedding.in_features != 96:
+            raise FusedUnsupported("the fused encoder is built for a 96-wide actor proprio")
+        if getattr(model, "num_heads", 16) != 16 or getattr(model, "mha_dim", 64) != 64:
+            raise FusedUnsupported("the fused encoder is built for D=64, 16 heads")
+
+    def weights(self) -> N.GladActorWeights:
+        m = self.model
+        w = N.GladActorWeights()
+        w.conv = m.map_cnn.conv_struct()
+        w.proprio_emb = N.qlinear_struct(m.actor_proprio_embedding)
+        w.query_proj = N.qlinear_struct(m.query_projector)
+        w.gps_w = _fp16(m.global_pool_selector.weight, "global_pool_selector.weight").data_ptr()
+        w.gps_b = _fp16(m.global_pool_selector.bias, "global_pool_selector.bias").data_ptr()
+        w.scorer_w = _fp16(m.topk_scorer.weight, "topk_scorer.weight").data_ptr()
+        w.scorer_b = _fp16(m.topk_scorer.bias, "topk_scorer.bias").data_ptr()
+        w.mha_in_w = _fp16(m.mha.in_proj_weight, "mha.in_proj_weight").data_ptr()
+        w.mha_in_b = _fp16(m.mha.in_proj_bias, "mha.in_proj_bias").data_ptr()
+        w.mha_out_w = _fp16(m.mha.out_proj.weight, "mha.out_proj.weight").data_ptr()
+        w.mha_out_b = _fp16(m.mha.out_proj.bias, "mha.out_proj.bias").data_ptr()
+        for i, p in enumerate(MLP_PATHS):
+            layer = m.get_submodule(p)
+            if isinstance(layer, QuantLinear):
+                w.mlp[i] = N.qlinear_struct(layer)
+        return w
+
+    def workspace(self, B: int, device) -> torch.Tensor:
+        key = (B, str(device))
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = torch.empty(N.load().glad_actor_workspace_size(B), dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+    def run(self, obs: torch.Tensor, mean: torch.Tensor | None, aux: N.GladActorAux | None = None,
+            noise: torch.Tensor | None = None) -> None:
+        """Launch the fused forward on the current stream (no host sync)."""
+        N.require_cuda(obs)
+        if obs.dim() != 2 or obs.stride(1) != 1:
+            raise ValueError("obs must be a row-major [B, 96+2079] tensor")
+        if obs.dtype not in (torch.float32, torch.float16):
+            raise TypeError("obs must be float32 or float16")
+        B = obs.shape[0]
+        ws = self.workspace(B, obs.device)
+        rc = N.load().glad_actor_forward(
+            self.weights(), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
+            B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise), N.ptr(mean), aux,
+            ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
+        N.check(rc, "glad_actor_forward")
+
+    def act(self, obs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        B = obs.shape[0]
+        mean = out if out is not None else torch.empty(B, 29, dtype=torch.float32, device=obs.device)
+        self.run(obs, mean)
+        return mean
+
+    def encode(self, obs: torch.Tensor, noise: torch.Tensor | None = None):
+        """``_encode_terrain`` outputs: (encoded [B,224] fp16, attn_weights [B,1,32],
+        topk_indices [B,32] int64, gc_weights [B,187,1])."""
+        B, dev = obs.shape[0], obs.device
+        enc = torch.empty(B, 224, dtype=torch.float16, device=dev)
+        attn = torch.empty(B, 1, 32, dtype=torch.float16, device=dev)
+        idx = torch.empty(B, 32, dtype=torch.int64, device=dev)
+        gcw = torch.empty(B, 187, 1, dtype=torch.float16, device=dev)
+        aux = N.GladActorAux()
+        aux.encoded, aux.attn_weights, aux.topk_idx, aux.gc_weights = (
+            enc.data_ptr(), attn.data_ptr(), idx.data_ptr(), gcw.data_ptr())
+        self.run(obs, None, aux, noise)
+        return enc, attn, idx, gcw

@@ -1,0 +1,214 @@
+"""InferenceRunner: rollout inference of a GLAD inference copy (qrt/runtime.py:63-275).
+
+Modes (qrt/runtime.py:34-37, 83-84):
+  "max-autotune" / "manual-graph": the fused forward is captured once per
+      (batch, dtype, device) in a CUDA graph with static input/output buffers;
+      each call copies the observations in and replays.
+  "eager": the fused forward is launched directly each call.
+
+The fused path needs the qrt full-mode layout (QuantCNN + QuantLinear on the
+encoder and actor MLP). A model without it runs ``act_inference`` op by op.
+
+Weight hand-over (qrt/runtime.py:195-271): ``refresh_quant`` requantises
+every quantised layer in two launches (all QuantLinears in one table, the
+QuantCNN in one); ``sync_weights_from`` adds one batched cast-copy of every
+same-named parameter/buffer. Both are captured as one CUDA graph on first
+use; buffers never move, so captured forwards stay valid.
+"""
+from __future__ import annotations
+
+import warnings
+
+import torch
+
+from . import _native as N
+from .encoder_opt import _gumbel_noise
+from .fused import FusedActor, FusedUnsupported
+from .qconv import QuantCNN
+from .qlinear import QuantLinear
+
+_MODES = ("max-autotune", "manual-graph", "eager")
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == torch.float16:
+        return N.DTYPE_F16
+    if t.dtype == torch.float32:
+        return N.DTYPE_F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+class _Graph:
+    def __init__(self, fn, static_in):
+        self.static_in = static_in
+        s = torch.cuda.Stream(device=static_in.device)
+        s.wait_stream(torch.cuda.current_stream(static_in.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                fn(static_in)
+        torch.cuda.current_stream(static_in.device).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = fn(static_in)
+
+    def __call__(self, x):
+        if x.data_ptr() != self.static_in.data_ptr():
+            self.static_in.copy_(x)
+        self.graph.replay()
+        return self.out
+
+
+class InferenceRunner:
+    def __init__(self, model, mode: str = "max-autotune", with_critic: bool = False,
+                 clone_outputs: bool = False):
+        if mode not in _MODES:
+            raise ValueError(f"unknown mode: {mode}")
+        if model.training:
+            warnings.warn("[rl_quant_b200] model is in train mode; call model.eval() for rollouts")
+        self.model = model
+        self.mode = mode
+        self.with_critic = with_critic
+        self.clone_outputs = clone_outputs
+        self._quant_layers = [m for m in model.modules() if m is not model and hasattr(m, "requantize_")]
+        try:
+            self._fused = FusedActor(model)
+        except FusedUnsupported as e:
+            self._fused = None
+            warnings.warn(f"[rl_quant_b200] fused GLAD forward unavailable ({e}); running op by op")
+        self._graphs: dict[tuple, _Graph] = {}
+        self._g_refresh = None
+        self._g_sync = None
+        self._sync_items = None
+
+    # -- forward functions ----------------------------------------------------------------
+    def _act_fn(self, po):
+        if self._fused is not None:
+            mean = torch.empty(po.shape[0], 29, dtype=torch.float32, device=po.device)
+            # train-mode rollouts keep the Gumbel top-k exploration (qrt/encoder_opt.py:87-91)
+            noise = _gumbel_noise((po.shape[0], 187), po.device) if self.model.training else None
+            self._fused.run(po, mean, noise=noise)
+            return mean
+        return self.model.act_inference({"policy_obs": po})[0]
+
+    def _val_fn(self, co):
+        m = self.model
+        c = m.critic_obs_normalizer(co)
+        enc_fn = getattr(m, "_encode_terrain_orig", None) if co.shape[1] - 2079 != getattr(
+            m, "actor_proprio_dim", -1) else None
+        enc, _, _, _ = (enc_fn or m._encode_terrain)(c)
+        return m.critic(enc)
+
+    def _call(self, key, fn, x):
+        if self.mode == "eager":
+            return fn(x)
+        k = (key, tuple(x.shape), x.dtype, x.device)
+        g = self._graphs.get(k)
+        if g is None:
+            g = _Graph(fn, x.clone())
+            self._graphs[k] = g
+        out = g(x)
+        return out.clone() if self.clone_outputs else out
+
+    # -- public API (qrt/runtime.py:128-191) ------------------------------------------------
+    @torch.inference_mode()
+    def warmup(self, example_po, example_co=None, n_warmup: int = 3):
+        for _ in range(n_warmup):
+            self.act(example_po)
+        if self.with_critic:
+            if example_co is None:
+                raise ValueError("warmup needs example_co when with_critic=True")
+            for _ in range(n_warmup):
+                self.evaluate(example_co)
+        torch.cuda.synchronize()
+        return self
+
+    @torch.inference_mode()
+    def act(self, policy_obs):
+        """Actor forward -> action mean [B, num_actions] (fp32 holding the fp16 result)."""
+        return self._call("act", self._act_fn, policy_obs)
+
+    @torch.inference_mode()
+    def evaluate(self, critic_obs):
+        if not self.with_critic:
+            raise RuntimeError("evaluate needs InferenceRunner(with_critic=True)")
+        return self._call("val", self._val_fn, critic_obs)
+
+    @torch.inference_mode()
+    def act_sample(self, policy_obs):
+        mean = self.act(policy_obs)
+        std = self.model.std if hasattr(self.model, "std") else torch.exp(self.model.log_std)
+        return torch.normal(mean, std.to(mean.dtype).expand_as(mean))
+
+    # -- weight hand-over --------------------------------------------------------------------
+    def _requant_all(self):
+        qls = [m for m in self._quant_layers if isinstance(m, QuantLinear) and m.act_mode != "dynamic_full"]
+        if qls:
+            for i in range(0, len(qls), 16):
+                chunk = qls[i:i + 16]
+                arr = (N.GladQLinearSrc * len(chunk))(*[q.requant_src() for q in chunk])
+                N.check(N.load().glad_requant_qlinear(arr, len(chunk), N.stream_handle()), "requant")
+        for m in self._quant_layers:
+            if isinstance(m, QuantCNN):
+                m.requantize_()
+            elif not isinstance(m, QuantLinear):
+                m.requantize_()
+
+    def _graphed(self, attr, fn):
+        g = getattr(self, attr)
+        if g is None:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                fn()
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            setattr(self, attr, g)
+        g.replay()
+
+    @torch.inference_mode()
+    def refresh_quant(self, use_graph: bool = True):
+        """Requantise every quantised layer from its current weights."""
+        if not self._quant_layers:
+            return
+        if not use_graph:
+            self._requant_all()
+            return
+        self._graphed("_g_refresh", self._requant_all)
+
+    @torch.inference_mode()
+    def sync_weights_from(self, src_model, use_graph: bool = True):
+        """Cast-copy every same-named parameter/buffer of ``src_model`` (the fp32
+        master) into this copy, then requantise (qrt/runtime.py:224-271)."""
+        if self._sync_items is None:
+            for p in self.model.parameters():
+                p.requires_grad_(False)
+            dst = dict(self.model.named_parameters())
+            dst.update(dict(self.model.named_buffers()))
+            items, keep = [], []
+            for name, s in list(src_model.named_parameters()) + list(src_model.named_buffers()):
+                d = dst.get(name)
+                if d is None or d.shape != s.shape or not d.is_floating_point() or not s.is_floating_point():
+                    continue
+                if not (d.is_contiguous() and s.is_contiguous()):
+                    raise ValueError(f"{name}: sync needs contiguous tensors")
+                items.append(N.GladCastCopy(s.data_ptr(), d.data_ptr(), d.numel(), _dt(s), _dt(d)))
+                keep.append((s, d))
+            self._sync_items = (N.GladCastCopy * len(items))(*items)
+            self._sync_keep = keep
+
+        def _do():
+            if len(self._sync_items):
+                N.check(N.load().glad_cast_copy(self._sync_items, len(self._sync_items), N.stream_handle()),
+                        "sync cast-copy")
+            self._requant_all()
+
+        if not use_graph:
+            _do()
+            return
+        self._graphed("_g_sync", _do)
+
+    def __repr__(self):
+        return (f"InferenceRunner(mode={self.mode}, with_critic={self.with_critic}, "
+                f"fused={self._fused is not None}, quant_layers={len(self._quant_layers)})")

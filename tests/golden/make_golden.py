@@ -144,7 +144,7 @@ def main():
         w[k] = to_np(v)
     w["meta.s_cnn"] = np.float32(s_cnn)
     for p in INT8_PATHS:
-        w[f"plan.{p}.s_z"] = np.float32(plan[p]["s_z"])
+        w[f"plan.{p}.s_z"] = np.float64(plan[p]["s_z"])
     np.savez_compressed(os.path.join(HERE, "glad_weights.npz"), **w)
 
     # -- conv chain op fixture (config 2 semantics, reference kernels) -----
