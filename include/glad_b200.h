@@ -154,6 +154,23 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
  * call. n = 0 switches recording off. Not part of the reference interface.  */
 int glad_actor_stage_events(void* const* events, int n);
 
+/* Allocation-free variant of glad_actor_forward. No counterpart in the
+ * reference: it serves callers that cannot allocate device memory for this
+ * library -- a host runtime that owns all device memory through its own pool
+ * and forbids plugins to call cudaMalloc, or that cannot afford the
+ * synchronisation and fragmentation of allocating inside a rollout loop.
+ * The scratch is a static device array owned by the library, sized for at
+ * most GLAD_NOALLOC_MAX_B environments (about 11.2 MiB held on every GPU that
+ * loads the library until exit); larger B is rejected with
+ * GLAD_ERR_INVALID_ARG. The first call on a device resolves the array's
+ * address (make it before any stream capture). Calls share the array:
+ * calls that overlap on the GPU race, so serialise them on one stream.
+ * Arguments and results are those of glad_actor_forward.                    */
+#define GLAD_NOALLOC_MAX_B 2048
+int glad_actor_forward_noalloc(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                               int64_t ld_obs, int act_mode, const float* topk_noise,
+                               float* mean_out, const GladActorAux* aux, void* stream);
+
 /* Device-side status word of the last launches that used `workspace`
  * (0 = fine; bits = a bounded wait ran out). Synchronises `stream`.        */
 int glad_workspace_status(const void* workspace, uint32_t* status, void* stream);

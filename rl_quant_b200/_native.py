@@ -26,6 +26,7 @@ DTYPE_F16 = 1
 ACT_STATIC = 0
 ACT_DYNAMIC = 1
 ACT_MODES = {"static": ACT_STATIC, "dynamic": ACT_DYNAMIC}
+NOALLOC_MAX_B = 2048      # GLAD_NOALLOC_MAX_B
 
 
 class GladConvWeights(Structure):
@@ -81,6 +82,8 @@ SIGNATURES = {
     "glad_actor_workspace_size": (c_size_t, [c_int64]),
     "glad_actor_forward": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int, c_void_p,
                                    c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
+    "glad_actor_forward_noalloc": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int,
+                                           c_void_p, c_void_p, POINTER(GladActorAux), c_void_p]),
     "glad_actor_stage_events": (c_int, [POINTER(c_void_p), c_int]),
     "glad_workspace_status": (c_int, [c_void_p, POINTER(c_uint32), c_void_p]),
     "glad_requant_qlinear": (c_int, [POINTER(GladQLinearSrc), c_int, c_void_p]),

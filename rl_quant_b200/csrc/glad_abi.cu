@@ -169,6 +169,11 @@ ActorWs actor_ws(void* base, int64_t B) {
 
 }  // namespace
 
+namespace glad {
+// Error reporting for entry points defined in other translation units.
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace glad
+
 extern "C" {
 
 const char* glad_last_error(void) { return g_err; }
