@@ -300,11 +300,15 @@ int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int 
   }
   p.next_slot = -1;
   p.slots = slots;
-  const size_t smem128 = qgemm_smem_bytes(L->in_features, 128);
-  if (smem128 <= 220 * 1024)
-    GLAD_CHECK_CUDA(launch_qgemm<128>(p, st), "qlinear launch");
+  const int N = L->out_features;
+  cudaError_t le;
+  if (N >= 512 && qgemm_smem_bytes(L->in_features, 128) <= 200 * 1024)
+    le = launch_qgemm<128>(p, st);
+  else if (N >= 256 && qgemm_smem_bytes(L->in_features, 64) <= 200 * 1024)
+    le = launch_qgemm<64>(p, st);
   else
-    GLAD_CHECK_CUDA(launch_qgemm<32>(p, st), "qlinear launch");
+    le = launch_qgemm<32>(p, st);
+  GLAD_CHECK_CUDA(le, "qlinear launch");
   if (s_z_out) {
     const float* sz[6] = {L->s_z, L->s_z, L->s_z, L->s_z, L->s_z, L->s_z};
     const int let[6] = {L->alpha != nullptr, 0, 0, 0, 0, 0};
@@ -440,7 +444,10 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
       g.next_beta = w->mlp[i + 1].beta;
       g.next_let = w->mlp[i + 1].alpha != nullptr;
       g.next_slot = 3 + i;
-      GLAD_CHECK_CUDA(launch_qgemm<128>(g, st), "actor MLP launch");
+      // N tile chosen so each layer launches ~B/128 x 4 CTAs
+      cudaError_t le = mn[i] >= 512 ? launch_qgemm<128>(g, st)
+                       : mn[i] >= 256 ? launch_qgemm<64>(g, st) : launch_qgemm<32>(g, st);
+      GLAD_CHECK_CUDA(le, "actor MLP launch");
     } else {
       g.y32 = mean_out;
       g.ldy32 = kActions;

@@ -34,21 +34,33 @@ __device__ __forceinline__ float fp16r(float x) { return __half2float(__float2ha
 //  with LET: z = x*alpha + beta in fp32 (two roundings), q = rint(z/s) (dynamic)
 //            or rint(z*inv_sz) (static);
 //  without : z stays fp16 and the scaled value is rounded to fp16 before rint.
+//
+// rint(z/s) needs the correctly rounded quotient only near a rounding
+// boundary: t = z*RN(1/s) differs from RN(z/s) by at most ~1.8e-7*|z/s|, so
+// rint(t) == rint(RN(z/s)) unless t lies within that distance of a
+// half-integer; only then is the IEEE division evaluated.
 struct ActQuant {
   bool let;
   bool dyn;
   float s;      // dynamic scale (fp32 with LET; fp16-valued without)
+  float rcp;    // RN(1/s)
   float inv;    // static inv_sz (fp32 with LET; fp16-valued without)
   __device__ __forceinline__ int quant(float x, float alpha, float beta) const {
-    float v;
+    float r;
     if (let) {
-      float z = __fadd_rn(__fmul_rn(x, alpha), beta);
-      v = dyn ? __fdiv_rn(z, s) : __fmul_rn(z, inv);
+      const float z = __fadd_rn(__fmul_rn(x, alpha), beta);
+      if (dyn) {
+        const float t = __fmul_rn(z, rcp);
+        r = rintf(t);
+        if (0.5f - fabsf(t - r) <= fabsf(t) * 4.8e-7f) r = rintf(__fdiv_rn(z, s));
+      } else {
+        r = rintf(__fmul_rn(z, inv));
+      }
     } else {
-      v = fp16r(dyn ? __fdiv_rn(x, s) : __fmul_rn(x, inv));
+      r = rintf(fp16r(dyn ? __fdiv_rn(x, s) : __fmul_rn(x, inv)));
     }
-    int q = __float2int_rn(v);
-    return q < -128 ? -128 : (q > 127 ? 127 : q);
+    r = fminf(fmaxf(r, -128.0f), 127.0f);
+    return (int)r;
   }
   // |z| of one input element (what the dynamic absmax reduces).
   __device__ __forceinline__ float absz(float x, float alpha, float beta) const {
@@ -70,6 +82,7 @@ __device__ __forceinline__ ActQuant make_act_quant(const GladQLinear& L, int act
   a.let = L.alpha != nullptr;
   a.dyn = act_mode == GLAD_ACT_DYNAMIC;
   a.s = a.dyn ? dyn_scale(slots[slot], a.let) : 1.0f;
+  a.rcp = __fdiv_rn(1.0f, a.s);
   a.inv = a.let ? *L.inv_sz : fp16r(*L.inv_sz);
   return a;
 }

@@ -38,24 +38,31 @@ constexpr int kStripBytes = 4736;                      // >= (255 + 2*18 + 2 + 1
 constexpr int kW2sBytes = 5 * 2048;                    // 5 K-steps x (2 chunks x 64 n x 16 B)
 constexpr int kStageBytes = 8864;                      // (128 + 2079) * 4 rounded up + 16
 constexpr int kTmemCols = 128;
+constexpr int kFrontThreads = 256;
+#ifndef FRONT_MIN_BLOCKS
+#define FRONT_MIN_BLOCKS 2
+#endif
+constexpr int kMaxProp = 96;                           // proprio width of the fused front mode
 
 struct __align__(128) FrontSmem {
   uint8_t planes[kPlanesBytes];
   uint8_t w1s[kW1sBytes];
   uint8_t strip[kStripBytes];
   uint8_t w2s[kW2sBytes];
-  uint8_t stage[2][kStageBytes];
+  uint8_t stage[kStageBytes];
   float b1[16], qa[16], qc[16];
   float dq[64], b2[64], a2[64], c2[64];
   float wg[64], ws[64];                 // GPS weight, scorer weight (local half)
-  float red[8][64];                     // pooling partial sums
-  float wmax[4], wsum[4];
+  float2 lpart[2][2][128];              // [tile][channel half][row] partial (gps, scorer) logits
+  __half wt16[2][128];                  // softmax weights per row of each tile
+  float pool[2][4][64];                 // [tile][lane quarter][channel] pooled partial sums
+  float wmax[8], wsum[8];
   __half prop16[128];                   // proprio (fp16)
   __half pe16[64];
   __half gc16[64];
   alignas(16) int8_t q8[128];           // quantised proprio
-  alignas(16) int8_t pe_w8[64 * 128];   // actor_proprio_embedding int8 rows (K <= 128)
-  float pe_a[128], pe_b[128];           // its LET alpha / beta
+  alignas(16) int8_t pe_w8[64 * kMaxProp];  // actor_proprio_embedding int8 rows
+  float pe_a[kMaxProp], pe_b[kMaxProp]; // its LET alpha / beta
   float pe_scale[64], pe_bp[64];        // its output scale and bias
   float qp_a[128], qp_b[128];           // query_projector LET (absmax of its input)
   uint64_t mbar;
@@ -111,12 +118,85 @@ __device__ __forceinline__ float row_elem(const RowStage& r, int i) {
   return __half2float(*reinterpret_cast<const __half*>(p));
 }
 
+// conv2 epilogue with fused multiply-adds: ((acc*dq + b) relu) * a2 + c2.
+__device__ __forceinline__ float conv2_val(int32_t acc, float dq, float b, float a2, float c2) {
+  return fmaf(fmaxf(fmaf(i2f_small(acc), dq, b), 0.0f), a2, c2);
+}
+
+// 32 values -> one warp sum per lane: lane L ends with the sum of channel L.
+__device__ __forceinline__ float warp_reduce32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const bool up = lane & 16;
+    const float send = up ? v[i] : v[i + 16];
+    const float keep = up ? v[i + 16] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? v[i] : v[i + 8];
+    const float keep = up ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 4;
+    const float send = up ? v[i] : v[i + 4];
+    const float keep = up ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 2;
+    const float send = up ? v[i] : v[i + 2];
+    const float keep = up ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  const bool up = lane & 1;
+  const float send = up ? v[0] : v[1];
+  const float keep = up ? v[1] : v[0];
+  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+}
+
+// 16 values -> warp sums: lanes L and L^16 end with the sum of channel L & 15.
+__device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? v[i] : v[i + 8];
+    const float keep = up ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 4;
+    const float send = up ? v[i] : v[i + 4];
+    const float keep = up ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 2;
+    const float send = up ? v[i] : v[i + 2];
+    const float keep = up ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  const bool up = lane & 1;
+  const float send = up ? v[0] : v[1];
+  const float keep = up ? v[1] : v[0];
+  const float r = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+  return r + __shfl_xor_sync(0xffffffffu, r, 16);
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ FrontParams p) {
+__global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(const __grid_constant__ FrontParams p) {
   extern __shared__ uint8_t smem_raw[];
   FrontSmem& s = *reinterpret_cast<FrontSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;     // TMEM lane quarter, column half / tile
+  constexpr int NT = kFrontThreads;
   constexpr bool kConv1 = MODE != kModeConv2;
   constexpr bool kConv2 = MODE != kModeConv1;
   constexpr bool kFront = MODE == kModeFront;
@@ -130,13 +210,13 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
   }
   {
     uint4 z = make_uint4(0, 0, 0, 0);
-    for (int i = tid; i < kPlanesBytes / 16; i += 128) reinterpret_cast<uint4*>(s.planes)[i] = z;
-    for (int i = tid; i < kStripBytes / 16; i += 128) reinterpret_cast<uint4*>(s.strip)[i] = z;
+    for (int i = tid; i < kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(s.planes)[i] = z;
+    for (int i = tid; i < kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(s.strip)[i] = z;
   }
   if (kConv1) {
     const __half* w1p = reinterpret_cast<const __half*>(p.conv.w1p);
     __half* dst = reinterpret_cast<__half*>(s.w1s);
-    for (int idx = tid; idx < kW1sBytes / 2; idx += 128) {
+    for (int idx = tid; idx < kW1sBytes / 2; idx += NT) {
       const int pr = idx >> 8, c = (idx >> 7) & 1, n = (idx >> 3) & 15, e = idx & 7;
       const int q = 2 * pr + c;
       __half v = __float2half(0.0f);
@@ -153,7 +233,7 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
     }
   }
   if (kConv2) {
-    for (int idx = tid; idx < kW2sBytes; idx += 128) {
+    for (int idx = tid; idx < kW2sBytes; idx += NT) {
       const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
       const int q = 2 * pr + c;
       int8_t v = 0;
@@ -171,27 +251,19 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
       }
     }
   }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = s.tmem_base;
-  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-  uint32_t phase = 0;
-
   // Front-mode constants.
   ActQuant aq_pe{};
   ActQuant aq_qp{};
   float gb = 0.0f;
   float zmax_qp = 0.0f;
+  const int P = p.prop_dim;
   if (kFront) {
     aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
     aq_qp.let = p.qp.alpha != nullptr;
     gb = __half2float(p.gps_b[0]);
-    const int P = p.prop_dim;
-    for (int i = tid; i < kD * P / 4; i += 128)
+    for (int i = tid; i < kD * P / 4; i += NT)
       reinterpret_cast<int*>(s.pe_w8)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
-    for (int k = tid; k < P; k += 128) {
+    for (int k = tid; k < P; k += NT) {
       s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
       s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;
     }
@@ -199,36 +271,35 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
       s.pe_scale[tid] = out_scale(p.pe, aq_pe, tid);
       s.pe_bp[tid] = p.pe.b_prime[tid];
     }
-    s.qp_a[tid] = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
-    s.qp_b[tid] = aq_qp.let ? p.qp.beta[tid] : 0.0f;
-    __syncthreads();
+    if (tid < 128) {
+      s.qp_a[tid] = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
+      s.qp_b[tid] = aq_qp.let ? p.qp.beta[tid] : 0.0f;
+    }
   }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+  uint32_t phase = 0;
 
   const int esz = (MODE == kModeConv2) ? 1 : (p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2);
   const int row_elems = (MODE == kModeConv2) ? kTok * kC2 : p.prop_dim + kMap;
-  int buf = 0;
   int64_t env = blockIdx.x;
-  if (env < p.B) {
-    RowStage r0 = row_stage(p.in, env, p.ld, esz, row_elems, s.stage[0]);
-    row_issue(r0, tid, 128);
-  }
+  if (env < p.B) row_issue(row_stage(p.in, env, p.ld, esz, row_elems, s.stage), tid, NT);
   cp_async_commit();
 
   for (; env < p.B; env += gridDim.x) {
     cp_async_wait_all();
     __syncthreads();
-    const RowStage rs = row_stage(p.in, env, p.ld, esz, row_elems, s.stage[buf]);
+    const RowStage rs = row_stage(p.in, env, p.ld, esz, row_elems, s.stage);
     const int64_t nxt = env + gridDim.x;
-    if (nxt < p.B) {
-      RowStage rn = row_stage(p.in, nxt, p.ld, esz, row_elems, s.stage[buf ^ 1]);
-      row_issue(rn, tid, 128);
-    }
-    cp_async_commit();
 
     if (kConv1) {
       // ---- input -> conv1 planes (fp16) -------------------------------------------
       const int moff = p.prop_dim;
-      for (int px = tid; px < kH1 * kW1; px += 128) {
+      for (int px = tid; px < kH1 * kW1; px += NT) {
         const int ih = px / kW1, iw = px - ih * kW1;
         float v0, v1, v2;
         if (esz == 4) {
@@ -249,12 +320,15 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
         *reinterpret_cast<uint2*>(s.planes + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
       }
       if (kFront) {
-        for (int k = tid; k < p.prop_dim; k += 128)
+        for (int k = tid; k < P; k += NT)
           s.prop16[k] = __float2half_rn(esz == 4 ? row_elem<4>(rs, k) : row_elem<2>(rs, k));
       }
       fence_async_smem();
       tc_fence_before();
       __syncthreads();
+      // stage is free: prefetch the next environment while this one computes
+      if (nxt < p.B) row_issue(row_stage(p.in, nxt, p.ld, esz, row_elems, s.stage), tid, NT);
+      cp_async_commit();
 
       if (tid == 0) {
         tc_fence_after();
@@ -275,17 +349,18 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
 
       if (kFront) {
         // proprio embedding while the tensor core runs (qrt/qlinear.py:123-138)
-        const int P = p.prop_dim;
-        for (int k = tid; k < P; k += 128)
+        for (int k = tid; k < P; k += NT)
           s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[k]), s.pe_a[k], s.pe_b[k]);
         __syncthreads();
-        if (tid < kD) {
-          const int n = tid;
-          const int* wrow = reinterpret_cast<const int*>(s.pe_w8 + n * P);
-          const int* qw = reinterpret_cast<const int*>(s.q8);
+        if (tid < 2 * kD) {
+          // two threads per output row, each half of K
+          const int n = tid >> 1, part = tid & 1;
+          const int* wrow = reinterpret_cast<const int*>(s.pe_w8 + n * P) + part * (P / 8);
+          const int* qw = reinterpret_cast<const int*>(s.q8) + part * (P / 8);
           int acc = 0;
-          for (int k4 = 0; k4 < P / 4; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
-          s.pe16[n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
+          for (int k4 = 0; k4 < P / 8; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+          if (part == 0) s.pe16[n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
         }
       }
 
@@ -296,49 +371,53 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
       __syncthreads();
       if (s.abort_flag) break;
 
-      // ---- conv1 epilogue: TMEM -> int8 z8 -> strip / global --------------------------
+      // ---- conv1 epilogue: warp half = tile; TMEM -> int8 z8 -> strip / global -------
+      {
+        const int t = half;
+        const int m = t * 128 + 32 * quarter + lane;
+        if (t * 128 + 32 * quarter < 11 * 19) {            // warp has rows inside the grid
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_base + t * 16, r);
+          tmem_ld_wait();
+          const int oh = m / 19, ow = m - oh * 19;
+          if (oh < kH2 && ow < kW2) {
+            uint32_t pk[4];
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + t * 16, r);
-        tmem_ld_wait();
-        const int m = t * 128 + 32 * warp + lane;
-        const int oh = m / 19, ow = m - oh * 19;
-        if (oh < kH2 && ow < kW2) {
-          uint32_t pk[4];
+            for (int w4 = 0; w4 < 4; ++w4) {
+              uint32_t word = 0;
 #pragma unroll
-          for (int w4 = 0; w4 < 4; ++w4) {
-            uint32_t word = 0;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const int c = w4 * 4 + b;
-              const int q = conv1_quant(__uint_as_float(r[c]), s.b1[c], s.qa[c], s.qc[c]);
-              word |= ((uint32_t)(q & 0xFF)) << (8 * b);
+              for (int b = 0; b < 4; ++b) {
+                const int c = w4 * 4 + b;
+                const int q = conv1_quant(__uint_as_float(r[c]), s.b1[c], s.qa[c], s.qc[c]);
+                word |= ((uint32_t)(q & 0xFF)) << (8 * b);
+              }
+              pk[w4] = word;
             }
-            pk[w4] = word;
+            const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            if (kConv2)
+              *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
+            if (p.z8_out)
+              reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;
           }
-          const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          if (kConv2)
-            *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
-          if (p.z8_out)
-            reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;
         }
       }
       tc_fence_before();
+    } else {
+      // kModeConv2: z8 rows of this environment -> strip
+      for (int t = tid; t < kTok; t += NT) {
+        const int oh = t / kW2, ow = t - oh * kW2;
+        const uint32_t b = (uint32_t)t * 16;
+        const uint8_t* src = (b >= rs.body_lo && b + 16 <= rs.body_hi) ? rs.stage + (b - rs.body_lo)
+                                                                        : rs.src + b;
+        *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) =
+            *reinterpret_cast<const uint4*>(src);
+      }
+      __syncthreads();
+      if (nxt < p.B) row_issue(row_stage(p.in, nxt, p.ld, esz, row_elems, s.stage), tid, NT);
+      cp_async_commit();
     }
 
     if (kConv2) {
-      if (MODE == kModeConv2) {
-        // z8 rows of this environment -> strip
-        for (int t = tid; t < kTok; t += 128) {
-          const int oh = t / kW2, ow = t - oh * kW2;
-          const uint32_t b = (uint32_t)t * 16;
-          const uint8_t* src = (b >= rs.body_lo && b + 16 <= rs.body_hi) ? rs.stage + (b - rs.body_lo)
-                                                                          : rs.src + b;
-          *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) =
-              *reinterpret_cast<const uint4*>(src);
-        }
-      }
       fence_async_smem();
       __syncthreads();
       if (tid == 0) {
@@ -364,127 +443,142 @@ __global__ void __launch_bounds__(128, 4) front_kernel(const __grid_constant__ F
       __syncthreads();
       if (s.abort_flag) break;
 
-      // ---- conv2 epilogue, pass 1 -------------------------------------------------------
-      float my_logit[2];
-      uint32_t pend[16];
+      // ---- conv2 epilogue, pass 1: thread = (row, 32-channel half) -------------------
+      uint32_t loc[2][16];                 // fp16 local features, packed in pairs
+      const int c0 = 32 * half;
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        const int m = t * 128 + 32 * warp + lane;
+        const int i = 32 * quarter + lane;
+        const int m = t * 128 + i;
         const int oh = m / kStripCols, ow = m - oh * kStripCols;
         const bool valid = oh < kH2 && ow < kW2;
         const int tok = oh * kW2 + ow;
-        float l0 = 0.0f, l1 = 0.0f;
+        if (t * 128 + 32 * quarter < 11 * kStripCols) {   // warp has rows inside the grid
+          float l0 = 0.0f, l1 = 0.0f;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          uint32_t r[16], r_next[16];
-          if ((cb & 1) == 0) {
-            tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
-            tmem_ld16(tmem + lane_base + t * 64 + cb * 16 + 16, r_next);
+          for (int hb = 0; hb < 2; ++hb) {
+            uint32_t r[16];
+            tmem_ld16(tmem + lane_base + t * 64 + c0 + 16 * hb, r);
             tmem_ld_wait();
-            for (int j = 0; j < 16; ++j) pend[j] = r_next[j];
-          } else {
-            for (int j = 0; j < 16; ++j) r[j] = pend[j];
-          }
-          __half h[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int c = cb * 16 + j;
-            h[j] = conv2_out((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]);
-          }
-          if (kFront) {
+            for (int j = 0; j < 16; j += 2) {
+              const int c = c0 + 16 * hb + j;
+              const float y0 = conv2_val((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]);
+              const float y1 = conv2_val((int32_t)r[j + 1], s.dq[c + 1], s.b2[c + 1], s.a2[c + 1], s.c2[c + 1]);
+              __half2 hh = __floats2half2_rn(y0, y1);
+              loc[t][8 * hb + (j >> 1)] = *reinterpret_cast<uint32_t*>(&hh);
+              if (kFront) {
+                const float2 f = __half22float2(hh);
+                l0 = fmaf(f.x, s.wg[c], l0);
+                l0 = fmaf(f.y, s.wg[c + 1], l0);
+                l1 = fmaf(f.x, s.ws[c], l1);
+                l1 = fmaf(f.y, s.ws[c + 1], l1);
+              }
+            }
+            if (valid && p.acc_out) {
+              int4* dst = reinterpret_cast<int4*>(p.acc_out + (env * kTok + tok) * kD + c0 + 16 * hb);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float f = __half2float(h[j]);
-              l0 = fmaf(f, s.wg[cb * 16 + j], l0);
-              l1 = fmaf(f, s.ws[cb * 16 + j], l1);
+              for (int q4 = 0; q4 < 4; ++q4)
+                dst[q4] = make_int4((int)r[4 * q4], (int)r[4 * q4 + 1], (int)r[4 * q4 + 2], (int)r[4 * q4 + 3]);
             }
           }
+          if (kFront) s.lpart[t][half][i] = make_float2(l0, l1);
           if (valid && p.feat_out) {
-            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + tok) * kD + cb * 16);
-            dst[0] = *reinterpret_cast<uint4*>(&h[0]);
-            dst[1] = *reinterpret_cast<uint4*>(&h[8]);
-          }
-          if (valid && p.acc_out) {
-            int4* dst = reinterpret_cast<int4*>(p.acc_out + (env * kTok + tok) * kD + cb * 16);
+            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + tok) * kD + c0);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2], (int)r[4 * j + 3]);
+            for (int q4 = 0; q4 < 4; ++q4)
+              dst[q4] = make_uint4(loc[t][4 * q4], loc[t][4 * q4 + 1], loc[t][4 * q4 + 2], loc[t][4 * q4 + 3]);
           }
-        }
-        if (kFront) {
-          // logits2 = local @ [w_gps; w_s[:, :D]]^T, rounded to fp16 (qrt/encoder_opt.py:69-73)
-          const float g = fp16r(__fadd_rn(fp16r(l0), gb));
-          my_logit[t] = valid ? g : -INFINITY;
-          if (valid) p.score_local[env * kTok + tok] = __float2half_rn(l1);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) loc[t][j] = 0;
         }
       }
+      tc_fence_before();
 
       if (kFront) {
-        // ---- softmax over the 187 tokens (qrt/encoder_opt.py:75) ------------------------
-        float mx = warp_max(fmaxf(my_logit[0], my_logit[1]));
-        if (lane == 0) s.wmax[warp] = mx;
         __syncthreads();
-        mx = fmaxf(fmaxf(s.wmax[0], s.wmax[1]), fmaxf(s.wmax[2], s.wmax[3]));
-        float e[2];
-#pragma unroll
-        for (int t = 0; t < 2; ++t) e[t] = my_logit[t] == -INFINITY ? 0.0f : expf(my_logit[t] - mx);
-        float sm = warp_sum(e[0] + e[1]);
-        if (lane == 0) s.wsum[warp] = sm;
-        __syncthreads();
-        sm = (s.wsum[0] + s.wsum[1]) + (s.wsum[2] + s.wsum[3]);
-
-        // ---- pass 2: gc = sum_i w_i * local_i (qrt/encoder_opt.py:76-77) ---------------
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int m = t * 128 + 32 * warp + lane;
+        // ---- logits (fp16, qrt/encoder_opt.py:69-73) and softmax over 187 tokens --------
+        // warps 0-3: tile 0 rows, warps 4-7: tile 1 rows
+        float my_logit;
+        {
+          const int t = half, i = 32 * quarter + lane;
+          const int m = t * 128 + i;
           const int oh = m / kStripCols, ow = m - oh * kStripCols;
           const bool valid = oh < kH2 && ow < kW2;
-          const __half wh = __float2half_rn(__fdiv_rn(e[t], sm));
-          if (valid && p.gc_w_out) p.gc_w_out[env * kTok + oh * kW2 + ow] = wh;
-          const float wt = valid ? __half2float(wh) : 0.0f;
-          float v[64];
-#pragma unroll
-          for (int cb = 0; cb < 4; cb += 2) {
-            uint32_t r[16], r2[16];
-            tmem_ld16(tmem + lane_base + t * 64 + cb * 16, r);
-            tmem_ld16(tmem + lane_base + t * 64 + cb * 16 + 16, r2);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int c = cb * 16 + j;
-              v[c] = wt * __half2float(conv2_out((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]));
-              v[c + 16] = wt * __half2float(conv2_out((int32_t)r2[j], s.dq[c + 16], s.b2[c + 16],
-                                                      s.a2[c + 16], s.c2[c + 16]));
-            }
+          float g = -INFINITY;
+          if (valid) {
+            const float2 a = s.lpart[t][0][i], b = s.lpart[t][1][i];
+            g = fp16r(__fadd_rn(fp16r(a.x + b.x), gb));
+            p.score_local[env * kTok + oh * kW2 + ow] = __float2half_rn(a.y + b.y);
           }
-          warp_reduce64(v, lane);
-          const int c0 = reduce64_channel(lane);
-          s.red[t * 4 + warp][c0] = v[0];
-          s.red[t * 4 + warp][c0 + 1] = v[1];
+          my_logit = g;
         }
-        tc_fence_before();
+        float mx = warp_max(my_logit);
+        if (lane == 0) s.wmax[warp] = mx;
+        __syncthreads();
+        mx = s.wmax[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s.wmax[w]);
+        const float e = my_logit == -INFINITY ? 0.0f : expf(my_logit - mx);
+        float sm = warp_sum(e);
+        if (lane == 0) s.wsum[warp] = sm;
+        __syncthreads();
+        sm = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sm += s.wsum[w];
+        {
+          const int t = half, i = 32 * quarter + lane;
+          const int m = t * 128 + i;
+          const int oh = m / kStripCols, ow = m - oh * kStripCols;
+          const bool valid = oh < kH2 && ow < kW2;
+          const __half wh = __float2half_rn(__fdiv_rn(e, sm));
+          s.wt16[t][i] = valid ? wh : __float2half(0.0f);
+          if (valid && p.gc_w_out) p.gc_w_out[env * kTok + oh * kW2 + ow] = wh;
+        }
+        __syncthreads();
+        // ---- pass 2: gc = sum_i w_i * local_i over this thread's 32 channels ------------
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (t * 128 + 32 * quarter < 11 * kStripCols) {
+            const float wt = __half2float(s.wt16[t][32 * quarter + lane]);
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb) {
+              float v[16];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&loc[t][8 * hb + j]));
+                v[2 * j] = wt * f.x;
+                v[2 * j + 1] = wt * f.y;
+              }
+              const float r = warp_reduce16(v, lane);     // lanes L and L^16 hold channel L&15
+              if (lane < 16) s.pool[t][quarter][c0 + 16 * hb + lane] = r;
+            }
+          } else {
+            s.pool[t][quarter][c0 + lane] = 0.0f;
+          }
+        }
         __syncthreads();
         if (tid < kD) {
           float g = 0.0f;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) g += s.red[j][tid];
+          for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) g += s.pool[t][q][tid];
           const __half gh = __float2half_rn(g);
           s.gc16[tid] = gh;
           p.enc[env * kEnc + 64 + tid] = gh;
           p.pe_out[env * kD + tid] = s.pe16[tid];
         }
-        for (int k = tid; k < p.prop_dim; k += 128) p.enc[env * kEnc + 128 + k] = s.prop16[k];
+        for (int k = tid; k < P; k += NT) p.enc[env * kEnc + 128 + k] = s.prop16[k];
         __syncthreads();
         if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
           // |alpha*cat(gc, pe) + beta| for the query projector's dynamic s_z
           const float x = __half2float(tid < kD ? s.gc16[tid] : s.pe16[tid - kD]);
           zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, s.qp_a[tid], s.qp_b[tid]));
         }
-      } else {
-        tc_fence_before();
       }
     }
-    buf ^= 1;
   }
 
   // ---- teardown --------------------------------------------------------------------------
@@ -515,7 +609,7 @@ cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st) {
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)front_kernel<MODE>, done);
   if (e != cudaSuccess) return e;
-  front_kernel<MODE><<<grid, 128, smem, st>>>(p);
+  front_kernel<MODE><<<grid, kFrontThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 

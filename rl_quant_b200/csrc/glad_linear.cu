@@ -11,12 +11,16 @@
 namespace glad {
 
 // ---- tcgen05 int8 GEMM --------------------------------------------------------------
-// CTA = 128 rows x NT columns; A (activations) is quantised on the way into
-// shared memory, B is the layer's int8 weight rows. Both K-major, no swizzle:
-//   A: [K/16 chunks][128 rows][16 B]   (LBO = 2048, SBO = 128)
-//   B: [K/16 chunks][NT rows][16 B]    (LBO = NT*16, SBO = 128)
+// CTA = 128 rows x NT columns, 256 threads. A (activations) is quantised on
+// the way into shared memory, B is the layer's int8 weight rows. Both
+// K-major, no swizzle:
+//   A: [Kp/16 chunks][128 rows][16 B]   (LBO = 2048, SBO = 128)
+//   B: [Kp/16 chunks][NT rows][16 B]    (LBO = NT*16, SBO = 128)
+// Epilogue: warp w reads TMEM lane quarter (w & 3) and column half (w >> 2).
+constexpr int kGemmThreads = 256;
+
 template <int NT>
-__global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -28,7 +32,9 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
   float* cbias = cscale + NT;
   float* calpha = cbias + NT;
   float* cbeta = calpha + NT;
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(cbeta + NT);
+  float* kalpha = cbeta + NT;            // [Kp] this layer's LET
+  float* kbeta = kalpha + Kp;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(kbeta + Kp);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -45,11 +51,10 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
     fence_mbar_init();
     *abort_flag = 0;
   }
-  const ActQuant aq = make_act_quant(p.L, p.act_mode, p.slots, p.slot);
-  // weights: rows n0..n0+NT of w8 (zero past Np)
+  // weights: rows n0..n0+NT of w8 (zero past Np / K)
   const int kc16 = Kp / 16;
   const bool rows16 = (K & 15) == 0;
-  for (int idx = tid; idx < NT * kc16; idx += 128) {
+  for (int idx = tid; idx < NT * kc16; idx += kGemmThreads) {
     const int c = idx / NT, n = idx - c * NT;
     uint8_t* dst = Bs + c * (NT * 16) + n * 16;
     const int8_t* src = p.L.w8 + (int64_t)(n0 + n) * K + c * 16;
@@ -63,7 +68,8 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
     }
   }
   cp_async_commit();
-  for (int j = tid; j < NT; j += 128) {
+  const ActQuant aq = make_act_quant(p.L, p.act_mode, p.slots, p.slot);
+  for (int j = tid; j < NT; j += kGemmThreads) {
     const int n = n0 + j;
     const bool in = n < N;
     cscale[j] = in ? out_scale(p.L, aq, n) : 0.0f;
@@ -71,10 +77,15 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
     calpha[j] = (in && p.next_let) ? p.next_alpha[n] : 0.0f;
     cbeta[j] = (in && p.next_let) ? p.next_beta[n] : 0.0f;
   }
+  for (int k = tid; k < Kp; k += kGemmThreads) {
+    kalpha[k] = (aq.let && k < K) ? p.L.alpha[k] : 0.0f;
+    kbeta[k] = (aq.let && k < K) ? p.L.beta[k] : 0.0f;
+  }
+  __syncthreads();
   // activations: quantise 8 elements at a time
   const int k8n = Kp / 8, k8real = K / 8;
   const bool f32in = p.x_dtype == GLAD_DTYPE_F32;
-  for (int idx = tid; idx < 128 * k8n; idx += 128) {
+  for (int idx = tid; idx < 128 * k8n; idx += kGemmThreads) {
     const int r = idx / k8n, k8 = idx - r * k8n;
     const int64_t m = m0 + r;
     uint2 out = make_uint2(0, 0);
@@ -100,9 +111,7 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int k = k8 * 8 + e;
-        const float a = aq.let ? __ldg(p.L.alpha + k) : 0.0f;
-        const float b = aq.let ? __ldg(p.L.beta + k) : 0.0f;
-        w[e >> 2] |= (uint32_t)(aq.quant(x[e], a, b) & 0xFF) << (8 * (e & 3));
+        w[e >> 2] |= (uint32_t)(aq.quant(x[e], kalpha[k], kbeta[k]) & 0xFF) << (8 * (e & 3));
       }
       out = make_uint2(w[0], w[1]);
     }
@@ -132,35 +141,49 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
 
   float zmax = 0.0f;
   if (!*abort_flag) {
-    const int64_t m = m0 + 32 * warp + lane;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int64_t m = m0 + 32 * quarter + lane;
     const bool row_ok = m < p.M;
     ActQuant nq{};
     nq.let = p.next_let != 0;
+    static_assert(NT % 32 == 0, "N tile must be a multiple of 32");
+    constexpr int kHalfCols = NT / 2;
+    constexpr int kChunks = kHalfCols / 16;
 #pragma unroll 1
-    for (int cb = 0; cb < NT / 16; ++cb) {
+    for (int cb = 0; cb < kChunks; ++cb) {
+      const int col0 = half * kHalfCols + cb * 16;     // first column of this chunk (tile-local)
       uint32_t rr[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + cb * 16, rr);
+      tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + col0, rr);
       tmem_ld_wait();
-      __half h[16];
+      __align__(16) __half h[16];
       float f[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int jj = cb * 16 + j;
+        const int jj = col0 + j;
         f[j] = qlinear_out32((int32_t)rr[j], cscale[jj], cbias[jj]);
         h[j] = __float2half_rn(f[j]);
         if (p.elu) h[j] = elu16(h[j]);
+        if (p.next_slot >= 0 && n0 + jj < N)
+          zmax = fmaxf(zmax, nq.absz(__half2float(h[j]), calpha[jj], cbeta[jj]));
       }
       if (row_ok) {
-        const int nb = n0 + cb * 16;
+        const int nb = n0 + col0;
+        if (p.y) {
+          __half* dst = p.y + m * p.ldy + nb;
+          if (nb + 16 <= N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+            reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<const uint4*>(h)[0];
+            reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<const uint4*>(h)[1];
+          } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = nb + j;
-          if (n < N) {
-            if (p.y) p.y[m * p.ldy + n] = h[j];
-            if (p.y32) p.y32[m * p.ldy32 + n] = p.y32_round16 ? __half2float(h[j]) : f[j];
-            if (p.next_slot >= 0)
-              zmax = fmaxf(zmax, nq.absz(__half2float(h[j]), calpha[cb * 16 + j], cbeta[cb * 16 + j]));
+            for (int j = 0; j < 16; ++j)
+              if (nb + j < N) dst[j] = h[j];
           }
+        }
+        if (p.y32) {
+          float* dst = p.y32 + m * p.ldy32 + nb;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (nb + j < N) dst[j] = p.y32_round16 ? __half2float(h[j]) : f[j];
         }
       }
     }
@@ -184,7 +207,7 @@ __global__ void __launch_bounds__(128, 1) qgemm_kernel(const __grid_constant__ G
 
 size_t qgemm_smem_bytes(int K, int NT) {
   const size_t Kp = (size_t)((K + 31) & ~31);
-  return Kp * 128 + Kp * NT + 4 * NT * sizeof(float) + 64 + 128;
+  return Kp * 128 + Kp * NT + 4 * NT * sizeof(float) + 2 * Kp * sizeof(float) + 64 + 128;
 }
 
 template <int NT>
@@ -195,7 +218,7 @@ cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int Np = (p.L.out_features + 7) & ~7;
   dim3 grid((unsigned)((p.M + 127) / 128), (unsigned)((Np + NT - 1) / NT));
-  qgemm_kernel<NT><<<grid, 128, smem, st>>>(p);
+  qgemm_kernel<NT><<<grid, kGemmThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 template cudaError_t launch_qgemm<128>(const GemmParams&, cudaStream_t);

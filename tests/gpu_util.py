@@ -9,6 +9,18 @@ from rl_quant_b200 import _native as N
 QL_NAMES = ("actor_proprio_embedding", "query_projector", "actor.0", "actor.2", "actor.4", "actor.6")
 
 
+def fp16_ulp_close(a, b, max_ulp=1, min_exact=0.999):
+    """fp16 arrays equal except for rare one-ulp differences (the conv2
+    epilogue runs with fused multiply-adds; qrt's eager order rounds twice)."""
+    a = np.asarray(a, np.float16).astype(np.float32)
+    b = np.asarray(b, np.float16).astype(np.float32)
+    ulp = np.maximum(np.spacing(np.maximum(np.abs(a), np.abs(b)).astype(np.float16)).astype(np.float32),
+                     np.float32(2.0 ** -24))
+    d = np.abs(a - b) / ulp
+    assert d.max() <= max_ulp + 1e-6, float(d.max())
+    assert (d == 0).mean() >= min_exact, float((d == 0).mean())
+
+
 class DeviceWeights:
     """Every tensor of the golden state dict on the GPU (kept alive here)."""
 

@@ -12,7 +12,7 @@ import torch
 from oracle import glad_oracle as O
 from rl_quant_b200.synthetic import glad_obs
 
-from gpu_util import DeviceWeights, actor_forward
+from gpu_util import DeviceWeights, actor_forward, fp16_ulp_close
 
 pytestmark = pytest.mark.gpu
 
@@ -60,11 +60,11 @@ def test_actor_vs_oracle_with_aux(dw, Wt, golden_weights, mode, B, dtype):
     z8 = aux["z8"].cpu().numpy()
     dz = np.abs(z8.astype(np.int16) - oaux["z8"].astype(np.int16))
     assert dz.max() <= 1 and (dz > 0).mean() < 1e-3
-    # local features: bit-exact given the kernel's own z8
+    # local features given the kernel's own z8: integer part exact, epilogue within one fp16 ulp
     w = golden_weights
     loc = O.conv2_int8_fused(z8, w["map_cnn.w8"], w["map_cnn.dq"], w["map_cnn.b2f"], w["map_cnn.a2"],
                              w["map_cnn.c2"]).reshape(B, 187, 64)
-    assert np.array_equal(aux["local"].cpu().numpy(), loc)
+    fp16_ulp_close(aux["local"].cpu().numpy(), loc)
     # top-32: exact on the logits the kernel selected from
     lg = aux["topk_logits"].cpu().numpy()
     idx = aux["topk_idx"].cpu().numpy()

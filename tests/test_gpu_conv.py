@@ -7,7 +7,7 @@ from oracle import glad_oracle as O
 from rl_quant_b200 import _native as N
 from rl_quant_b200.synthetic import glad_obs
 
-from gpu_util import DeviceWeights
+from gpu_util import DeviceWeights, fp16_ulp_close
 
 pytestmark = pytest.mark.gpu
 
@@ -47,7 +47,7 @@ def test_conv2_int32_accumulators_bit_exact(dw, golden_weights, B):
     ref_acc = O.conv2_acc(z8, w["map_cnn.w8"])
     assert np.array_equal(acc.cpu().numpy(), ref_acc)
     ref_feat = O.conv2_epilogue(ref_acc, w["map_cnn.dq"], w["map_cnn.b2f"], w["map_cnn.a2"], w["map_cnn.c2"])
-    assert np.array_equal(feat.cpu().numpy(), ref_feat)
+    fp16_ulp_close(feat.cpu().numpy(), ref_feat)
 
 
 def test_conv1_matches_reference_kernel(dw, golden_conv):
@@ -85,7 +85,7 @@ def test_conv_chain_equals_two_ops(dw, golden_weights, B):
     w = golden_weights
     ref = O.conv2_int8_fused(z8.cpu().numpy(), w["map_cnn.w8"], w["map_cnn.dq"], w["map_cnn.b2f"],
                              w["map_cnn.a2"], w["map_cnn.c2"])
-    assert np.array_equal(feat.cpu().numpy(), ref)
+    fp16_ulp_close(feat.cpu().numpy(), ref)
 
 
 def test_conv_rejects_bad_arguments(dw):
