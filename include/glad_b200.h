@@ -90,6 +90,37 @@ typedef struct GladActorWeights {
   GladQLinear mlp[4];            /* actor.0 224->512, .2 ->256, .4 ->128, .6 ->29 */
 } GladActorWeights;
 
+/* Plain fp16 Linear (weight [out,in] f16 row-major, bias [out] f16 or NULL). */
+typedef struct GladLinear16 {
+  const void* weight;
+  const void* bias;
+  int32_t in_features;
+  int32_t out_features;
+} GladLinear16;
+
+/* The critic forward's tensors (qrt/integration.py:133-135): the shared
+ * encoder (QuantCNN, INT8 query_projector, fp16 GPS/scorer/MHA), the critic
+ * proprio embedding and the fp16 critic MLP (not quantised,
+ * qrt/integration.py:42-43). When the critic observation has the actor's
+ * proprio width the reference encodes it with actor_proprio_embedding
+ * (rsl_rl actor_critic_encoder.py:226-229): then set proprio_emb_q and leave
+ * proprio_emb.weight NULL.                                                    */
+typedef struct GladCriticWeights {
+  GladConvWeights conv;
+  GladLinear16 proprio_emb;      /* critic_proprio_embedding, P -> 64 (fp16)    */
+  GladQLinear proprio_emb_q;     /* used when proprio_emb.weight is NULL       */
+  GladQLinear query_proj;
+  const void* gps_w;
+  const void* gps_b;
+  const void* scorer_w;
+  const void* scorer_b;
+  const void* mha_in_w;
+  const void* mha_in_b;
+  const void* mha_out_w;
+  const void* mha_out_b;
+  GladLinear16 mlp[4];           /* critic.0 (128+P)->512, .2 ->256, .4 ->128, .6 ->1 */
+} GladCriticWeights;
+
 /* Optional per-call outputs of the fused forward (any field may be NULL). */
 typedef struct GladActorAux {
   int8_t* z8;            /* [B*187,16] i8   conv1 output (QuantCNN z8)          */
@@ -146,6 +177,17 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
                        int64_t ld_obs, int act_mode, const float* topk_noise, float* mean_out,
                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/* The compiled critic function of qrt full mode (qrt/integration.py:133-135):
+ * the same encoder over the critic observation group, then the fp16 critic
+ * MLP. obs [B, P+2079] (P <= 104), value_out f32 [B,1] (the fp16 output
+ * widened, as `.float()` at qrt/integration.py:214). topk_noise and aux as
+ * for the actor (encoded has row stride 232 when set).                        */
+size_t glad_critic_workspace_size(int64_t B);
+int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
+                        int64_t ld_obs, int act_mode, const float* topk_noise, float* value_out,
+                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
+                        void* stream);
 
 /* Diagnostics: record CUDA events (cudaEvent_t, passed as void*) between the
  * stages of the following glad_actor_forward calls on this host thread:

@@ -44,6 +44,17 @@ class GladActorWeights(Structure):
                                 "mha_out_w", "mha_out_b")] + [("mlp", GladQLinear * 4)]
 
 
+class GladLinear16(Structure):
+    _fields_ = [("weight", c_void_p), ("bias", c_void_p), ("in_features", c_int32), ("out_features", c_int32)]
+
+
+class GladCriticWeights(Structure):
+    _fields_ = [("conv", GladConvWeights), ("proprio_emb", GladLinear16), ("proprio_emb_q", GladQLinear),
+                ("query_proj", GladQLinear)] + [
+        (n, c_void_p) for n in ("gps_w", "gps_b", "scorer_w", "scorer_b", "mha_in_w", "mha_in_b",
+                                "mha_out_w", "mha_out_b")] + [("mlp", GladLinear16 * 4)]
+
+
 class GladActorAux(Structure):
     _fields_ = [(n, c_void_p) for n in ("z8", "local", "gc_weights", "score_local", "topk_logits",
                                         "topk_idx", "attn_weights", "encoded", "act_scales")]
@@ -82,6 +93,9 @@ SIGNATURES = {
     "glad_actor_workspace_size": (c_size_t, [c_int64]),
     "glad_actor_forward": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int, c_void_p,
                                    c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
+    "glad_critic_workspace_size": (c_size_t, [c_int64]),
+    "glad_critic_forward": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
+                                    c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
     "glad_actor_forward_noalloc": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                            c_void_p, c_void_p, POINTER(GladActorAux), c_void_p]),
     "glad_actor_stage_events": (c_int, [POINTER(c_void_p), c_int]),

@@ -18,6 +18,9 @@ size_t tail_smem_bytes();
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st);
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st);
+template <int NT>
+cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st);
+size_t hgemm_smem_bytes(int K, int NT);
 size_t qgemm_smem_bytes(int K, int NT);
 cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
                           const float* alpha, const float* beta, int round16, float* slot,
@@ -146,7 +149,7 @@ struct ActorWs {
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
-ActorWs actor_ws(void* base, int64_t B) {
+ActorWs actor_ws(void* base, int64_t B, int enc_width = kEnc) {
   ActorWs w;
   uint8_t* p = reinterpret_cast<uint8_t*>(base);
   size_t off = 0;
@@ -159,7 +162,7 @@ ActorWs actor_ws(void* base, int64_t B) {
   w.z8 = reinterpret_cast<int8_t*>(take((size_t)B * kTok * 16));
   w.score_local = reinterpret_cast<__half*>(take((size_t)B * kTok * 2));
   w.pe = reinterpret_cast<__half*>(take((size_t)B * kD * 2));
-  w.enc = reinterpret_cast<__half*>(take((size_t)B * kEnc * 2));
+  w.enc = reinterpret_cast<__half*>(take((size_t)B * enc_width * 2));
   w.h1 = reinterpret_cast<__half*>(take((size_t)B * 512 * 2));
   w.h2 = reinterpret_cast<__half*>(take((size_t)B * 256 * 2));
   w.h3 = reinterpret_cast<__half*>(take((size_t)B * 128 * 2));
@@ -199,7 +202,7 @@ int glad_conv1_fused_q(const void* x_nhwc, int64_t B, const GladConvWeights* w, 
   p.B = B;
   p.conv = *w;
   p.z8_out = z8_out;
-  GLAD_CHECK_CUDA(launch_front<kModeConv1>(p, front_grid(B, d, 4), (cudaStream_t)stream),
+  GLAD_CHECK_CUDA(launch_front<kModeConv1>(p, front_grid(B, d, 2), (cudaStream_t)stream),
                   "conv1 launch");
   return GLAD_OK;
 }
@@ -224,7 +227,7 @@ int glad_conv2_int8_fused(const int8_t* z8, int64_t B, const GladConvWeights* w,
   p.conv = *w;
   p.feat_out = reinterpret_cast<__half*>(feat_out);
   p.acc_out = acc_out;
-  GLAD_CHECK_CUDA(launch_front<kModeConv2>(p, front_grid(B, d, 4), (cudaStream_t)stream),
+  GLAD_CHECK_CUDA(launch_front<kModeConv2>(p, front_grid(B, d, 2), (cudaStream_t)stream),
                   "conv2 launch");
   return GLAD_OK;
 }
@@ -249,7 +252,7 @@ int glad_conv_chain(const void* x_nhwc, int64_t B, const GladConvWeights* w, voi
   p.conv = *w;
   p.feat_out = reinterpret_cast<__half*>(feat_out);
   p.z8_out = z8_out;
-  GLAD_CHECK_CUDA(launch_front<kModeChain>(p, front_grid(B, d, 4), (cudaStream_t)stream),
+  GLAD_CHECK_CUDA(launch_front<kModeChain>(p, front_grid(B, d, 2), (cudaStream_t)stream),
                   "conv chain launch");
   return GLAD_OK;
 }
@@ -388,6 +391,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.pe = w->proprio_emb;
   fp.qp = w->query_proj;
   fp.act_mode = act_mode;
+  fp.ld_enc = kEnc;
   fp.z8_out = z8;
   fp.feat_out = reinterpret_cast<__half*>(ax.local);
   fp.score_local = score_local;
@@ -395,7 +399,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.enc = enc;
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
-  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 4), st), "front launch");
+  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st), "front launch");
   stage_mark(2, st);
 
   TailParams tp{};
@@ -410,7 +414,10 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.out_b = reinterpret_cast<const __half*>(w->mha_out_b);
   tp.a0_alpha = w->mlp[0].alpha;
   tp.a0_beta = w->mlp[0].beta;
+  tp.a0_absmax = 1;
   tp.act_mode = act_mode;
+  tp.ld_enc = kEnc;
+  tp.prop_dim = P;
   tp.noise = topk_noise;
   tp.z8 = z8;
   tp.score_local = score_local;
@@ -465,6 +472,153 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
                         w->mlp[2].alpha != nullptr, w->mlp[3].alpha != nullptr};
     GLAD_CHECK_CUDA(launch_act_scales(ws.slots, act_mode, sz, let, ax.act_scales, st),
                     "scale launch");
+  }
+  return GLAD_OK;
+}
+
+constexpr int kCriticEnc = 232;   // encoded row stride of the critic (128 + P <= 232)
+
+size_t glad_critic_workspace_size(int64_t B) {
+  return actor_ws(nullptr, B < 0 ? 0 : B, kCriticEnc).bytes;
+}
+
+int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
+                        int64_t ld_obs, int act_mode, const float* topk_noise, float* value_out,
+                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  g_err[0] = 0;
+  if (!w) return fail(GLAD_ERR_INVALID_ARG, "weights are NULL");
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown act_mode %d", act_mode);
+  if (obs_dtype != GLAD_DTYPE_F16 && obs_dtype != GLAD_DTYPE_F32)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown obs dtype %d", obs_dtype);
+  const bool pe16 = w->proprio_emb.weight != nullptr;
+  int rc;
+  int P;
+  if (pe16) {
+    P = w->proprio_emb.in_features;
+    if (w->proprio_emb.out_features != kD)
+      return fail(GLAD_ERR_INVALID_ARG, "critic_proprio_embedding must have 64 outputs");
+  } else {
+    if ((rc = check_ql(&w->proprio_emb_q, "proprio embedding", 0, kD, false))) return rc;
+    P = w->proprio_emb_q.in_features;
+  }
+  if (P <= 0 || P > 104) return fail(GLAD_ERR_INVALID_ARG, "critic proprio width %d outside [1, 104]", P);
+  if (ld_obs < P + kMap) return fail(GLAD_ERR_INVALID_ARG, "ld_obs %lld < %d", (long long)ld_obs, P + kMap);
+  if (B == 0) return GLAD_OK;
+  if (!obs || !value_out) return fail(GLAD_ERR_INVALID_ARG, "obs and value_out must be set");
+  if (!aligned(obs, obs_dtype == GLAD_DTYPE_F32 ? 4 : 2))
+    return fail(GLAD_ERR_INVALID_ARG, "obs is not element-aligned");
+  if ((rc = check_conv(&w->conv, true, true))) return rc;
+  if ((rc = check_ql(&w->query_proj, "query_projector", 128, 64))) return rc;
+  const int hk[4] = {128 + P, 512, 256, 128}, hn[4] = {512, 256, 128, 1};
+  for (int i = 0; i < 4; ++i) {
+    const GladLinear16& L = w->mlp[i];
+    if (!L.weight || L.in_features != hk[i] || L.out_features != hn[i])
+      return fail(GLAD_ERR_INVALID_ARG, "critic MLP layer %d must be %d -> %d", i, hk[i], hn[i]);
+  }
+  if (!w->gps_w || !w->gps_b || !w->scorer_w || !w->scorer_b || !w->mha_in_w || !w->mha_in_b ||
+      !w->mha_out_w || !w->mha_out_b)
+    return fail(GLAD_ERR_INVALID_ARG, "fp16 encoder weights must be set");
+  const ActorWs ws = actor_ws(workspace, B, kCriticEnc);
+  if (!workspace || workspace_bytes < ws.bytes)
+    return fail(GLAD_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", ws.bytes, workspace_bytes);
+  if (!aligned(workspace, 256)) return fail(GLAD_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const GladActorAux none{};
+  const GladActorAux& ax = aux ? *aux : none;
+  int8_t* z8 = ax.z8 ? ax.z8 : ws.z8;
+  __half* score_local = ax.score_local ? reinterpret_cast<__half*>(ax.score_local) : ws.score_local;
+  __half* enc = ax.encoded ? reinterpret_cast<__half*>(ax.encoded) : ws.enc;
+  if (!aligned(z8, 16) || !aligned(enc, 16))
+    return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded must be 16-byte aligned");
+
+  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
+  if (!pe16 && act_mode == GLAD_ACT_DYNAMIC)
+    GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb_q.alpha,
+                                  w->proprio_emb_q.beta, 1, &ws.slots[0], d.sms, st),
+                    "absmax launch");
+  FrontParams fp{};
+  fp.in = obs;
+  fp.ld = ld_obs;
+  fp.in_dtype = obs_dtype;
+  fp.prop_dim = P;
+  fp.B = B;
+  fp.conv = w->conv;
+  fp.gps_w = reinterpret_cast<const __half*>(w->gps_w);
+  fp.gps_b = reinterpret_cast<const __half*>(w->gps_b);
+  fp.scorer_w = reinterpret_cast<const __half*>(w->scorer_w);
+  fp.pe_f16 = pe16 ? 1 : 0;
+  fp.pe = w->proprio_emb_q;
+  fp.pe16_w = reinterpret_cast<const __half*>(w->proprio_emb.weight);
+  fp.pe16_b = reinterpret_cast<const __half*>(w->proprio_emb.bias);
+  fp.qp = w->query_proj;
+  fp.act_mode = act_mode;
+  fp.ld_enc = kCriticEnc;
+  fp.z8_out = z8;
+  fp.feat_out = reinterpret_cast<__half*>(ax.local);
+  fp.score_local = score_local;
+  fp.gc_w_out = reinterpret_cast<__half*>(ax.gc_weights);
+  fp.enc = enc;
+  fp.pe_out = ws.pe;
+  fp.slots = ws.slots;
+  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st), "front launch");
+
+  TailParams tp{};
+  tp.B = B;
+  tp.conv = w->conv;
+  tp.qp = w->query_proj;
+  tp.scorer_w = reinterpret_cast<const __half*>(w->scorer_w);
+  tp.scorer_b = reinterpret_cast<const __half*>(w->scorer_b);
+  tp.in_w = reinterpret_cast<const __half*>(w->mha_in_w);
+  tp.in_b = reinterpret_cast<const __half*>(w->mha_in_b);
+  tp.out_w = reinterpret_cast<const __half*>(w->mha_out_w);
+  tp.out_b = reinterpret_cast<const __half*>(w->mha_out_b);
+  tp.a0_absmax = 0;                 // the critic MLP is fp16: no scale to reduce
+  tp.noise = topk_noise;
+  tp.act_mode = act_mode;
+  tp.ld_enc = kCriticEnc;
+  tp.prop_dim = P;
+  tp.z8 = z8;
+  tp.score_local = score_local;
+  tp.pe = ws.pe;
+  tp.enc = enc;
+  tp.topk_logits_out = reinterpret_cast<__half*>(ax.topk_logits);
+  tp.topk_idx_out = ax.topk_idx;
+  tp.attn_w_out = reinterpret_cast<__half*>(ax.attn_weights);
+  tp.slots = ws.slots;
+  const int64_t groups = (B + 3) / 4;
+  const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
+  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st), "tail launch");
+
+  const __half* xs[4] = {enc, ws.h1, ws.h2, ws.h3};
+  const int64_t lds[4] = {kCriticEnc, 512, 256, 128};
+  __half* ys[3] = {ws.h1, ws.h2, ws.h3};
+  for (int i = 0; i < 4; ++i) {
+    HGemmParams g{};
+    g.w = reinterpret_cast<const __half*>(w->mlp[i].weight);
+    g.b = reinterpret_cast<const __half*>(w->mlp[i].bias);
+    g.K = hk[i];
+    g.N = hn[i];
+    g.x = xs[i];
+    g.M = B;
+    g.ldx = lds[i];
+    cudaError_t le;
+    if (i < 3) {
+      g.y = ys[i];
+      g.ldy = hn[i];
+      g.elu = 1;
+      le = hn[i] >= 512 ? launch_hgemm<128>(g, st) : hn[i] >= 256 ? launch_hgemm<64>(g, st)
+                                                                   : launch_hgemm<32>(g, st);
+    } else {
+      g.y32 = value_out;
+      g.ldy32 = 1;
+      le = launch_hgemm<32>(g, st);
+    }
+    GLAD_CHECK_CUDA(le, "critic MLP launch");
   }
   return GLAD_OK;
 }

@@ -183,16 +183,20 @@ struct FrontParams {
   const __half* gps_w;
   const __half* gps_b;
   const __half* scorer_w;
-  GladQLinear pe;
+  GladQLinear pe;          // int8 proprio embedding (pe_f16 == 0)
+  const __half* pe16_w;    // fp16 proprio embedding [64, prop_dim] (pe_f16 != 0)
+  const __half* pe16_b;    // [64]
+  int pe_f16;
   GladQLinear qp;          // only alpha/beta are read (absmax of its input)
   int act_mode;
+  int ld_enc;              // row stride of `enc` (>= 128 + prop_dim)
   // outputs
   int8_t* z8_out;          // [B*187,16]
   __half* feat_out;        // [B*187,64]
   int32_t* acc_out;        // [B*187,64]
   __half* score_local;     // [B,187]
   __half* gc_w_out;        // [B,187]
-  __half* enc;             // [B,224]: writes columns 64..223 (gc, proprio)
+  __half* enc;             // [B,ld_enc]: writes columns 64..127+prop_dim (gc, proprio)
   __half* pe_out;          // [B,64]
   float* slots;
 };
@@ -207,18 +211,35 @@ struct TailParams {
   const __half* in_b;      // [192]
   const __half* out_w;     // [64,64]
   const __half* out_b;     // [64]
-  const float* a0_alpha;   // actor.0 LET (absmax of its input), may be null
+  const float* a0_alpha;   // LET of the layer after the encoder (absmax of its input)
   const float* a0_beta;
+  int a0_absmax;           // reduce that absmax (an INT8 layer follows the encoder)
   int act_mode;
+  int ld_enc;              // row stride of `enc`
+  int prop_dim;            // proprio columns of `enc` (from column 128)
   const float* noise;      // [B,187] or null
   const int8_t* z8;        // [B*187,16]
   const __half* score_local;
   const __half* pe;        // [B,64]
-  __half* enc;             // [B,224]: reads 64..223, writes 0..63
+  __half* enc;             // [B,ld_enc]: reads 64..127+prop_dim, writes 0..63
   __half* topk_logits_out; // [B,187] or null
   int64_t* topk_idx_out;   // [B,32] or null
   __half* attn_w_out;      // [B,32] or null
   float* slots;
+};
+
+// fp16 Linear (+ bias, optional ELU) as a tcgen05 kind::f16 GEMM.
+struct HGemmParams {
+  const __half* w;         // [N, K] row-major
+  const __half* b;         // [N] or null
+  int K, N;
+  const __half* x;         // [M, K] row stride ldx
+  int64_t M, ldx;
+  __half* y;               // [M, ldy] fp16 out (or null)
+  int64_t ldy;
+  float* y32;              // [M, ldy32] float(fp16 out) (or null)
+  int64_t ldy32;
+  int elu;
 };
 
 struct GemmParams {

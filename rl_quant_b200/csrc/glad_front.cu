@@ -42,7 +42,7 @@ constexpr int kFrontThreads = 256;
 #ifndef FRONT_MIN_BLOCKS
 #define FRONT_MIN_BLOCKS 2
 #endif
-constexpr int kMaxProp = 96;                           // proprio width of the fused front mode
+constexpr int kMaxProp = 104;                          // proprio width limit of the fused front mode
 
 struct __align__(128) FrontSmem {
   uint8_t planes[kPlanesBytes];
@@ -50,9 +50,15 @@ struct __align__(128) FrontSmem {
   uint8_t strip[kStripBytes];
   uint8_t w2s[kW2sBytes];
   uint8_t stage[kStageBytes];
-  float b1[16], qa[16], qc[16];
-  float dq[64], b2[64], a2[64], c2[64];
-  float wg[64], ws[64];                 // GPS weight, scorer weight (local half)
+  alignas(16) float b1[16];
+  alignas(16) float qa[16];
+  alignas(16) float qc[16];
+  alignas(16) float dq[64];
+  alignas(16) float b2[64];
+  alignas(16) float a2[64];
+  alignas(16) float c2[64];
+  alignas(16) float wg[64];             // GPS weight (local half of the merged GEMM)
+  alignas(16) float ws[64];             // scorer weight, local half
   float2 lpart[2][2][128];              // [tile][channel half][row] partial (gps, scorer) logits
   __half wt16[2][128];                  // softmax weights per row of each tile
   float pool[2][4][64];                 // [tile][lane quarter][channel] pooled partial sums
@@ -61,8 +67,8 @@ struct __align__(128) FrontSmem {
   __half pe16[64];
   __half gc16[64];
   alignas(16) int8_t q8[128];           // quantised proprio
-  alignas(16) int8_t pe_w8[64 * kMaxProp];  // actor_proprio_embedding int8 rows
-  float pe_a[kMaxProp], pe_b[kMaxProp]; // its LET alpha / beta
+  alignas(16) uint8_t pe_w[64 * kMaxProp * 2];  // proprio embedding rows: int8 or fp16
+  float pe_a[kMaxProp], pe_b[kMaxProp]; // int8 embedding: LET alpha / beta
   float pe_scale[64], pe_bp[64];        // its output scale and bias
   float qp_a[128], qp_b[128];           // query_projector LET (absmax of its input)
   uint64_t mbar;
@@ -258,18 +264,24 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
   float zmax_qp = 0.0f;
   const int P = p.prop_dim;
   if (kFront) {
-    aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
+    if (!p.pe_f16) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
     aq_qp.let = p.qp.alpha != nullptr;
     gb = __half2float(p.gps_b[0]);
-    for (int i = tid; i < kD * P / 4; i += NT)
-      reinterpret_cast<int*>(s.pe_w8)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
-    for (int k = tid; k < P; k += NT) {
-      s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
-      s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;
-    }
-    if (tid < kD) {
-      s.pe_scale[tid] = out_scale(p.pe, aq_pe, tid);
-      s.pe_bp[tid] = p.pe.b_prime[tid];
+    if (p.pe_f16) {
+      __half* dst = reinterpret_cast<__half*>(s.pe_w);
+      for (int i = tid; i < kD * P; i += NT) dst[i] = p.pe16_w[i];
+      if (tid < kD) s.pe_bp[tid] = p.pe16_b ? __half2float(p.pe16_b[tid]) : 0.0f;
+    } else {
+      for (int i = tid; i < kD * P / 4; i += NT)
+        reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
+      for (int k = tid; k < P; k += NT) {
+        s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
+        s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;
+      }
+      if (tid < kD) {
+        s.pe_scale[tid] = out_scale(p.pe, aq_pe, tid);
+        s.pe_bp[tid] = p.pe.b_prime[tid];
+      }
     }
     if (tid < 128) {
       s.qp_a[tid] = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
@@ -348,19 +360,34 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
       }
 
       if (kFront) {
-        // proprio embedding while the tensor core runs (qrt/qlinear.py:123-138)
-        for (int k = tid; k < P; k += NT)
-          s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[k]), s.pe_a[k], s.pe_b[k]);
-        __syncthreads();
-        if (tid < 2 * kD) {
-          // two threads per output row, each half of K
-          const int n = tid >> 1, part = tid & 1;
-          const int* wrow = reinterpret_cast<const int*>(s.pe_w8 + n * P) + part * (P / 8);
-          const int* qw = reinterpret_cast<const int*>(s.q8) + part * (P / 8);
-          int acc = 0;
-          for (int k4 = 0; k4 < P / 8; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
-          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-          if (part == 0) s.pe16[n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
+        // proprio embedding while the tensor core runs
+        if (p.pe_f16) {
+          // fp16 nn.Linear: fp32 accumulation, bias, one rounding
+          if (tid < 2 * kD) {
+            const int n = tid >> 1, part = tid & 1;
+            const __half* wrow = reinterpret_cast<const __half*>(s.pe_w) + n * P;
+            const int half_k = (P + 1) >> 1;
+            const int k0 = part * half_k, k1 = min(P, k0 + half_k);
+            float a = 0.0f;
+            for (int k = k0; k < k1; ++k) a = fmaf(__half2float(s.prop16[k]), __half2float(wrow[k]), a);
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            if (part == 0) s.pe16[n] = __float2half_rn(a + s.pe_bp[n]);
+          }
+        } else {
+          // W8A8 QuantLinear (qrt/qlinear.py:123-138)
+          for (int k = tid; k < P; k += NT)
+            s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[k]), s.pe_a[k], s.pe_b[k]);
+          __syncthreads();
+          if (tid < 2 * kD) {
+            // two threads per output row, each half of K
+            const int n = tid >> 1, part = tid & 1;
+            const int* wrow = reinterpret_cast<const int*>(s.pe_w + n * P) + part * (P / 8);
+            const int* qw = reinterpret_cast<const int*>(s.q8) + part * (P / 8);
+            int acc = 0;
+            for (int k4 = 0; k4 < P / 8; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            if (part == 0) s.pe16[n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
+          }
         }
       }
 
@@ -384,11 +411,16 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
             uint32_t pk[4];
 #pragma unroll
             for (int w4 = 0; w4 < 4; ++w4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(&s.b1[4 * w4]);
+              const float4 qa4 = *reinterpret_cast<const float4*>(&s.qa[4 * w4]);
+              const float4 qc4 = *reinterpret_cast<const float4*>(&s.qc[4 * w4]);
+              const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+              const float aa[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
+              const float cc[4] = {qc4.x, qc4.y, qc4.z, qc4.w};
               uint32_t word = 0;
 #pragma unroll
               for (int b = 0; b < 4; ++b) {
-                const int c = w4 * 4 + b;
-                const int q = conv1_quant(__uint_as_float(r[c]), s.b1[c], s.qa[c], s.qc[c]);
+                const int q = conv1_quant(__uint_as_float(r[4 * w4 + b]), bb[b], aa[b], cc[b]);
                 word |= ((uint32_t)(q & 0xFF)) << (8 * b);
               }
               pk[w4] = word;
@@ -461,18 +493,32 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
             tmem_ld16(tmem + lane_base + t * 64 + c0 + 16 * hb, r);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; j += 2) {
+            for (int j = 0; j < 16; j += 4) {
               const int c = c0 + 16 * hb + j;
-              const float y0 = conv2_val((int32_t)r[j], s.dq[c], s.b2[c], s.a2[c], s.c2[c]);
-              const float y1 = conv2_val((int32_t)r[j + 1], s.dq[c + 1], s.b2[c + 1], s.a2[c + 1], s.c2[c + 1]);
-              __half2 hh = __floats2half2_rn(y0, y1);
-              loc[t][8 * hb + (j >> 1)] = *reinterpret_cast<uint32_t*>(&hh);
+              // per-channel constants, four channels per 16-byte shared load
+              const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
+              const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
+              const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
+              const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
+              const float y0 = conv2_val((int32_t)r[j], dq4.x, b24.x, a24.x, c24.x);
+              const float y1 = conv2_val((int32_t)r[j + 1], dq4.y, b24.y, a24.y, c24.y);
+              const float y2 = conv2_val((int32_t)r[j + 2], dq4.z, b24.z, a24.z, c24.z);
+              const float y3 = conv2_val((int32_t)r[j + 3], dq4.w, b24.w, a24.w, c24.w);
+              __half2 h01 = __floats2half2_rn(y0, y1), h23 = __floats2half2_rn(y2, y3);
+              loc[t][8 * hb + (j >> 1)] = *reinterpret_cast<uint32_t*>(&h01);
+              loc[t][8 * hb + (j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h23);
               if (kFront) {
-                const float2 f = __half22float2(hh);
-                l0 = fmaf(f.x, s.wg[c], l0);
-                l0 = fmaf(f.y, s.wg[c + 1], l0);
-                l1 = fmaf(f.x, s.ws[c], l1);
-                l1 = fmaf(f.y, s.ws[c + 1], l1);
+                const float4 wg4 = *reinterpret_cast<const float4*>(&s.wg[c]);
+                const float4 ws4 = *reinterpret_cast<const float4*>(&s.ws[c]);
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                l0 = fmaf(f01.x, wg4.x, l0);
+                l0 = fmaf(f01.y, wg4.y, l0);
+                l0 = fmaf(f23.x, wg4.z, l0);
+                l0 = fmaf(f23.y, wg4.w, l0);
+                l1 = fmaf(f01.x, ws4.x, l1);
+                l1 = fmaf(f01.y, ws4.y, l1);
+                l1 = fmaf(f23.x, ws4.z, l1);
+                l1 = fmaf(f23.y, ws4.w, l1);
               }
             }
             if (valid && p.acc_out) {
@@ -567,10 +613,10 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
             for (int q = 0; q < 4; ++q) g += s.pool[t][q][tid];
           const __half gh = __float2half_rn(g);
           s.gc16[tid] = gh;
-          p.enc[env * kEnc + 64 + tid] = gh;
+          p.enc[env * p.ld_enc + 64 + tid] = gh;
           p.pe_out[env * kD + tid] = s.pe16[tid];
         }
-        for (int k = tid; k < P; k += NT) p.enc[env * kEnc + 128 + k] = s.prop16[k];
+        for (int k = tid; k < P; k += NT) p.enc[env * p.ld_enc + 128 + k] = s.prop16[k];
         __syncthreads();
         if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
           // |alpha*cat(gc, pe) + beta| for the query projector's dynamic s_z

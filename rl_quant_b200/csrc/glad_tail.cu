@@ -30,7 +30,7 @@ struct __align__(128) TailSmem {
   float dq[64], b2[64], a2c[64], c2[64];
   float bin[192], bout[64];
   float wsq[64];                  // scorer weight, query half
-  float a0_a[224], a0_b[224];
+  float a0_a[232], a0_b[232];
   float qv[4][64];                // query (fp16 values)
   float qm[4][64];                // MHA query projection (fp16 values)
   float om[4][64];                // attention output (fp16 values)
@@ -96,7 +96,8 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
   }
   for (int k = tid; k < 192; k += 128) s.bin[k] = __half2float(p.in_b[k]);
   const bool a0_let = p.a0_alpha != nullptr;
-  for (int k = tid; k < kEnc; k += 128) {
+  const int enc_w = 128 + p.prop_dim;
+  for (int k = tid; k < enc_w; k += 128) {
     s.a0_a[k] = a0_let ? p.a0_alpha[k] : 0.0f;
     s.a0_b[k] = a0_let ? p.a0_beta[k] : 0.0f;
   }
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     const int r = 32 * warp + lane;              // GEMM row of this thread
     if (have) {
       // ---- 1. query projector: W8A8 over cat(gc, pe) ---------------------------------
-      const __half* gc = p.enc + env * kEnc + 64;
+      const __half* gc = p.enc + env * p.ld_enc + 64;
       const __half* pe = p.pe + env * kD;
       uint32_t qword = 0;
 #pragma unroll
@@ -336,20 +337,20 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
         f2[h] = fp16r(__fadd_rn(fp16r(a), s.bout[n]));
       }
       __half2 fh = __floats2half2_rn(f2[0], f2[1]);
-      reinterpret_cast<__half2*>(p.enc + env * kEnc)[lane] = fh;
-      if (p.act_mode == GLAD_ACT_DYNAMIC) {
+      reinterpret_cast<__half2*>(p.enc + env * p.ld_enc)[lane] = fh;
+      if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
         // |alpha*encoded + beta| for actor.0's dynamic s_z
         float zm = fmaxf(aq_a0.absz(f2[0], s.a0_a[2 * lane], s.a0_b[2 * lane]),
                          aq_a0.absz(f2[1], s.a0_a[2 * lane + 1], s.a0_b[2 * lane + 1]));
-        for (int k = 64 + lane; k < kEnc; k += 32)
-          zm = fmaxf(zm, aq_a0.absz(__half2float(p.enc[env * kEnc + k]), s.a0_a[k], s.a0_b[k]));
+        for (int k = 64 + lane; k < enc_w; k += 32)
+          zm = fmaxf(zm, aq_a0.absz(__half2float(p.enc[env * p.ld_enc + k]), s.a0_a[k], s.a0_b[k]));
         zmax_a0 = fmaxf(zmax_a0, zm);
       }
     }
     __syncthreads();
   }
 
-  if (p.act_mode == GLAD_ACT_DYNAMIC) {
+  if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
     const float m = warp_max(zmax_a0);
     if (lane == 0 && m > 0.0f) atomic_max_nonneg(&p.slots[2], m);
   }

@@ -118,3 +118,71 @@ class FusedActor:
             enc.data_ptr(), attn.data_ptr(), idx.data_ptr(), gcw.data_ptr())
         self.run(obs, None, aux, noise)
         return enc, attn, idx, gcw
+
+
+class FusedCritic:
+    """The fused critic forward (``glad_critic_forward``) of one GLAD inference
+    copy: shared encoder, critic proprio embedding, fp16 critic MLP."""
+
+    def __init__(self, model: nn.Module):
+        self.model = model
+        if not isinstance(model.map_cnn, QuantCNN):
+            raise FusedUnsupported("map_cnn is not a QuantCNN (swap_cnn first)")
+        if not isinstance(model.query_projector, QuantLinear):
+            raise FusedUnsupported("query_projector is not a QuantLinear")
+        for p in ("critic.0", "critic.2", "critic.4", "critic.6"):
+            layer = model.get_submodule(p)
+            if type(layer) is not nn.Linear:
+                raise FusedUnsupported(f"{p} must be an fp16 nn.Linear (the critic MLP is not quantised)")
+        self.P = int(model.critic_proprio_dim)
+        if self.P > 104:
+            raise FusedUnsupported("critic proprio width above 104")
+        # the reference picks the actor's embedding when both widths agree
+        # (rsl_rl actor_critic_encoder.py:226-229)
+        self.use_actor_emb = self.P == int(model.actor_proprio_dim)
+        if self.use_actor_emb and not isinstance(model.actor_proprio_embedding, QuantLinear):
+            raise FusedUnsupported("actor_proprio_embedding must be a QuantLinear")
+        self.act_mode = model_act_mode(model)
+        self._ws: dict[tuple, torch.Tensor] = {}
+
+    def weights(self) -> N.GladCriticWeights:
+        m = self.model
+        w = N.GladCriticWeights()
+        w.conv = m.map_cnn.conv_struct()
+        if self.use_actor_emb:
+            w.proprio_emb_q = N.qlinear_struct(m.actor_proprio_embedding)
+        else:
+            e = m.critic_proprio_embedding
+            w.proprio_emb = N.GladLinear16(_fp16(e.weight, "critic_proprio_embedding.weight").data_ptr(),
+                                           N.ptr(e.bias), e.in_features, e.out_features)
+        w.query_proj = N.qlinear_struct(m.query_projector)
+        w.gps_w = _fp16(m.global_pool_selector.weight, "global_pool_selector.weight").data_ptr()
+        w.gps_b = _fp16(m.global_pool_selector.bias, "global_pool_selector.bias").data_ptr()
+        w.scorer_w = _fp16(m.topk_scorer.weight, "topk_scorer.weight").data_ptr()
+        w.scorer_b = _fp16(m.topk_scorer.bias, "topk_scorer.bias").data_ptr()
+        w.mha_in_w = _fp16(m.mha.in_proj_weight, "mha.in_proj_weight").data_ptr()
+        w.mha_in_b = _fp16(m.mha.in_proj_bias, "mha.in_proj_bias").data_ptr()
+        w.mha_out_w = _fp16(m.mha.out_proj.weight, "mha.out_proj.weight").data_ptr()
+        w.mha_out_b = _fp16(m.mha.out_proj.bias, "mha.out_proj.bias").data_ptr()
+        for i, p in enumerate(("critic.0", "critic.2", "critic.4", "critic.6")):
+            L = m.get_submodule(p)
+            w.mlp[i] = N.GladLinear16(_fp16(L.weight, f"{p}.weight").data_ptr(),
+                                      N.ptr(_fp16(L.bias, f"{p}.bias")) if L.bias is not None else None,
+                                      L.in_features, L.out_features)
+        return w
+
+    def run(self, obs: torch.Tensor, value: torch.Tensor, noise: torch.Tensor | None = None) -> None:
+        N.require_cuda(obs)
+        if obs.dim() != 2 or obs.stride(1) != 1:
+            raise ValueError("obs must be a row-major [B, P+2079] tensor")
+        B = obs.shape[0]
+        key = (B, str(obs.device))
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = torch.empty(N.load().glad_critic_workspace_size(B), dtype=torch.uint8, device=obs.device)
+            self._ws[key] = ws
+        rc = N.load().glad_critic_forward(
+            self.weights(), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
+            B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise), value.data_ptr(), None,
+            ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
+        N.check(rc, "glad_critic_forward")

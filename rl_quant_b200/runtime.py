@@ -23,7 +23,7 @@ import torch
 
 from . import _native as N
 from .encoder_opt import _gumbel_noise
-from .fused import FusedActor, FusedUnsupported
+from .fused import FusedActor, FusedCritic, FusedUnsupported
 from .qconv import QuantCNN
 from .qlinear import QuantLinear
 
@@ -75,6 +75,12 @@ class InferenceRunner:
         except FusedUnsupported as e:
             self._fused = None
             warnings.warn(f"[rl_quant_b200] fused GLAD forward unavailable ({e}); running op by op")
+        self._fused_critic = None
+        if with_critic:
+            try:
+                self._fused_critic = FusedCritic(model)
+            except FusedUnsupported as e:
+                warnings.warn(f"[rl_quant_b200] fused GLAD critic unavailable ({e}); running op by op")
         self._graphs: dict[tuple, _Graph] = {}
         self._g_refresh = None
         self._g_sync = None
@@ -92,6 +98,11 @@ class InferenceRunner:
 
     def _val_fn(self, co):
         m = self.model
+        if self._fused_critic is not None and co.shape[1] == self._fused_critic.P + 2079:
+            value = torch.empty(co.shape[0], 1, dtype=torch.float32, device=co.device)
+            noise = _gumbel_noise((co.shape[0], 187), co.device) if m.training else None
+            self._fused_critic.run(m.critic_obs_normalizer(co), value, noise)
+            return value
         c = m.critic_obs_normalizer(co)
         enc_fn = getattr(m, "_encode_terrain_orig", None) if co.shape[1] - 2079 != getattr(
             m, "actor_proprio_dim", -1) else None

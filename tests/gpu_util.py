@@ -60,6 +60,48 @@ class DeviceWeights:
         return w
 
 
+def critic_weights(dw: DeviceWeights) -> N.GladCriticWeights:
+    t = dw.t
+    w = N.GladCriticWeights()
+    w.conv = dw.conv()
+    e = t["critic_proprio_embedding.weight"]
+    w.proprio_emb = N.GladLinear16(e.data_ptr(), t["critic_proprio_embedding.bias"].data_ptr(),
+                                   int(e.shape[1]), int(e.shape[0]))
+    w.query_proj = dw.ql("query_projector")
+    w.gps_w, w.gps_b = N.ptr(t["global_pool_selector.weight"]), N.ptr(t["global_pool_selector.bias"])
+    w.scorer_w, w.scorer_b = N.ptr(t["topk_scorer.weight"]), N.ptr(t["topk_scorer.bias"])
+    w.mha_in_w, w.mha_in_b = N.ptr(t["mha.in_proj_weight"]), N.ptr(t["mha.in_proj_bias"])
+    w.mha_out_w, w.mha_out_b = N.ptr(t["mha.out_proj.weight"]), N.ptr(t["mha.out_proj.bias"])
+    for i, n in enumerate(("critic.0", "critic.2", "critic.4", "critic.6")):
+        W = t[f"{n}.weight"]
+        w.mlp[i] = N.GladLinear16(W.data_ptr(), t[f"{n}.bias"].data_ptr(), int(W.shape[1]), int(W.shape[0]))
+    return w
+
+
+def critic_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, with_aux=True):
+    B, dev = obs.shape[0], obs.device
+    value = torch.empty(B, 1, dtype=torch.float32, device=dev)
+    aux = N.GladActorAux()
+    aux_t = {}
+    if with_aux:
+        aux_t = {"topk_logits": torch.empty(B, 187, dtype=torch.float16, device=dev),
+                 "topk_idx": torch.empty(B, 32, dtype=torch.int64, device=dev),
+                 "encoded": torch.empty(B, 232, dtype=torch.float16, device=dev)}
+        for k, v in aux_t.items():
+            setattr(aux, k, v.data_ptr())
+    lib = N.load()
+    nbytes = lib.glad_critic_workspace_size(B)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dtype = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
+    N.check(lib.glad_critic_forward(critic_weights(dw), obs.data_ptr(), dtype, B, obs.stride(0),
+                                    N.ACT_MODES[act_mode], None, value.data_ptr(), aux, ws.data_ptr(), nbytes,
+                                    N.stream_handle()), "glad_critic_forward")
+    st = N.c_uint32(0)
+    N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
+    torch.cuda.synchronize()
+    return value, aux_t
+
+
 def actor_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, noise=None, with_aux=True):
     """Run glad_actor_forward; returns (mean, aux dict of tensors)."""
     B = obs.shape[0]

@@ -191,3 +191,16 @@ def test_cpu_tensors_are_rejected(gm):
         m.get_submodule("actor.0")(torch.randn(4, 224).half())
     with pytest.raises(RuntimeError):
         QuantLinear(nn.Linear(16, 8))
+
+
+@pytest.mark.parametrize("mode", ["eager", "manual-graph"])
+def test_runner_evaluate_matches_reference(gm, golden_fwd, mode):
+    m, _ = gm
+    r = InferenceRunner(m, mode=mode, with_critic=True)
+    assert r._fused_critic is not None
+    for B in (3, 16):
+        d = golden_fwd[B]
+        v = r.evaluate(torch.from_numpy(d["critic_obs"]).cuda().half()).float().cpu().numpy()
+        ref = d["dynamic.value"]
+        assert v.shape == (B, 1)
+        assert np.abs(v - ref).max() <= 1e-2
