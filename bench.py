@@ -142,8 +142,9 @@ def run_ours(args):
     import torch.distributed as dist
 
     from rl_quant_b200 import InferenceRunner, _native as N
-    from rl_quant_b200.fused import FusedActor
-    from rl_quant_b200.synthetic import glad_obs
+    from rl_quant_b200.fused import FusedActor, FusedCritic
+    from rl_quant_b200.synthetic import glad_obs, glad_obs_pair
+    from rl_quant_b200.weight_sync import PackedWeights
 
     rank, local, world = rank_info()
     if world > 1:
@@ -151,8 +152,11 @@ def run_ours(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     B = args.batch
-    _, infer = build_inference_copy(device, args.act_mode)
+    master, infer = build_inference_copy(device, args.act_mode)
+    # every tensor of the inference copy in one device blob: one broadcast per PPO iteration
+    packed = PackedWeights(infer)
     fused = FusedActor(infer)
+    fused_critic = FusedCritic(infer)
     if fused.act_mode != args.act_mode:
         raise RuntimeError("calibrated model has the wrong act_mode")
 
@@ -222,8 +226,44 @@ def run_ours(args):
         N.load().glad_actor_stage_events(None, 0)
     stage_ms = [x / reps for x in stage_ms]
 
+    # actor + critic forward (one PPO rollout step of both heads)
+    n_ac = min(4, args.nbuf)
+    pairs = [glad_obs_pair(B, seed=5000 + 97 * rank + i) for i in range(n_ac)]
+    a_in = [p[0].to(device) for p in pairs]
+    c_in = [p[1].to(device) for p in pairs]
+    values = [torch.empty(B, 1, dtype=torch.float32, device=device) for _ in range(n_ac)]
+    for i in range(n_ac):
+        fused.run(a_in[i], means[i])
+        fused_critic.run(c_in[i], values[i])
+    torch.cuda.synchronize()
+    ac_graphs = []
+    with torch.cuda.stream(side):
+        for i in range(n_ac):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                fused.run(a_in[i], means[i])
+                fused_critic.run(c_in[i], values[i])
+            ac_graphs.append(g)
+    torch.cuda.current_stream(device).wait_stream(side)
+    k_ac = max(10, min(args.steps, 1000))
+    for k in range(10):
+        ac_graphs[k % n_ac].replay()
+    barrier()
+    e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e4.record()
+    for k in range(k_ac):
+        ac_graphs[k % n_ac].replay()
+    e5.record()
+    barrier()
+    ms_ac = e4.elapsed_time(e5)
+    if world > 1:
+        t = torch.tensor([ms_ac], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_ac = float(t.item())
+    ac_value = B * world / (ms_ac / k_ac / 1e3)
+
     # end to end through InferenceRunner.act with host buffers
-    runner = InferenceRunner(infer, mode="manual-graph")
+    runner = InferenceRunner(infer, mode="manual-graph", with_critic=True)
     host = [o.cpu().pin_memory() for o in obs[:2]]
     dev_in = torch.empty_like(obs[0])
     out_host = torch.empty(B, 29, dtype=torch.float32).pin_memory()
@@ -245,6 +285,40 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_e2e = float(t.item())
     e2e_value = B * world / (ms_e2e / k_e2e / 1e3)
+
+    # per-iteration weight hand-over: W += 1e-3 N(0,1) on the fp32 master (rank 0,
+    # not timed), then [rank 0: graphed cast-copy + requantise] + one NCCL
+    # broadcast of the packed blob to every rank (timed, max over ranks)
+    n_sync = 30
+    gen = torch.Generator(device=device).manual_seed(7)
+    sync_ms = 0.0
+    for it in range(n_sync + 3):
+        if rank == 0:
+            with torch.no_grad():
+                for p_ in master.parameters():
+                    p_.add_(1e-3 * torch.randn(p_.shape, device=device, generator=gen))
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        if rank == 0:
+            runner.sync_weights_from(master)
+        if world > 1:
+            packed.broadcast(src=0)
+        s1.record()
+        barrier()
+        if it >= 3:
+            sync_ms += s0.elapsed_time(s1)
+    sync_ms /= n_sync
+    checks_ok = True
+    if world > 1:
+        t = torch.tensor([sync_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sync_ms = float(t.item())
+        cs = torch.tensor([packed.checksum()], dtype=torch.int64, device=device)
+        lo, hi = cs.clone(), cs.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        checks_ok = bool(lo.item() == hi.item())
 
     if rank == 0:
         peaks = {}
@@ -289,13 +363,19 @@ def run_ours(args):
                                  "frac_hbm": fwd_gbs / hbm_peak, "macs_per_env": MACS_PER_ENV,
                                  "achieved_tops": tops},
             "stage_ms": dict(zip(N_STAGES, stage_ms)),
+            "actor_critic": {"value": ac_value, "unit": UNIT, "ms_per_step": ms_ac / k_ac,
+                             "workload": f"actor + critic forward, B={B} per GPU, {world * B} envs"},
+            "weight_sync": {"ms": sync_ms, "bytes": packed.nbytes,
+                            "collective": "nccl broadcast of one packed blob" if world > 1 else "none (1 GPU)",
+                            "steps": "cast-copy fp32 master -> fp16 copy + requantise (one CUDA graph) + broadcast",
+                            "ranks_identical": checks_ok},
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * (7 if args.act_mode == "dynamic" else 6),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
-        del graphs
+        del graphs, ac_graphs
         dist.destroy_process_group()
 
 
