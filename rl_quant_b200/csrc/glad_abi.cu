@@ -13,13 +13,13 @@
 namespace glad {
 size_t front_smem_bytes();
 template <int MODE>
-cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st);
+cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl = false);
 size_t tail_smem_bytes();
-cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st);
+cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl = false);
 template <int NT>
-cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st);
+cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
 template <int NT>
-cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st);
+cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st, bool pdl = false);
 size_t hgemm_smem_bytes(int K, int NT);
 size_t qgemm_smem_bytes(int K, int NT);
 cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
@@ -373,6 +373,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
 
   stage_mark(0, st);
   GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
+  const bool front_pdl = act_mode == GLAD_ACT_DYNAMIC;
   if (act_mode == GLAD_ACT_DYNAMIC)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb.alpha,
                                   w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st),
@@ -399,7 +400,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.enc = enc;
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
-  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st), "front launch");
+  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st, front_pdl), "front launch");
   stage_mark(2, st);
 
   TailParams tp{};
@@ -429,7 +430,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.slots = ws.slots;
   const int64_t groups = (B + 3) / 4;
   const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
-  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st), "tail launch");
+  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st, true), "tail launch");
   stage_mark(3, st);
 
   __half* hs[4] = {enc, ws.h1, ws.h2, ws.h3};
@@ -452,15 +453,15 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
       g.next_let = w->mlp[i + 1].alpha != nullptr;
       g.next_slot = 3 + i;
       // N tile chosen so each layer launches ~B/128 x 4 CTAs
-      cudaError_t le = mn[i] >= 512 ? launch_qgemm<128>(g, st)
-                       : mn[i] >= 256 ? launch_qgemm<64>(g, st) : launch_qgemm<32>(g, st);
+      cudaError_t le = mn[i] >= 512 ? launch_qgemm<128>(g, st, true)
+                       : mn[i] >= 256 ? launch_qgemm<64>(g, st, true) : launch_qgemm<32>(g, st, true);
       GLAD_CHECK_CUDA(le, "actor MLP launch");
     } else {
       g.y32 = mean_out;
       g.ldy32 = kActions;
       g.y32_round16 = 1;                   // mean = fp16 output .float() (integration.py:206)
       g.next_slot = -1;
-      GLAD_CHECK_CUDA(launch_qgemm<32>(g, st), "actor head launch");
+      GLAD_CHECK_CUDA(launch_qgemm<32>(g, st, true), "actor head launch");
     }
     stage_mark(4 + i, st);
   }
@@ -537,7 +538,8 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
     return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded must be 16-byte aligned");
 
   GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
-  if (!pe16 && act_mode == GLAD_ACT_DYNAMIC)
+  const bool front_pdl = !pe16 && act_mode == GLAD_ACT_DYNAMIC;
+  if (front_pdl)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb_q.alpha,
                                   w->proprio_emb_q.beta, 1, &ws.slots[0], d.sms, st),
                     "absmax launch");
@@ -565,7 +567,7 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   fp.enc = enc;
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
-  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st), "front launch");
+  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st, front_pdl), "front launch");
 
   TailParams tp{};
   tp.B = B;
@@ -592,7 +594,7 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   tp.slots = ws.slots;
   const int64_t groups = (B + 3) / 4;
   const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
-  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st), "tail launch");
+  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st, true), "tail launch");
 
   const __half* xs[4] = {enc, ws.h1, ws.h2, ws.h3};
   const int64_t lds[4] = {kCriticEnc, 512, 256, 128};
@@ -611,12 +613,12 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
       g.y = ys[i];
       g.ldy = hn[i];
       g.elu = 1;
-      le = hn[i] >= 512 ? launch_hgemm<128>(g, st) : hn[i] >= 256 ? launch_hgemm<64>(g, st)
-                                                                   : launch_hgemm<32>(g, st);
+      le = hn[i] >= 512 ? launch_hgemm<128>(g, st, true) : hn[i] >= 256 ? launch_hgemm<64>(g, st, true)
+                                                                         : launch_hgemm<32>(g, st, true);
     } else {
       g.y32 = value_out;
       g.ldy32 = 1;
-      le = launch_hgemm<32>(g, st);
+      le = launch_hgemm<32>(g, st, true);
     }
     GLAD_CHECK_CUDA(le, "critic MLP launch");
   }

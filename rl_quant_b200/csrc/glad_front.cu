@@ -207,6 +207,7 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
   constexpr bool kConv2 = MODE != kModeConv1;
   constexpr bool kFront = MODE == kModeFront;
 
+  grid_dep_launch();                    // the next kernel may start its prologue
   // ---- one-time set-up ------------------------------------------------------
   if (warp == 0) tmem_alloc(&s.tmem_base, kTmemCols);
   if (tid == 0) {
@@ -257,6 +258,7 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
       }
     }
   }
+  grid_dep_wait();                      // inputs of the preceding kernel are visible from here
   // Front-mode constants.
   ActQuant aq_pe{};
   ActQuant aq_qp{};
@@ -650,18 +652,17 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
 size_t front_smem_bytes() { return sizeof(FrontSmem) + 128; }
 
 template <int MODE>
-cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st) {
+cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl) {
   const size_t smem = front_smem_bytes();
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)front_kernel<MODE>, done);
   if (e != cudaSuccess) return e;
-  front_kernel<MODE><<<grid, kFrontThreads, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(front_kernel<MODE>, dim3(grid), dim3(kFrontThreads), smem, st, pdl, p);
 }
 
-template cudaError_t launch_front<kModeConv1>(const FrontParams&, int, cudaStream_t);
-template cudaError_t launch_front<kModeConv2>(const FrontParams&, int, cudaStream_t);
-template cudaError_t launch_front<kModeChain>(const FrontParams&, int, cudaStream_t);
-template cudaError_t launch_front<kModeFront>(const FrontParams&, int, cudaStream_t);
+template cudaError_t launch_front<kModeConv1>(const FrontParams&, int, cudaStream_t, bool);
+template cudaError_t launch_front<kModeConv2>(const FrontParams&, int, cudaStream_t, bool);
+template cudaError_t launch_front<kModeChain>(const FrontParams&, int, cudaStream_t, bool);
+template cudaError_t launch_front<kModeFront>(const FrontParams&, int, cudaStream_t, bool);
 
 }  // namespace glad

@@ -43,6 +43,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
   const int n0 = blockIdx.y * NT;
   const int N = p.L.out_features;
   const int Np = (N + 7) & ~7;
+  grid_dep_launch();
   constexpr uint32_t kCols = NT < 32 ? 32 : NT;
 
   if (warp == 0) tmem_alloc(tmem_slot, kCols);
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) qgemm_kernel(const __grid_con
     }
   }
   cp_async_commit();
+  grid_dep_wait();                      // the producer of x and of the absmax slot is done
   const ActQuant aq = make_act_quant(p.L, p.act_mode, p.slots, p.slot);
   for (int j = tid; j < NT; j += kGemmThreads) {
     const int n = n0 + j;
@@ -211,19 +213,18 @@ size_t qgemm_smem_bytes(int K, int NT) {
 }
 
 template <int NT>
-cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st) {
+cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl) {
   const size_t smem = qgemm_smem_bytes(p.L.in_features, NT);
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)qgemm_kernel<NT>, done);
   if (e != cudaSuccess) return e;
   const int Np = (p.L.out_features + 7) & ~7;
   dim3 grid((unsigned)((p.M + 127) / 128), (unsigned)((Np + NT - 1) / NT));
-  qgemm_kernel<NT><<<grid, kGemmThreads, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(qgemm_kernel<NT>, grid, dim3(kGemmThreads), smem, st, pdl, p);
 }
-template cudaError_t launch_qgemm<128>(const GemmParams&, cudaStream_t);
-template cudaError_t launch_qgemm<64>(const GemmParams&, cudaStream_t);
-template cudaError_t launch_qgemm<32>(const GemmParams&, cudaStream_t);
+template cudaError_t launch_qgemm<128>(const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_qgemm<64>(const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_qgemm<32>(const GemmParams&, cudaStream_t, bool);
 
 // ---- fp16 Linear on tcgen05 (kind::f16) -------------------------------------------
 // The critic MLP is not quantised (qrt/integration.py:42-43): y = x W^T + b in
@@ -247,6 +248,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hgemm_kernel(const __grid_con
   const int64_t m0 = (int64_t)blockIdx.x * 128;
   const int n0 = blockIdx.y * NT;
   const int N = p.N;
+  grid_dep_launch();
   constexpr uint32_t kCols = NT < 32 ? 32 : NT;
 
   if (warp == 0) tmem_alloc(tmem_slot, kCols);
@@ -272,20 +274,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hgemm_kernel(const __grid_con
   }
   for (int j = tid; j < NT; j += kGemmThreads)
     cbias[j] = (p.b && n0 + j < N) ? __half2float(p.b[n0 + j]) : 0.0f;
-  // activations
-  for (int idx = tid; idx < 128 * kc8; idx += kGemmThreads) {
-    const int r = idx / kc8, c = idx - r * kc8;
-    const int64_t m = m0 + r;
-    __align__(16) __half v[8];
-    const __half* src = p.x + m * p.ldx + c * 8;
-    const bool row = m < p.M;
-    if (row && c * 8 + 8 <= K && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-      *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(src);
-    } else {
+  grid_dep_wait();                      // the producer of x is done
+  // activations (batched loads, see the int8 GEMM)
+  constexpr int kUh = 8;
+  const int totalh = 128 * kc8;
+  for (int base_idx = 0; base_idx < totalh; base_idx += kUh * kGemmThreads) {
+    uint4 v[kUh];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = (row && c * 8 + e < K) ? src[e] : __float2half(0.0f);
+    for (int u = 0; u < kUh; ++u) {
+      const int idx = base_idx + u * kGemmThreads + tid;
+      const int r = idx / kc8, c = idx - r * kc8;
+      const int64_t m = m0 + r;
+      const __half* src = p.x + m * p.ldx + c * 8;
+      const bool row = idx < totalh && m < p.M;
+      if (row && c * 8 + 8 <= K && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        v[u] = *reinterpret_cast<const uint4*>(src);
+      } else {
+        __align__(16) __half t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = (row && c * 8 + e < K) ? src[e] : __float2half(0.0f);
+        v[u] = *reinterpret_cast<const uint4*>(t);
+      }
     }
-    *reinterpret_cast<uint4*>(As + c * 2048 + r * 16) = *reinterpret_cast<const uint4*>(v);
+#pragma unroll
+    for (int u = 0; u < kUh; ++u) {
+      const int idx = base_idx + u * kGemmThreads + tid;
+      if (idx >= totalh) continue;
+      const int r = idx / kc8, c = idx - r * kc8;
+      *reinterpret_cast<uint4*>(As + c * 2048 + r * 16) = v[u];
+    }
   }
   fence_async_smem();
   tc_fence_before();
@@ -361,18 +378,17 @@ size_t hgemm_smem_bytes(int K, int NT) {
 }
 
 template <int NT>
-cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st) {
+cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st, bool pdl) {
   const size_t smem = hgemm_smem_bytes(p.K, NT);
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)hgemm_kernel<NT>, done);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)((p.M + 127) / 128), (unsigned)((p.N + NT - 1) / NT));
-  hgemm_kernel<NT><<<grid, kGemmThreads, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(hgemm_kernel<NT>, grid, dim3(kGemmThreads), smem, st, pdl, p);
 }
-template cudaError_t launch_hgemm<128>(const HGemmParams&, cudaStream_t);
-template cudaError_t launch_hgemm<64>(const HGemmParams&, cudaStream_t);
-template cudaError_t launch_hgemm<32>(const HGemmParams&, cudaStream_t);
+template cudaError_t launch_hgemm<128>(const HGemmParams&, cudaStream_t, bool);
+template cudaError_t launch_hgemm<64>(const HGemmParams&, cudaStream_t, bool);
+template cudaError_t launch_hgemm<32>(const HGemmParams&, cudaStream_t, bool);
 
 // ---- dynamic absmax of alpha*x + beta over [M, K] ---------------------------------------
 // `round16`: the input is first rounded to fp16 (the .half() cast in front of
@@ -380,28 +396,47 @@ template cudaError_t launch_hgemm<32>(const HGemmParams&, cudaStream_t);
 __global__ void absmax_kernel(const void* x, int dtype, int64_t M, int64_t ld, int K,
                               const float* alpha, const float* beta, int round16,
                               float* slot) {
+  grid_dep_launch();
   ActQuant q{};
   q.let = alpha != nullptr;
   float m = 0.0f;
-  const int64_t total = M * (int64_t)K;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / K;
-    const int k = (int)(i - r * K);
-    float v = dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(x)[r * ld + k]
-                                      : __half2float(reinterpret_cast<const __half*>(x)[r * ld + k]);
-    if (round16) v = fp16r(v);
-    m = fmaxf(m, q.absz(v, q.let ? alpha[k] : 0.0f, q.let ? beta[k] : 0.0f));
+  // block = 256 threads = 8 rows x 32 lanes; lanes walk the row's K columns
+  const int lane = threadIdx.x & 31, rw = threadIdx.x >> 5;
+  for (int64_t r0 = (int64_t)blockIdx.x * 8; r0 < M; r0 += (int64_t)gridDim.x * 8) {
+    const int64_t r = r0 + rw;
+    if (r >= M) continue;
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = lane + 32 * u;
+      v[u] = 0.0f;
+      if (k < K)
+        v[u] = dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(x)[r * ld + k]
+                                       : __half2float(reinterpret_cast<const __half*>(x)[r * ld + k]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = lane + 32 * u;
+      if (k < K) {
+        const float xv = round16 ? fp16r(v[u]) : v[u];
+        m = fmaxf(m, q.absz(xv, q.let ? alpha[k] : 0.0f, q.let ? beta[k] : 0.0f));
+      }
+    }
+    for (int k = lane + 128; k < K; k += 32) {     // rows wider than 128
+      float xv = dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(x)[r * ld + k]
+                                         : __half2float(reinterpret_cast<const __half*>(x)[r * ld + k]);
+      if (round16) xv = fp16r(xv);
+      m = fmaxf(m, q.absz(xv, q.let ? alpha[k] : 0.0f, q.let ? beta[k] : 0.0f));
+    }
   }
   m = warp_max(m);
-  if ((threadIdx.x & 31) == 0 && m > 0.0f) atomic_max_nonneg(slot, m);
+  if (lane == 0 && m > 0.0f) atomic_max_nonneg(slot, m);
 }
 
 cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
                           const float* alpha, const float* beta, int round16, float* slot,
                           int num_sms, cudaStream_t st) {
-  const int64_t total = M * (int64_t)K;
-  int64_t blocks = (total + 255) / 256;
+  int64_t blocks = (M + 7) / 8;
   if (blocks > 4LL * num_sms) blocks = 4LL * num_sms;
   if (blocks < 1) blocks = 1;
   absmax_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, dtype, M, ld, K, alpha, beta, round16, slot);

@@ -53,6 +53,7 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+  grid_dep_launch();
   if (warp == 0) tmem_alloc(&s.tmem_base, kTailTmemCols);
   if (tid == 0) {
     mbar_init(&s.mbar, 1);
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
   }
   for (int idx = tid; idx < 64 * 128 / 16; idx += 128)
     reinterpret_cast<uint4*>(s.w8qp)[idx] = reinterpret_cast<const uint4*>(p.qp.w8)[idx];
+  grid_dep_wait();                      // outputs of the front kernel are visible from here
   const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
   for (int k = tid; k < 128; k += 128) {
     s.qp_a[k] = aq.let ? p.qp.alpha[k] : 0.0f;
@@ -368,13 +370,12 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
 
 size_t tail_smem_bytes() { return sizeof(TailSmem) + 128; }
 
-cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st) {
+cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl) {
   const size_t smem = tail_smem_bytes();
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)tail_kernel, done);
   if (e != cudaSuccess) return e;
-  tail_kernel<<<grid, 128, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(tail_kernel, dim3(grid), dim3(128), smem, st, pdl, p);
 }
 
 }  // namespace glad

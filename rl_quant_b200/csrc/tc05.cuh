@@ -8,6 +8,8 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <cstdlib>
+#include <utility>
 
 namespace glad {
 
@@ -60,6 +62,41 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     if (global_timer_ns() - t0 > limit_ns) return false;
   }
+}
+
+// ---- programmatic dependent launch ------------------------------------------------
+// Without the launch attribute both are no-ops.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// GLAD_PDL=1 in the environment turns programmatic dependent launch on for the
+// fused forwards' kernel chains (read once per process; off by default).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("GLAD_PDL");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
+// Launch `kernel` on `st`, optionally as a programmatic dependent of the
+// preceding kernel in the stream (its prologue may then overlap that kernel).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---- proxy fences -------------------------------------------------------------
