@@ -649,10 +649,496 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
   }
 }
 
+// ============================================================================================
+// Fused encoder front, software-pipelined across environments.
+//
+// Per iteration (environment e, planes buffer b = e & 1):
+//   wait conv1(e) -> conv1 epilogue -> issue conv2(e)
+//   stage -> planes[b^1] for e+1, prefetch e+2, issue conv1(e+1), proprio emb(e+1)
+//   wait conv2(e) -> logits, softmax, pooled gc, outputs of e
+// so the tensor core works on one environment while the CUDA cores convert
+// the next or finish the previous. conv1 accumulators live in TMEM columns
+// [128,160), conv2's in [0,128). All MMA descriptors are built once.
+// ============================================================================================
+constexpr int kFusedTmemCols = 256;
+
+struct __align__(128) FusedSmem {
+  uint8_t planes[2][kPlanesBytes];
+  uint8_t w1s[kW1sBytes];
+  uint8_t strip[kStripBytes];
+  uint8_t w2s[kW2sBytes];
+  uint8_t stage[kStageBytes];
+  alignas(16) float b1[16];
+  alignas(16) float qa[16];
+  alignas(16) float qc[16];
+  alignas(16) float dq[64];
+  alignas(16) float b2[64];
+  alignas(16) float a2[64];
+  alignas(16) float c2[64];
+  alignas(16) float wg[64];
+  alignas(16) float ws[64];
+  float2 lpart[2][2][128];
+  __half wt16[2][128];
+  float pool[2][4][64];
+  float wmax[8], wsum[8];
+  __half prop16[2][128];
+  __half pe16[2][64];
+  __half gc16[64];
+  alignas(16) int8_t q8[128];
+  alignas(16) uint8_t pe_w[64 * kMaxProp * 2];
+  float pe_a[kMaxProp], pe_b[kMaxProp];
+  float pe_scale[64], pe_bp[64];
+  float qp_a[128], qp_b[128];
+  uint64_t c1_adesc[2][16];            // [planes buffer][tile*8 + K-step]
+  uint64_t c1_bdesc[8];
+  uint64_t c2_adesc[10];               // [tile*5 + K-step]
+  uint64_t c2_bdesc[5];
+  uint64_t bar1, bar2;                 // conv1 / conv2 completion
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS)
+front_fused_kernel(const __grid_constant__ FrontParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  FusedSmem& s = *reinterpret_cast<FusedSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  constexpr int NT = kFrontThreads;
+  grid_dep_launch();
+
+  // ---- one-time set-up ------------------------------------------------------------------
+  if (warp == 0) tmem_alloc(&s.tmem_base, kFusedTmemCols);
+  if (tid == 0) {
+    mbar_init(&s.bar1, 1);
+    mbar_init(&s.bar2, 1);
+    fence_mbar_init();
+    s.abort_flag = 0;
+  }
+  {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < 2 * kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
+    for (int i = tid; i < kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(s.strip)[i] = z;
+  }
+  {
+    const __half* w1p = reinterpret_cast<const __half*>(p.conv.w1p);
+    __half* dst = reinterpret_cast<__half*>(s.w1s);
+    for (int idx = tid; idx < kW1sBytes / 2; idx += NT) {
+      const int pr = idx >> 8, c = (idx >> 7) & 1, n = (idx >> 3) & 15, e = idx & 7;
+      const int q = 2 * pr + c;
+      __half v = __float2half(0.0f);
+      if (q < 15) {
+        const int kh = q / 3, kw = 2 * (q % 3) + (e >> 2), ch = e & 3;
+        if (kw < 5 && ch < 3) v = w1p[(kh * 16 + kw * 3 + ch) * 16 + n];
+      }
+      dst[idx] = v;
+    }
+    for (int idx = tid; idx < kW2sBytes; idx += NT) {
+      const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
+      const int q = 2 * pr + c;
+      s.w2s[idx] = q < 9 ? (uint8_t)p.conv.w8[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
+    }
+    if (tid < 16) {
+      s.b1[tid] = p.conv.b1f[tid];
+      s.qa[tid] = p.conv.qa[tid];
+      s.qc[tid] = p.conv.qc[tid];
+    }
+    if (tid < 64) {
+      s.dq[tid] = p.conv.dq[tid];
+      s.b2[tid] = p.conv.b2f[tid];
+      s.a2[tid] = p.conv.a2[tid];
+      s.c2[tid] = p.conv.c2[tid];
+      s.wg[tid] = __half2float(p.gps_w[tid]);
+      s.ws[tid] = __half2float(p.scorer_w[tid]);
+    }
+  }
+  const int P = p.prop_dim;
+  grid_dep_wait();
+  ActQuant aq_pe{};
+  ActQuant aq_qp{};
+  if (!p.pe_f16) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
+  aq_qp.let = p.qp.alpha != nullptr;
+  const float gb = __half2float(p.gps_b[0]);
+  if (p.pe_f16) {
+    __half* dst = reinterpret_cast<__half*>(s.pe_w);
+    for (int i = tid; i < kD * P; i += NT) dst[i] = p.pe16_w[i];
+    if (tid < kD) s.pe_bp[tid] = p.pe16_b ? __half2float(p.pe16_b[tid]) : 0.0f;
+  } else {
+    for (int i = tid; i < kD * P / 4; i += NT)
+      reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
+    for (int k = tid; k < P; k += NT) {
+      s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
+      s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;
+    }
+    if (tid < kD) {
+      s.pe_scale[tid] = out_scale(p.pe, aq_pe, tid);
+      s.pe_bp[tid] = p.pe.b_prime[tid];
+    }
+  }
+  if (tid < 128) {
+    s.qp_a[tid] = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
+    s.qp_b[tid] = aq_qp.let ? p.qp.beta[tid] : 0.0f;
+  }
+  if (tid == 0) {
+    // every MMA descriptor of the loop, built once
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t pb = smem_u32(s.planes[b]);
+      for (int t = 0; t < 2; ++t)
+        for (int pr = 0; pr < 8; ++pr) {
+          const uint32_t c0 = conv1_chunk_off(2 * pr), c1 = conv1_chunk_off(2 * pr + 1);
+          s.c1_adesc[b][t * 8 + pr] = smem_desc(pb + c0 + t * 128 * 16, c1 - c0, 128);
+        }
+    }
+    for (int pr = 0; pr < 8; ++pr) s.c1_bdesc[pr] = smem_desc(smem_u32(s.w1s) + pr * 512, 256, 128);
+    const uint32_t sb = smem_u32(s.strip);
+    for (int t = 0; t < 2; ++t)
+      for (int pr = 0; pr < 5; ++pr) {
+        const int o0 = conv2_tap_off(2 * pr), o1 = conv2_tap_off(2 * pr + 1);
+        s.c2_adesc[t * 5 + pr] = smem_desc(sb + (t * 128 + o0) * 16, (o1 - o0) * 16, 128);
+      }
+    for (int pr = 0; pr < 5; ++pr) s.c2_bdesc[pr] = smem_desc(smem_u32(s.w2s) + pr * 2048, 1024, 128);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t tmem_c1 = tmem + 128;
+  const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+  uint32_t ph1 = 0, ph2 = 0;
+  float zmax_qp = 0.0f;
+
+  const int esz = p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2;
+  const int row_elems = P + kMap;
+
+  // convert the staged row of `e` into planes[b] / prop16[b]
+  auto convert = [&](int64_t e, int b) {
+    const RowStage rs = row_stage(p.in, e, p.ld, esz, row_elems, s.stage);
+    for (int px = tid; px < kH1 * kW1; px += NT) {
+      const int ih = px / kW1, iw = px - ih * kW1;
+      float v0, v1, v2;
+      if (esz == 4) {
+        v0 = row_elem<4>(rs, P + px * 3);
+        v1 = row_elem<4>(rs, P + px * 3 + 1);
+        v2 = row_elem<4>(rs, P + px * 3 + 2);
+      } else {
+        v0 = row_elem<2>(rs, P + px * 3);
+        v1 = row_elem<2>(rs, P + px * 3 + 1);
+        v2 = row_elem<2>(rs, P + px * 3 + 2);
+      }
+      const int pl = ih & 1, r = ((ih - pl) >> 1) + 1, slot = iw + 2;
+      __half2 h01 = __floats2half2_rn(v0, v1);
+      __half2 h2z = __floats2half2_rn(v2, 0.0f);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&h01);
+      pk.y = *reinterpret_cast<uint32_t*>(&h2z);
+      *reinterpret_cast<uint2*>(s.planes[b] + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
+    }
+    for (int k = tid; k < P; k += NT)
+      s.prop16[b][k] = __float2half_rn(esz == 4 ? row_elem<4>(rs, k) : row_elem<2>(rs, k));
+  };
+  auto issue_conv1 = [&](int b) {
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16(128, 16);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr)
+          mma_f16(tmem_c1 + t * 16, s.c1_adesc[b][t * 8 + pr], s.c1_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
+      mma_commit(&s.bar1);
+    }
+  };
+  // proprio embedding of the environment in buffer b (threads 0-127)
+  auto proprio_emb = [&](int b) {
+    if (p.pe_f16) {
+      if (tid < 2 * kD) {
+        const int n = tid >> 1, part = tid & 1;
+        const __half* wrow = reinterpret_cast<const __half*>(s.pe_w) + n * P;
+        const int half_k = (P + 1) >> 1;
+        const int k0 = part * half_k, k1 = min(P, k0 + half_k);
+        float a = 0.0f;
+        for (int k = k0; k < k1; ++k) a = fmaf(__half2float(s.prop16[b][k]), __half2float(wrow[k]), a);
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        if (part == 0) s.pe16[b][n] = __float2half_rn(a + s.pe_bp[n]);
+      }
+    } else {
+      for (int k = tid; k < P; k += NT)
+        s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[b][k]), s.pe_a[k], s.pe_b[k]);
+      __syncthreads();
+      if (tid < 2 * kD) {
+        const int n = tid >> 1, part = tid & 1;
+        const int* wrow = reinterpret_cast<const int*>(s.pe_w + n * P) + part * (P / 8);
+        const int* qw = reinterpret_cast<const int*>(s.q8) + part * (P / 8);
+        int acc = 0;
+        for (int k4 = 0; k4 < P / 8; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (part == 0) s.pe16[b][n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
+      }
+    }
+  };
+
+  // ---- prologue: first environment through conv1 issue ---------------------------------
+  int64_t env = blockIdx.x;
+  if (env < p.B) {
+    row_issue(row_stage(p.in, env, p.ld, esz, row_elems, s.stage), tid, NT);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    convert(env, 0);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    const int64_t nx = env + gridDim.x;
+    if (nx < p.B) row_issue(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), tid, NT);
+    cp_async_commit();
+    issue_conv1(0);
+    proprio_emb(0);
+  }
+
+  int b = 0;
+  for (; env < p.B; env += gridDim.x, b ^= 1) {
+    const int64_t nxt = env + gridDim.x;
+    // ---- conv1(e) done -> z8 -> strip, issue conv2(e) ---------------------------------------
+    if (!mbar_wait_bounded(&s.bar1, ph1)) s.abort_flag = 1;
+    ph1 ^= 1;
+    tc_fence_after();
+    __syncthreads();
+    if (s.abort_flag) break;
+    {
+      const int t = half;
+      const int m = t * 128 + 32 * quarter + lane;
+      if (t * 128 + 32 * quarter < 11 * 19) {
+        uint32_t r[16];
+        tmem_ld16(tmem_c1 + lane_base + t * 16, r);
+        tmem_ld_wait();
+        const int oh = m / 19, ow = m - oh * 19;
+        if (oh < kH2 && ow < kW2) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(&s.b1[4 * w4]);
+            const float4 qa4 = *reinterpret_cast<const float4*>(&s.qa[4 * w4]);
+            const float4 qc4 = *reinterpret_cast<const float4*>(&s.qc[4 * w4]);
+            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+            const float aa[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
+            const float cc[4] = {qc4.x, qc4.y, qc4.z, qc4.w};
+            uint32_t word = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int q = conv1_quant(__uint_as_float(r[4 * w4 + k]), bb[k], aa[k], cc[k]);
+              word |= ((uint32_t)(q & 0xFF)) << (8 * k);
+            }
+            pk[w4] = word;
+          }
+          const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
+          reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;
+        }
+      }
+    }
+    tc_fence_before();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_i8(128, 64);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int pr = 0; pr < 5; ++pr)
+          mma_i8(tmem + t * 64, s.c2_adesc[t * 5 + pr], s.c2_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
+      mma_commit(&s.bar2);
+    }
+
+    // ---- next environment: convert, prefetch, issue its conv1 (overlaps conv2(e)) ---------
+    if (nxt < p.B) {
+      cp_async_wait_all();
+      __syncthreads();
+      convert(nxt, b ^ 1);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      const int64_t nn = nxt + gridDim.x;
+      if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, NT);
+      cp_async_commit();
+      issue_conv1(b ^ 1);
+      proprio_emb(b ^ 1);
+    }
+
+    // ---- conv2(e) done -> local features -> logits, softmax pool ---------------------------
+    if (!mbar_wait_bounded(&s.bar2, ph2)) s.abort_flag = 1;
+    ph2 ^= 1;
+    tc_fence_after();
+    __syncthreads();
+    if (s.abort_flag) break;
+
+    uint32_t loc[2][16];
+    const int c0 = 32 * half;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int i = 32 * quarter + lane;
+      if (t * 128 + 32 * quarter < 11 * kStripCols) {
+        float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_base + t * 64 + c0 + 16 * hb, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const int c = c0 + 16 * hb + j;
+            const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
+            const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
+            const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
+            const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
+            const float y0 = conv2_val((int32_t)r[j], dq4.x, b24.x, a24.x, c24.x);
+            const float y1 = conv2_val((int32_t)r[j + 1], dq4.y, b24.y, a24.y, c24.y);
+            const float y2 = conv2_val((int32_t)r[j + 2], dq4.z, b24.z, a24.z, c24.z);
+            const float y3 = conv2_val((int32_t)r[j + 3], dq4.w, b24.w, a24.w, c24.w);
+            __half2 h01 = __floats2half2_rn(y0, y1), h23 = __floats2half2_rn(y2, y3);
+            loc[t][8 * hb + (j >> 1)] = *reinterpret_cast<uint32_t*>(&h01);
+            loc[t][8 * hb + (j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h23);
+            const float4 wg4 = *reinterpret_cast<const float4*>(&s.wg[c]);
+            const float4 ws4 = *reinterpret_cast<const float4*>(&s.ws[c]);
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            l0 = fmaf(f01.x, wg4.x, l0);
+            l0 = fmaf(f01.y, wg4.y, l0);
+            l0 = fmaf(f23.x, wg4.z, l0);
+            l0 = fmaf(f23.y, wg4.w, l0);
+            l1 = fmaf(f01.x, ws4.x, l1);
+            l1 = fmaf(f01.y, ws4.y, l1);
+            l1 = fmaf(f23.x, ws4.z, l1);
+            l1 = fmaf(f23.y, ws4.w, l1);
+          }
+        }
+        s.lpart[t][half][i] = make_float2(l0, l1);
+        if (p.feat_out) {
+          const int m = t * 128 + i;
+          const int oh = m / kStripCols, ow = m - oh * kStripCols;
+          if (oh < kH2 && ow < kW2) {
+            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh * kW2 + ow) * kD + c0);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              dst[q4] = make_uint4(loc[t][4 * q4], loc[t][4 * q4 + 1], loc[t][4 * q4 + 2], loc[t][4 * q4 + 3]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) loc[t][j] = 0;
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    // logits (qrt/encoder_opt.py:69-73) and the softmax over the 187 tokens (:75)
+    float my_logit;
+    int my_tok = -1;
+    {
+      const int t = half, i = 32 * quarter + lane;
+      const int m = t * 128 + i;
+      const int oh = m / kStripCols, ow = m - oh * kStripCols;
+      float g = -INFINITY;
+      if (oh < kH2 && ow < kW2) {
+        my_tok = oh * kW2 + ow;
+        const float2 a = s.lpart[t][0][i], c = s.lpart[t][1][i];
+        g = fp16r(__fadd_rn(fp16r(a.x + c.x), gb));
+        p.score_local[env * kTok + my_tok] = __float2half_rn(a.y + c.y);
+      }
+      my_logit = g;
+    }
+    float mx = warp_max(my_logit);
+    if (lane == 0) s.wmax[warp] = mx;
+    __syncthreads();
+    mx = s.wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s.wmax[w]);
+    const float ex = my_tok < 0 ? 0.0f : expf(my_logit - mx);
+    float sm = warp_sum(ex);
+    if (lane == 0) s.wsum[warp] = sm;
+    __syncthreads();
+    sm = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sm += s.wsum[w];
+    {
+      const __half wh = __float2half_rn(__fdiv_rn(ex, sm));
+      s.wt16[half][32 * quarter + lane] = my_tok < 0 ? __float2half(0.0f) : wh;
+      if (my_tok >= 0 && p.gc_w_out) p.gc_w_out[env * kTok + my_tok] = wh;
+    }
+    __syncthreads();
+    // pooled global context, gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77)
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t * 128 + 32 * quarter < 11 * kStripCols) {
+        const float wt = __half2float(s.wt16[t][32 * quarter + lane]);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 ff = __half22float2(*reinterpret_cast<const __half2*>(&loc[t][8 * hb + j]));
+            v[2 * j] = wt * ff.x;
+            v[2 * j + 1] = wt * ff.y;
+          }
+          const float r = warp_reduce16(v, lane);
+          if (lane < 16) s.pool[t][quarter][c0 + 16 * hb + lane] = r;
+        }
+      } else {
+        s.pool[t][quarter][c0 + lane] = 0.0f;
+      }
+    }
+    __syncthreads();
+    if (tid < kD) {
+      float g = 0.0f;
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) g += s.pool[t][q][tid];
+      const __half gh = __float2half_rn(g);
+      s.gc16[tid] = gh;
+      p.enc[env * p.ld_enc + 64 + tid] = gh;
+      p.pe_out[env * kD + tid] = s.pe16[b][tid];
+    }
+    for (int k = tid; k < P; k += NT) p.enc[env * p.ld_enc + 128 + k] = s.prop16[b][k];
+    __syncthreads();
+    if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
+      const float x = __half2float(tid < kD ? s.gc16[tid] : s.pe16[b][tid - kD]);
+      zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, s.qp_a[tid], s.qp_b[tid]));
+    }
+  }
+
+  // ---- teardown ----------------------------------------------------------------------------
+  cp_async_wait_all();
+  if (s.abort_flag) {
+    mbar_wait_bounded(&s.bar1, ph1);
+    mbar_wait_bounded(&s.bar2, ph2);
+  }
+  if (p.act_mode == GLAD_ACT_DYNAMIC) {
+    const float m = warp_max(zmax_qp);
+    if (lane == 0 && m > 0.0f) atomic_max_nonneg(&p.slots[1], m);
+  }
+  if (s.abort_flag && tid == 0 && p.slots)
+    atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrMmaTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kFusedTmemCols);
+  }
+}
+
 size_t front_smem_bytes() { return sizeof(FrontSmem) + 128; }
 
 template <int MODE>
 cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl) {
+  if (MODE == kModeFront) {
+    // the fused forward's front runs the pipelined kernel
+    static bool done_f[64] = {false};
+    cudaError_t e = allow_max_smem((const void*)front_fused_kernel, done_f);
+    if (e != cudaSuccess) return e;
+    return launch_k(front_fused_kernel, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
+                    pdl, p);
+  }
   const size_t smem = front_smem_bytes();
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)front_kernel<MODE>, done);
