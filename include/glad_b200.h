@@ -193,8 +193,18 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
  * stages of the following glad_actor_forward calls on this host thread:
  * events[0] before the first launch, then one after each stage (absmax, front,
  * tail, actor.0, actor.2, actor.4, actor.6), so n = 8 covers a dynamic-mode
- * call. n = 0 switches recording off. Not part of the reference interface.  */
+ * call. When the fused MLP kernel runs, the actor.0 stage spans all four
+ * layers and the other three are empty. n = 0 switches recording off. Not
+ * part of the reference interface.                                          */
 int glad_actor_stage_events(void* const* events, int n);
+
+/* 1 if glad_actor_forward runs the actor MLP as one fused kernel for a B-row
+ * call in `act_mode` on the current device, 0 if it runs one GEMM kernel per
+ * layer, < 0 on error. The fused kernel's dynamic-s_z grid barrier needs all
+ * of its CTAs resident at once (B <= 128 x the device's resident 4-CTA
+ * clusters); the environment variable GLAD_MLP_FUSED=0 disables it. Both
+ * paths give identical results. Not part of the reference interface.       */
+int glad_actor_mlp_fused(int64_t B, int act_mode);
 
 /* Allocation-free variant of glad_actor_forward. No counterpart in the
  * reference: it serves callers that cannot allocate device memory for this

@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -30,6 +31,9 @@ cudaError_t launch_act_scales(const float* slots, int act_mode, const float* con
 cudaError_t launch_requant_qlinear(const GladQLinearSrc* layers, int n, cudaStream_t st);
 cudaError_t launch_requant_qcnn(const GladQCNNSrc& s, cudaStream_t st);
 cudaError_t launch_cast_copy(const GladCastCopy* items, int n, cudaStream_t st);
+int mlp_max_tiles(int act_mode, cudaStream_t st);
+cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x, int64_t M, int64_t ldx,
+                       float* mean, int64_t ldm, float* slots, cudaStream_t st);
 }  // namespace glad
 
 using namespace glad;
@@ -148,6 +152,12 @@ struct ActorWs {
 };
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool use_fused_mlp(int64_t B, int act_mode, cudaStream_t st) {
+  const char* env = getenv("GLAD_MLP_FUSED");
+  if (env && env[0] == '0') return false;
+  return (B + 127) / 128 <= (int64_t)mlp_max_tiles(act_mode, st);
+}
 
 ActorWs actor_ws(void* base, int64_t B, int enc_width = kEnc) {
   ActorWs w;
@@ -433,8 +443,22 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st, true), "tail launch");
   stage_mark(3, st);
 
+  // Actor MLP: one fused kernel when the grid fits on the device at once (its
+  // dynamic-s_z grid barrier needs every CTA resident), else one GEMM per layer.
+  // GLAD_MLP_FUSED=0 selects the per-layer kernels.
+  bool fused_mlp = false;
+  if (mean_out) {
+    bool w_ok = true;
+    for (int i = 0; i < 4; ++i) w_ok = w_ok && aligned(w->mlp[i].w8, 16);
+    if (w_ok && use_fused_mlp(B, act_mode, st)) {
+      GLAD_CHECK_CUDA(launch_mlp(w->mlp, act_mode, enc, B, kEnc, mean_out, kActions, ws.slots, st),
+                      "fused actor MLP launch");
+      fused_mlp = true;
+      for (int i = 0; i < 4; ++i) stage_mark(4 + i, st);
+    }
+  }
   __half* hs[4] = {enc, ws.h1, ws.h2, ws.h3};
-  for (int i = 0; i < (mean_out ? 4 : 0); ++i) {
+  for (int i = 0; i < (mean_out && !fused_mlp ? 4 : 0); ++i) {
     GemmParams g{};
     g.L = w->mlp[i];
     g.act_mode = act_mode;
@@ -623,6 +647,17 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
     GLAD_CHECK_CUDA(le, "critic MLP launch");
   }
   return GLAD_OK;
+}
+
+int glad_actor_mlp_fused(int64_t B, int act_mode) {
+  g_err[0] = 0;
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown act_mode %d", act_mode);
+  DeviceInfo d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  return use_fused_mlp(B, act_mode, 0) ? 1 : 0;
 }
 
 int glad_actor_stage_events(void* const* events, int n) {

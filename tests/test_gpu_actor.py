@@ -109,3 +109,19 @@ def test_actor_batch_independence(dw):
     full, _ = actor_forward(dw, obs, "static", with_aux=False)
     part, _ = actor_forward(dw, obs[5:17].contiguous(), "static", with_aux=False)
     assert torch.equal(full[5:17], part)
+
+
+@pytest.mark.parametrize("mode", ["dynamic", "static"])
+@pytest.mark.parametrize("B", [5, 300, 4096])
+def test_fused_mlp_equals_per_layer_kernels(dw, mode, B, monkeypatch):
+    """The one-kernel actor MLP (clusters + grid barrier) and the one-GEMM-per-layer
+    path compute the same integers and the same roundings: means are identical."""
+    from rl_quant_b200 import _native as N
+    assert N.load().glad_actor_mlp_fused(B, N.ACT_MODES[mode]) == 1
+    obs = glad_obs(B, seed=31 + B).cuda()
+    fused, _ = actor_forward(dw, obs, mode, with_aux=False)
+    monkeypatch.setenv("GLAD_MLP_FUSED", "0")
+    assert N.load().glad_actor_mlp_fused(B, N.ACT_MODES[mode]) == 0
+    layered, _ = actor_forward(dw, obs, mode, with_aux=False)
+    assert torch.isfinite(fused).all()
+    assert torch.equal(fused, layered)
