@@ -24,7 +24,7 @@
 namespace glad {
 
 constexpr int kMlpCluster = 4;
-constexpr int kMlpThreads = 256;
+constexpr int kMlpThreads = 512;                 // 16 warps: 4 per TMEM lane quarter
 constexpr int kSlotBarrier = 16;                 // slots[16..18]: grid-barrier arrival counters
 
 // shared memory (bytes)
@@ -34,19 +34,22 @@ constexpr int kOffW0 = kOffA1 + 128 * 512;       // B slices [K/16][rows][16 B]:
 constexpr int kOffW1 = kOffW0 + 128 * 224;       //   64x512
 constexpr int kOffW2 = kOffW1 + 64 * 512;        //   32x256
 constexpr int kOffW3 = kOffW2 + 32 * 256;        //   32x128 (head, rank 0)
-constexpr int kOffF = kOffW3 + 32 * 128;         // float constants
+constexpr int kOffH = kOffW3 + 32 * 128;         // fp16 activations [16-col chunk][2][128 rows][8 halves]
+constexpr int kOffF = kOffH + 128 * 128 * 2;     // float constants
 constexpr int kFInA = 0;                         // [224] LET alpha / beta of layer 0's input
 constexpr int kFInB = 224;
-constexpr int kFSc = 448;                        // [256] s_w (dynamic) or dq_scale (static) per own column
+constexpr int kFSw = 448;                        // [256] s_w (dynamic) or dq_scale (static), own columns
 constexpr int kFBp = 704;                        // [256] b_prime
 constexpr int kFNa = 960;                        // [224] LET alpha / beta of the next layer, own columns
 constexpr int kFNb = 1184;
-constexpr int kFCount = 1408;
+constexpr int kFSc = 1408;                       // [256] output scale of the running layer
+constexpr int kFCount = 1664;
 constexpr int kOffBar = kOffF + kFCount * 4;
 constexpr int kMlpSmem = kOffBar + 64;
 constexpr uint32_t kMlpTmemCols = 128;
+static_assert(kMlpSmem + 128 <= 227 * 1024, "shared memory");
 
-// per-layer shape: K, own output columns, column base into the kFSc/kFBp/kFNa tables
+// per-layer shape: K, own output columns, column base into the per-column tables
 __host__ __device__ constexpr int mlp_k(int l) { return l == 0 ? 224 : l == 1 ? 512 : l == 2 ? 256 : 128; }
 __host__ __device__ constexpr int mlp_n(int l) { return l == 0 ? 512 : l == 1 ? 256 : l == 2 ? 128 : kActions; }
 __host__ __device__ constexpr int mlp_nj(int l) { return l == 0 ? 128 : l == 1 ? 64 : 32; }
@@ -76,67 +79,60 @@ __device__ __forceinline__ void mlp_load_w(uint8_t* dst, const int8_t* w8, int K
   }
 }
 
-// 16 fp16 values (two uint4) -> 16 int8 (one uint4) with per-column LET constants.
-__device__ __forceinline__ uint4 mlp_quant16(const uint32_t (&h)[8], const ActQuant& aq, const float* a,
-                                             const float* b) {
+// 16 fp16 values -> 16 int8 (one uint4) with per-column LET constants.
+__device__ __forceinline__ uint4 mlp_quant16(const uint4 v0, const uint4 v1, const ActQuant& aq,
+                                             const float* a, const float* b) {
+  const uint32_t h[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
   uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const __half2 h2 = *reinterpret_cast<const __half2*>(&h[j >> 1]);
-    const float x = (j & 1) ? __high2float(h2) : __low2float(h2);
-    const int q = aq.quant(x, a[j], b[j]);
-    w[j >> 2] |= (uint32_t)(q & 0xFF) << (8 * (j & 3));
+  for (int j = 0; j < 16; j += 4) {
+    const float4 a4 = *reinterpret_cast<const float4*>(a + j);
+    const float4 b4 = *reinterpret_cast<const float4*>(b + j);
+    const float2 x01 = __half22float2(*reinterpret_cast<const __half2*>(&h[j >> 1]));
+    const float2 x23 = __half22float2(*reinterpret_cast<const __half2*>(&h[(j >> 1) + 1]));
+    const int q0 = aq.quant(x01.x, a4.x, b4.x), q1 = aq.quant(x01.y, a4.y, b4.y);
+    const int q2 = aq.quant(x23.x, a4.z, b4.z), q3 = aq.quant(x23.y, a4.w, b4.w);
+    w[j >> 2] = (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
+                ((uint32_t)(q3 & 0xFF) << 24);
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-struct MlpCtx {
-  uint8_t* sm;
-  float* F;
-  uint64_t* mbar;
-  int* abort_flag;
-  uint32_t tmem;
-  uint32_t rank;
-  int tid, warp, lane, quarter, half, row;
-  int64_t m;
-  bool row_ok, dyn;
-  bool mma_timeout;        // this thread's last MMA wait ran out (the MMA may still be in flight)
-  uint32_t phase;
-};
-
-__device__ __forceinline__ void mlp_mma(MlpCtx& c, int abuf, int wbuf, int K, uint32_t idesc, int nj) {
-  if (c.tid == 0) {
+__device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mbar, uint32_t& phase,
+                                        int* abort_flag, bool& mma_timeout, int abuf, int wbuf, int K,
+                                        uint32_t idesc, int nj) {
+  if (threadIdx.x == 0) {
     tc_fence_after();
-    const uint32_t ab = smem_u32(c.sm + abuf), bb = smem_u32(c.sm + wbuf);
+    const uint32_t ab = smem_u32(sm + abuf), bb = smem_u32(sm + wbuf);
     for (int kc = 0; kc < K / 32; ++kc) {
       const uint64_t ad = smem_desc(ab + kc * 2 * 2048, 2048, 128);
       const uint64_t bd = smem_desc(bb + kc * 2 * nj * 16, nj * 16, 128);
-      mma_i8(c.tmem, ad, bd, idesc, kc > 0 ? 1u : 0u);
+      mma_i8(tmem, ad, bd, idesc, kc > 0 ? 1u : 0u);
     }
-    mma_commit(c.mbar);
+    mma_commit(mbar);
   }
-  if (!mbar_wait_bounded(c.mbar, c.phase)) {
-    *c.abort_flag = 1;
-    c.mma_timeout = true;
+  if (!mbar_wait_bounded(mbar, phase)) {
+    *abort_flag = 1;
+    mma_timeout = true;
   }
-  c.phase ^= 1;
+  phase ^= 1;
   tc_fence_after();
   __syncthreads();
 }
 
 // Grid-wide barrier on counter `ctr` (one arrival per CTA). The spin gives up
 // after 2 s (status bit, abort flag); an aborted CTA still arrives.
-__device__ __forceinline__ void mlp_grid_barrier(MlpCtx& c, uint32_t* ctr, uint32_t expected,
+__device__ __forceinline__ void mlp_grid_barrier(int* abort_flag, uint32_t* ctr, uint32_t expected,
                                                  uint32_t* status) {
   __syncthreads();
-  if (c.tid == 0) {
+  if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(ctr, 1u);
-    if (!*c.abort_flag) {
+    if (!*abort_flag) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_gpu(ctr) < expected) {
         if (global_timer_ns() - t0 > 2000000000ull) {
-          *c.abort_flag = 1;
+          *abort_flag = 1;
           atomicOr(status, kDevErrBarrierTimeout);
           break;
         }
@@ -148,133 +144,55 @@ __device__ __forceinline__ void mlp_grid_barrier(MlpCtx& c, uint32_t* ctr, uint3
   __syncthreads();
 }
 
-// Hidden layer l: MMA, epilogue (scale, bias, fp16, ELU), dynamic absmax of the
-// next layer's input, grid barrier, quantise own columns into every cluster
-// CTA's next A operand.
-template <int l>
-__device__ __forceinline__ void mlp_hidden(MlpCtx& c, const MlpParams& p, const ActQuant& aq,
-                                           ActQuant& aqn, uint32_t* status) {
-  constexpr int K = mlp_k(l), NJ = mlp_nj(l), CB = mlp_cb(l);
-  constexpr int kChunks = NJ / 32;               // 16-column chunks per thread (two column halves)
-  const bool run = !*c.abort_flag;
-  if (run) mlp_mma(c, mlp_abuf(l), mlp_wbuf(l), K, idesc_i8(128, NJ), NJ);
-  const bool ok = !*c.abort_flag;
-  const GladQLinear& Ln = p.L[l + 1];
-  const bool nlet = Ln.alpha != nullptr;
-  uint32_t hv[kChunks][8];
-  float zmax = 0.0f;
-  if (ok) {
-#pragma unroll
-    for (int ch = 0; ch < kChunks; ++ch) {
-      const int col0 = c.half * (NJ / 2) + ch * 16;
-      uint32_t r[16];
-      tmem_ld16(c.tmem + ((uint32_t)(32 * c.quarter) << 16) + col0, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 16; j += 2) {
-        __half h2v[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int lc = col0 + j + e;
-          const float sw = c.F[kFSc + CB + lc];
-          const float sc = c.dyn ? __fmul_rn(sw, aq.s) : sw;
-          const __half h = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + e], sc, c.F[kFBp + CB + lc])));
-          h2v[e] = h;
-          if (c.dyn && c.row_ok) {
-            const float x = __half2float(h);
-            zmax = fmaxf(zmax, nlet ? fabsf(__fadd_rn(__fmul_rn(x, c.F[kFNa + CB + lc]), c.F[kFNb + CB + lc]))
-                                    : fabsf(x));
-          }
-        }
-        __half2 pk = __halves2half2(h2v[0], h2v[1]);
-        hv[ch][j >> 1] = *reinterpret_cast<uint32_t*>(&pk);
-      }
-    }
-  }
-  tc_fence_before();
-  if (c.dyn) {
-    zmax = warp_max(zmax);
-    if (c.lane == 0 && zmax > 0.0f) atomic_max_nonneg(&p.slots[3 + l], zmax);
-    mlp_grid_barrier(c, reinterpret_cast<uint32_t*>(&p.slots[kSlotBarrier + l]), gridDim.x, status);
-    aqn.let = nlet;
-    aqn.dyn = true;
-    aqn.s = dyn_scale(ld_relaxed_gpu(&p.slots[3 + l]), nlet);
-    aqn.rcp = __fdiv_rn(1.0f, aqn.s);
-    aqn.inv = 0.0f;
-  } else {
-    aqn = make_act_quant(Ln, GLAD_ACT_STATIC, p.slots, 0);
-  }
-  if (!*c.abort_flag) {
-    const uint32_t abase = smem_u32(c.sm + mlp_abuf(l + 1));
-#pragma unroll
-    for (int ch = 0; ch < kChunks; ++ch) {
-      const int col0 = c.half * (NJ / 2) + ch * 16;
-      const uint4 q = mlp_quant16(hv[ch], aqn, &c.F[kFNa + CB + col0], &c.F[kFNb + CB + col0]);
-      const int kchunk = ((int)c.rank * NJ + col0) >> 4;     // K chunk of the next layer
-      const uint32_t off = abase + kchunk * 2048 + c.row * 16;
-#pragma unroll
-      for (int r = 0; r < kMlpCluster; ++r) st_cluster_v4(mapa_shared(off, r), q);
-    }
-  }
-  fence_async_cluster();
-  cluster_sync_all();
-}
-
 __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_constant__ MlpParams p) {
   extern __shared__ uint8_t smem_raw[];
-  MlpCtx c;
-  c.sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  c.F = reinterpret_cast<float*>(c.sm + kOffF);
-  c.mbar = reinterpret_cast<uint64_t*>(c.sm + kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c.sm + kOffBar + 8);
-  c.abort_flag = reinterpret_cast<int*>(c.sm + kOffBar + 12);
-  c.tid = threadIdx.x;
-  c.warp = c.tid >> 5;
-  c.lane = c.tid & 31;
-  c.quarter = c.warp & 3;
-  c.half = c.warp >> 2;
-  c.row = 32 * c.quarter + c.lane;
-  c.rank = cluster_ctarank();
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  float* F = reinterpret_cast<float*>(sm + kOffF);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffBar + 8);
+  int* abort_flag = reinterpret_cast<int*>(sm + kOffBar + 12);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, part = warp >> 2;   // TMEM lane quarter, column-chunk phase
+  const int row = 32 * quarter + lane;              // tile row of this thread in the epilogues
+  const uint32_t rank = cluster_ctarank();
   const int64_t m0 = (int64_t)(blockIdx.x / kMlpCluster) * 128;
-  c.m = m0 + c.row;
-  c.row_ok = c.m < p.M;
-  c.dyn = p.act_mode == GLAD_ACT_DYNAMIC;
-  c.phase = 0;
-  c.mma_timeout = false;
+  const int64_t m = m0 + row;
+  const bool row_ok = m < p.M;
+  const bool dyn = p.act_mode == GLAD_ACT_DYNAMIC;
   uint32_t* status = reinterpret_cast<uint32_t*>(&p.slots[kSlotStatus]);
-  const int tid = c.tid;
+  uint32_t phase = 0;
+  bool mma_timeout = false;
 
-  if (c.warp == 0) tmem_alloc(tmem_slot, kMlpTmemCols);
+  if (warp == 0) tmem_alloc(tmem_slot, kMlpTmemCols);
   if (tid == 0) {
-    mbar_init(c.mbar, 1);
+    mbar_init(mbar, 1);
     fence_mbar_init();
-    *c.abort_flag = 0;
+    *abort_flag = 0;
   }
   // weight slices of all four layers, in flight while the input is quantised
-  mlp_load_w(c.sm + kOffW0, p.L[0].w8, 224, (int)c.rank * 128, 128, tid);
-  mlp_load_w(c.sm + kOffW1, p.L[1].w8, 512, (int)c.rank * 64, 64, tid);
-  mlp_load_w(c.sm + kOffW2, p.L[2].w8, 256, (int)c.rank * 32, 32, tid);
-  if (c.rank == 0) mlp_load_w(c.sm + kOffW3, p.L[3].w8, 128, 0, 32, tid);
+  mlp_load_w(sm + kOffW0, p.L[0].w8, 224, (int)rank * 128, 128, tid);
+  mlp_load_w(sm + kOffW1, p.L[1].w8, 512, (int)rank * 64, 64, tid);
+  mlp_load_w(sm + kOffW2, p.L[2].w8, 256, (int)rank * 32, 32, tid);
+  if (rank == 0) mlp_load_w(sm + kOffW3, p.L[3].w8, 128, 0, 32, tid);
   cp_async_commit();
 
-  const ActQuant aq0 = make_act_quant(p.L[0], p.act_mode, p.slots, 2);
+  ActQuant aq = make_act_quant(p.L[0], p.act_mode, p.slots, 2);   // input of the running layer
   for (int k = tid; k < 224; k += kMlpThreads) {
-    c.F[kFInA + k] = aq0.let ? p.L[0].alpha[k] : 0.0f;
-    c.F[kFInB + k] = aq0.let ? p.L[0].beta[k] : 0.0f;
+    F[kFInA + k] = aq.let ? p.L[0].alpha[k] : 0.0f;
+    F[kFInB + k] = aq.let ? p.L[0].beta[k] : 0.0f;
   }
-#pragma unroll
   for (int l = 0; l < 4; ++l) {
     const GladQLinear& L = p.L[l];
-    const int nj = mlp_nj(l), n0 = l < 3 ? (int)c.rank * nj : 0;
+    const int nj = mlp_nj(l), n0 = l < 3 ? (int)rank * nj : 0;
     for (int j = tid; j < nj; j += kMlpThreads) {
       const int n = n0 + j;
       const bool in = n < mlp_n(l);
-      c.F[kFSc + mlp_cb(l) + j] = in ? (c.dyn ? L.s_w[n] : L.dq_scale[n]) : 0.0f;
-      c.F[kFBp + mlp_cb(l) + j] = in ? L.b_prime[n] : 0.0f;
+      F[kFSw + mlp_cb(l) + j] = in ? (dyn ? L.s_w[n] : L.dq_scale[n]) : 0.0f;
+      F[kFBp + mlp_cb(l) + j] = in ? L.b_prime[n] : 0.0f;
       if (l < 3) {
         const GladQLinear& Ln = p.L[l + 1];
-        c.F[kFNa + mlp_cb(l) + j] = Ln.alpha ? Ln.alpha[n] : 0.0f;
-        c.F[kFNb + mlp_cb(l) + j] = Ln.alpha ? Ln.beta[n] : 0.0f;
+        F[kFNa + mlp_cb(l) + j] = Ln.alpha ? Ln.alpha[n] : 0.0f;
+        F[kFNb + mlp_cb(l) + j] = Ln.alpha ? Ln.beta[n] : 0.0f;
       }
     }
   }
@@ -282,20 +200,19 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   tc_fence_before();
   cluster_sync_all();                            // every CTA of the cluster runs before DSMEM stores
   tc_fence_after();
-  c.tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
 
   // ---- layer 0 input: rank j quantises tile rows [32j, 32j+32) for the whole cluster ------
   {
-    const uint32_t abase = smem_u32(c.sm + kOffA0);
+    const uint32_t abase = smem_u32(sm + kOffA0);
     for (int it = tid; it < 32 * 14; it += kMlpThreads) {
-      const int rr = 32 * (int)c.rank + it / 14, kc = it % 14;
+      const int rr = 32 * (int)rank + it / 14, kc = it % 14;
       const int64_t mm = m0 + rr;
       uint4 q = make_uint4(0, 0, 0, 0);
       if (mm < p.M) {
         const uint4* src = reinterpret_cast<const uint4*>(p.x + mm * p.ldx + kc * 16);
-        const uint4 v0 = src[0], v1 = src[1];
-        const uint32_t h[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        q = mlp_quant16(h, aq0, &c.F[kFInA + kc * 16], &c.F[kFInB + kc * 16]);
+        q = mlp_quant16(src[0], src[1], aq, &F[kFInA + kc * 16], &F[kFInB + kc * 16]);
       }
       const uint32_t off = abase + kc * 2048 + rr * 16;
 #pragma unroll
@@ -307,44 +224,123 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   fence_async_cluster();
   cluster_sync_all();
 
-  ActQuant aq1, aq2, aq3;
-  mlp_hidden<0>(c, p, aq0, aq1, status);
-  mlp_hidden<1>(c, p, aq1, aq2, status);
-  mlp_hidden<2>(c, p, aq2, aq3, status);
+  // ---- hidden layers: MMA, epilogue to fp16 ELU (shared memory), absmax, grid barrier,
+  //      quantise own columns into every cluster CTA's next A operand --------------------------
+  uint4* H = reinterpret_cast<uint4*>(sm + kOffH);
+#pragma unroll 1
+  for (int l = 0; l < 3; ++l) {
+    const int NJ = mlp_nj(l), CB = mlp_cb(l), nch = NJ / 16;
+    for (int j = tid; j < NJ; j += kMlpThreads)
+      F[kFSc + CB + j] = dyn ? __fmul_rn(F[kFSw + CB + j], aq.s) : F[kFSw + CB + j];
+    if (!*abort_flag)
+      mlp_mma(sm, tmem, mbar, phase, abort_flag, mma_timeout, mlp_abuf(l), mlp_wbuf(l), mlp_k(l),
+              l == 0 ? idesc_i8(128, 128) : l == 1 ? idesc_i8(128, 64) : idesc_i8(128, 32), NJ);
+    const GladQLinear& Ln = p.L[l + 1];
+    const bool nlet = Ln.alpha != nullptr;
+    const bool want_max = dyn && row_ok;
+    float zmax = 0.0f;
+    if (!*abort_flag) {
+#pragma unroll 1
+      for (int ch = part; ch < nch; ch += 4) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + ch * 16, r);
+        tmem_ld_wait();
+        uint32_t h[8];
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          const int c = CB + ch * 16 + j;
+          const float4 sc = *reinterpret_cast<const float4*>(&F[kFSc + c]);
+          const float4 bp = *reinterpret_cast<const float4*>(&F[kFBp + c]);
+          const __half y0 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j], sc.x, bp.x)));
+          const __half y1 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + 1], sc.y, bp.y)));
+          const __half y2 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + 2], sc.z, bp.z)));
+          const __half y3 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + 3], sc.w, bp.w)));
+          const __half2 p01 = __halves2half2(y0, y1), p23 = __halves2half2(y2, y3);
+          h[j >> 1] = *reinterpret_cast<const uint32_t*>(&p01);
+          h[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&p23);
+          if (want_max) {
+            const float2 f01 = __half22float2(p01), f23 = __half22float2(p23);
+            if (nlet) {
+              const float4 na = *reinterpret_cast<const float4*>(&F[kFNa + c]);
+              const float4 nb = *reinterpret_cast<const float4*>(&F[kFNb + c]);
+              zmax = fmaxf(zmax, fabsf(__fadd_rn(__fmul_rn(f01.x, na.x), nb.x)));
+              zmax = fmaxf(zmax, fabsf(__fadd_rn(__fmul_rn(f01.y, na.y), nb.y)));
+              zmax = fmaxf(zmax, fabsf(__fadd_rn(__fmul_rn(f23.x, na.z), nb.z)));
+              zmax = fmaxf(zmax, fabsf(__fadd_rn(__fmul_rn(f23.y, na.w), nb.w)));
+            } else {
+              zmax = fmaxf(fmaxf(zmax, fmaxf(fabsf(f01.x), fabsf(f01.y))), fmaxf(fabsf(f23.x), fabsf(f23.y)));
+            }
+          }
+        }
+        H[(ch * 2) * 128 + row] = make_uint4(h[0], h[1], h[2], h[3]);
+        H[(ch * 2 + 1) * 128 + row] = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+    }
+    tc_fence_before();
+    if (dyn) {
+      zmax = warp_max(zmax);
+      if (lane == 0 && zmax > 0.0f) atomic_max_nonneg(&p.slots[3 + l], zmax);
+      mlp_grid_barrier(abort_flag, reinterpret_cast<uint32_t*>(&p.slots[kSlotBarrier + l]), gridDim.x,
+                       status);
+      aq.let = nlet;
+      aq.dyn = true;
+      aq.s = dyn_scale(ld_relaxed_gpu(&p.slots[3 + l]), nlet);
+      aq.rcp = __fdiv_rn(1.0f, aq.s);
+      aq.inv = 0.0f;
+    } else {
+      __syncthreads();
+      aq = make_act_quant(Ln, GLAD_ACT_STATIC, p.slots, 0);
+    }
+    if (!*abort_flag) {
+      const uint32_t abase = smem_u32(sm + mlp_abuf(l + 1));
+      const int kc0 = (int)rank * nch;             // first K chunk of the next layer owned here
+#pragma unroll 1
+      for (int it = tid; it < nch * 128; it += kMlpThreads) {
+        const int ch = it >> 7, rr = it & 127;
+        const uint4 q = mlp_quant16(H[(ch * 2) * 128 + rr], H[(ch * 2 + 1) * 128 + rr], aq,
+                                    &F[kFNa + CB + ch * 16], &F[kFNb + CB + ch * 16]);
+        const uint32_t off = abase + (kc0 + ch) * 2048 + rr * 16;
+#pragma unroll
+        for (int r = 0; r < kMlpCluster; ++r) st_cluster_v4(mapa_shared(off, r), q);
+      }
+    }
+    fence_async_cluster();
+    cluster_sync_all();
+  }
 
   // ---- head (rank 0): 128 x 32 (29 real) outputs, mean = float(fp16(y)) (qrt/integration.py:206)
-  if (c.rank == 0 && !*c.abort_flag) {
-    mlp_mma(c, mlp_abuf(3), mlp_wbuf(3), 128, idesc_i8(128, 32), 32);
-    if (!*c.abort_flag) {
-      const int col0 = c.half * 16;
+  if (rank == 0 && !*abort_flag) {
+    constexpr int CB = mlp_cb(3);
+    if (tid < 32) F[kFSc + CB + tid] = dyn ? __fmul_rn(F[kFSw + CB + tid], aq.s) : F[kFSw + CB + tid];
+    mlp_mma(sm, tmem, mbar, phase, abort_flag, mma_timeout, mlp_abuf(3), mlp_wbuf(3), 128,
+            idesc_i8(128, 32), 32);
+    if (!*abort_flag && part < 2) {
+      const int col0 = part * 16;
       uint32_t r[16];
-      tmem_ld16(c.tmem + ((uint32_t)(32 * c.quarter) << 16) + col0, r);
+      tmem_ld16(tmem + lane_base + col0, r);
       tmem_ld_wait();
-      if (c.row_ok) {
-        float* dst = p.mean + c.m * p.ldm;
+      if (row_ok) {
+        float* dst = p.mean + m * p.ldm;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = col0 + j;
-          if (n < kActions) {
-            const float sw = c.F[kFSc + mlp_cb(3) + n];
-            const float sc = c.dyn ? __fmul_rn(sw, aq3.s) : sw;
-            dst[n] = __half2float(qlinear_out((int32_t)r[j], sc, c.F[kFBp + mlp_cb(3) + n]));
-          }
+          if (n < kActions)
+            dst[n] = __half2float(qlinear_out((int32_t)r[j], F[kFSc + CB + n], F[kFBp + CB + n]));
         }
       }
     }
   }
 
   // ---- teardown ----------------------------------------------------------------------------
-  if (c.mma_timeout) {
-    mbar_wait_bounded(c.mbar, c.phase ^ 1);      // the MMA still in flight gets one more bounded wait
+  if (mma_timeout) {
+    mbar_wait_bounded(mbar, phase ^ 1);          // the MMA still in flight gets one more bounded wait
     atomicOr(status, kDevErrMmaTimeout);
   }
   tc_fence_before();
   cluster_sync_all();
-  if (c.warp == 0) {
+  if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(c.tmem, kMlpTmemCols);
+    tmem_dealloc(tmem, kMlpTmemCols);
   }
 }
 
