@@ -17,6 +17,7 @@ template <int MODE>
 cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl = false);
 size_t tail_smem_bytes();
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl = false);
+int tail_grid(int64_t B, int sms);
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
 template <int NT>
@@ -438,9 +439,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.topk_idx_out = ax.topk_idx;
   tp.attn_w_out = reinterpret_cast<__half*>(ax.attn_weights);
   tp.slots = ws.slots;
-  const int64_t groups = (B + 3) / 4;
-  const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
-  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st, true), "tail launch");
+  GLAD_CHECK_CUDA(launch_tail(tp, tail_grid(B, d.sms), st, true), "tail launch");
   stage_mark(3, st);
 
   // Actor MLP: one fused kernel when the grid fits on the device at once (its
@@ -616,9 +615,7 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   tp.topk_idx_out = ax.topk_idx;
   tp.attn_w_out = reinterpret_cast<__half*>(ax.attn_weights);
   tp.slots = ws.slots;
-  const int64_t groups = (B + 3) / 4;
-  const int tgrid = (int)(groups < (int64_t)d.sms * 2 ? groups : (int64_t)d.sms * 2);
-  GLAD_CHECK_CUDA(launch_tail(tp, tgrid, st, true), "tail launch");
+  GLAD_CHECK_CUDA(launch_tail(tp, tail_grid(B, d.sms), st, true), "tail launch");
 
   const __half* xs[4] = {enc, ws.h1, ws.h2, ws.h3};
   const int64_t lds[4] = {kCriticEnc, 512, 256, 128};

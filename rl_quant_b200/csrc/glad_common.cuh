@@ -169,6 +169,36 @@ __device__ __forceinline__ int reduce64_channel(int lane) {
          ((lane >> 1) & 1) * 4 + (lane & 1) * 2;
 }
 
+// 16 values -> warp sums: lanes L and L^16 end with the sum of channel L & 15.
+__device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? v[i] : v[i + 8];
+    const float keep = up ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 4;
+    const float send = up ? v[i] : v[i + 4];
+    const float keep = up ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 2;
+    const float send = up ? v[i] : v[i + 2];
+    const float keep = up ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  const bool up = lane & 1;
+  const float send = up ? v[0] : v[1];
+  const float keep = up ? v[1] : v[0];
+  const float r = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+  return r + __shfl_xor_sync(0xffffffffu, r, 16);
+}
+
 // ---- kernel parameter blocks -------------------------------------------------------
 enum FrontMode : int { kModeConv1 = 0, kModeConv2 = 1, kModeChain = 2, kModeFront = 3 };
 

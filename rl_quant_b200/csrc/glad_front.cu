@@ -165,36 +165,6 @@ __device__ __forceinline__ float warp_reduce32(float (&v)[32], int lane) {
   return keep + __shfl_xor_sync(0xffffffffu, send, 1);
 }
 
-// 16 values -> warp sums: lanes L and L^16 end with the sum of channel L & 15.
-__device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool up = lane & 8;
-    const float send = up ? v[i] : v[i + 8];
-    const float keep = up ? v[i + 8] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool up = lane & 4;
-    const float send = up ? v[i] : v[i + 4];
-    const float keep = up ? v[i + 4] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const bool up = lane & 2;
-    const float send = up ? v[i] : v[i + 2];
-    const float keep = up ? v[i + 2] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  const bool up = lane & 1;
-  const float send = up ? v[0] : v[1];
-  const float keep = up ? v[1] : v[0];
-  const float r = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-  return r + __shfl_xor_sync(0xffffffffu, r, 16);
-}
-
 template <int MODE>
 __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(const __grid_constant__ FrontParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -1131,19 +1101,20 @@ size_t front_smem_bytes() { return sizeof(FrontSmem) + 128; }
 
 template <int MODE>
 cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl) {
-  if (MODE == kModeFront) {
+  if constexpr (MODE == kModeFront) {
     // the fused forward's front runs the pipelined kernel
     static bool done_f[64] = {false};
     cudaError_t e = allow_max_smem((const void*)front_fused_kernel, done_f);
     if (e != cudaSuccess) return e;
     return launch_k(front_fused_kernel, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
                     pdl, p);
+  } else {
+    const size_t smem = front_smem_bytes();
+    static bool done[64] = {false};
+    cudaError_t e = allow_max_smem((const void*)front_kernel<MODE>, done);
+    if (e != cudaSuccess) return e;
+    return launch_k(front_kernel<MODE>, dim3(grid), dim3(kFrontThreads), smem, st, pdl, p);
   }
-  const size_t smem = front_smem_bytes();
-  static bool done[64] = {false};
-  cudaError_t e = allow_max_smem((const void*)front_kernel<MODE>, done);
-  if (e != cudaSuccess) return e;
-  return launch_k(front_kernel<MODE>, dim3(grid), dim3(kFrontThreads), smem, st, pdl, p);
 }
 
 template cudaError_t launch_front<kModeConv1>(const FrontParams&, int, cudaStream_t, bool);

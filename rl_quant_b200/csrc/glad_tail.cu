@@ -1,4 +1,4 @@
-// Encoder tail, four environments per CTA (one warp each):
+// Encoder tail, eight environments per CTA (one warp each):
 //   query = QuantLinear(cat(gc, proprio_emb))            qrt/encoder_opt.py:78-79
 //   score_query, top-32 of score_local + score_query     qrt/encoder_opt.py:82-95
 //   local features of the 32 selected tokens             (conv2 recomputed from z8)
@@ -8,34 +8,43 @@
 // The 187 local features are never stored: the front kernel keeps z8 (16 bytes
 // per token) and this kernel recomputes conv2 for the 32 selected tokens only
 // (identical integer arithmetic and epilogue, so identical fp16 values).
-// GEMM rows here are r = 32*warp + slot (M = 128 = 4 environments x 32 tokens).
+// GEMM rows are r = 32*warp + slot (M = 256 = 8 environments x 32 tokens, two
+// M=128 tiles: warps 0-3 and 4-7). The per-warp GEMVs read transposed weight
+// copies so that a warp's 32 lanes hit 32 different banks.
 #include <cuda_runtime.h>
 
 #include "glad_common.cuh"
 
 namespace glad {
 
-constexpr int kTailTmemCols = 256;   // [0,64) conv2 recompute, [64,192) K|V projection
+constexpr int kTailEnvs = 8;                 // environments per CTA (= warps)
+constexpr int kTailThreads = 32 * kTailEnvs;
+constexpr int kTailRows = 32 * kTailEnvs;    // GEMM rows per CTA
+constexpr int kTailTmemCols = 256;           // tile t: columns [128t, 128t+128): conv2, then K|V
 
 struct __align__(128) TailSmem {
   uint8_t w2s[5 * 2048];          // conv2 B operand (same layout as the front kernel)
-  uint8_t a1[10 * 2048];          // im2col rows of the selected tokens: [tap][row][16B]
-  uint8_t a2[8 * 2048];           // local features fp16: [k8 chunk][row][16B]
+  // im2col rows of the selected tokens [tap][row][16 B]; after the conv2 MMA the
+  // same bytes hold the local features (fp16) [k8 chunk][row][16 B]
+  uint8_t a12[10 * kTailRows * 16];
   uint8_t bkv[8 * 2048];          // in_proj rows 64..191 fp16: [k8 chunk][n][16B]
-  __half wq[64 * 64];             // in_proj rows 0..63
-  __half wo[64 * 64];             // out_proj
-  alignas(16) int8_t w8qp[64 * 128];
+  uint2 wqT[32 * 32];             // in_proj rows 0..63: [k pair][n pair] -> half2 (n even), half2 (n odd)
+  uint2 woT[32 * 32];             // out_proj, same layout
+  int2 w8qpT[32 * 32];            // query_projector int8: [k quad][n pair]
   float qp_a[128], qp_b[128];
   float qp_scale[64], qp_bp[64];
-  float dq[64], b2[64], a2c[64], c2[64];
+  alignas(16) float dq[64];
+  alignas(16) float b2[64];
+  alignas(16) float a2c[64];
+  alignas(16) float c2[64];
   float bin[192], bout[64];
   float wsq[64];                  // scorer weight, query half
   float a0_a[232], a0_b[232];
-  float qv[4][64];                // query (fp16 values)
-  float qm[4][64];                // MHA query projection (fp16 values)
-  float om[4][64];                // attention output (fp16 values)
-  uint32_t keys[4][32];
-  int sel[4][32];
+  float qv[kTailEnvs][64];        // query (fp16 values)
+  float qm[kTailEnvs][64];        // MHA query projection (fp16 values)
+  float om[kTailEnvs][64];        // attention output (fp16 values)
+  uint32_t keys[kTailEnvs][32];
+  int sel[kTailEnvs][32];
   uint64_t mbar;
   uint32_t tmem_base;
   int abort_flag;
@@ -47,11 +56,12 @@ __device__ __forceinline__ uint32_t ord16(__half h) {
   return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
 }
 
-__global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ TailParams p) {
+__global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_constant__ TailParams p) {
   extern __shared__ uint8_t smem_raw[];
   TailSmem& s = *reinterpret_cast<TailSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NT = kTailThreads;
 
   grid_dep_launch();
   if (warp == 0) tmem_alloc(&s.tmem_base, kTailTmemCols);
@@ -61,28 +71,32 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     s.abort_flag = 0;
   }
   // ---- constants -------------------------------------------------------------------
-  for (int idx = tid; idx < 5 * 2048; idx += 128) {
+  for (int idx = tid; idx < 5 * 2048; idx += NT) {
     const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
     const int q = 2 * pr + c;
     s.w2s[idx] = q < 9 ? (uint8_t)p.conv.w8[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
   }
-  for (int idx = tid; idx < 2048 / 16; idx += 128)
-    reinterpret_cast<uint4*>(s.a1 + 9 * 2048)[idx] = make_uint4(0, 0, 0, 0);
-  for (int idx = tid; idx < 128 * 64 / 8; idx += 128) {
+  for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9
+    reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
+  for (int idx = tid; idx < 128 * 64 / 8; idx += NT) {
     // bkv[c][n][8 halves] <- in_proj_weight[64 + n][8c .. 8c+8)
     const int n = idx >> 3, c = idx & 7;
     reinterpret_cast<uint4*>(s.bkv)[c * 128 + n] =
         reinterpret_cast<const uint4*>(p.in_w + (64 + n) * 64)[c];
   }
-  for (int idx = tid; idx < 64 * 64 / 8; idx += 128) {
-    reinterpret_cast<uint4*>(s.wq)[idx] = reinterpret_cast<const uint4*>(p.in_w)[idx];
-    reinterpret_cast<uint4*>(s.wo)[idx] = reinterpret_cast<const uint4*>(p.out_w)[idx];
+  for (int idx = tid; idx < 32 * 32; idx += NT) {
+    // [k pair c2][n pair np]: (W[2np][2c2..], W[2np+1][2c2..]) as two half2
+    const int c2 = idx >> 5, np = idx & 31;
+    const uint32_t* wi = reinterpret_cast<const uint32_t*>(p.in_w);
+    const uint32_t* wo = reinterpret_cast<const uint32_t*>(p.out_w);
+    s.wqT[idx] = make_uint2(wi[(2 * np) * 32 + c2], wi[(2 * np + 1) * 32 + c2]);
+    s.woT[idx] = make_uint2(wo[(2 * np) * 32 + c2], wo[(2 * np + 1) * 32 + c2]);
+    const int* w8 = reinterpret_cast<const int*>(p.qp.w8);
+    s.w8qpT[idx] = make_int2(w8[(2 * np) * 32 + c2], w8[(2 * np + 1) * 32 + c2]);
   }
-  for (int idx = tid; idx < 64 * 128 / 16; idx += 128)
-    reinterpret_cast<uint4*>(s.w8qp)[idx] = reinterpret_cast<const uint4*>(p.qp.w8)[idx];
   grid_dep_wait();                      // outputs of the front kernel are visible from here
   const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
-  for (int k = tid; k < 128; k += 128) {
+  for (int k = tid; k < 128; k += NT) {
     s.qp_a[k] = aq.let ? p.qp.alpha[k] : 0.0f;
     s.qp_b[k] = aq.let ? p.qp.beta[k] : 0.0f;
   }
@@ -96,10 +110,10 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     s.bout[tid] = __half2float(p.out_b[tid]);
     s.wsq[tid] = __half2float(p.scorer_w[64 + tid]);
   }
-  for (int k = tid; k < 192; k += 128) s.bin[k] = __half2float(p.in_b[k]);
+  for (int k = tid; k < 192; k += NT) s.bin[k] = __half2float(p.in_b[k]);
   const bool a0_let = p.a0_alpha != nullptr;
   const int enc_w = 128 + p.prop_dim;
-  for (int k = tid; k < enc_w; k += 128) {
+  for (int k = tid; k < enc_w; k += NT) {
     s.a0_a[k] = a0_let ? p.a0_alpha[k] : 0.0f;
     s.a0_b[k] = a0_let ? p.a0_beta[k] : 0.0f;
   }
@@ -109,15 +123,16 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
-  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  const int tile = warp >> 2;
+  const uint32_t tcol = tmem + tile * 128 + ((uint32_t)(32 * (warp & 3)) << 16);
   uint32_t phase = 0;
   float zmax_a0 = 0.0f;
   ActQuant aq_a0{};
   aq_a0.let = a0_let;
 
-  const int64_t ngroups = (p.B + 3) / 4;
+  const int64_t ngroups = (p.B + kTailEnvs - 1) / kTailEnvs;
   for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x) {
-    const int64_t env = g * 4 + warp;
+    const int64_t env = g * kTailEnvs + warp;
     const bool have = env < p.B;
     const int r = 32 * warp + lane;              // GEMM row of this thread
     if (have) {
@@ -132,13 +147,12 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
         qword |= (uint32_t)(aq.quant(x, s.qp_a[k], s.qp_b[k]) & 0xFF) << (8 * b);
       }
       int acc0 = 0, acc1 = 0;
-      const int* w0 = reinterpret_cast<const int*>(s.w8qp + (2 * lane) * 128);
-      const int* w1 = reinterpret_cast<const int*>(s.w8qp + (2 * lane + 1) * 128);
 #pragma unroll
       for (int w = 0; w < 32; ++w) {
         const int qw = (int)__shfl_sync(0xffffffffu, qword, w);
-        acc0 = __dp4a(qw, w0[w], acc0);
-        acc1 = __dp4a(qw, w1[w], acc1);
+        const int2 wv = s.w8qpT[w * 32 + lane];
+        acc0 = __dp4a(qw, wv.x, acc0);
+        acc1 = __dp4a(qw, wv.y, acc1);
       }
       const float q0 = __half2float(qlinear_out(acc0, s.qp_scale[2 * lane], s.qp_bp[2 * lane]));
       const float q1 = __half2float(qlinear_out(acc1, s.qp_scale[2 * lane + 1], s.qp_bp[2 * lane + 1]));
@@ -148,19 +162,22 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
       const float sqp = warp_sum(fmaf(q1, s.wsq[2 * lane + 1], q0 * s.wsq[2 * lane]));
       const float sq = fp16r(__fadd_rn(fp16r(sqp), sb));
       __syncwarp();
-      // MHA query projection: q_mha = fp16(fp16(query @ Wq^T) + b_q)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = 2 * lane + h;
-        float a = 0.0f;
-        const __half2* wr = reinterpret_cast<const __half2*>(s.wq + n * 64);
+      // MHA query projection: q_mha = fp16(fp16(query @ Wq^T) + b_q); lane -> n = 2*lane, 2*lane+1
+      {
+        float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
         for (int c2 = 0; c2 < 32; ++c2) {
-          const float2 w = __half22float2(wr[c2]);
-          a = fmaf(s.qv[warp][2 * c2], w.x, a);
-          a = fmaf(s.qv[warp][2 * c2 + 1], w.y, a);
+          const uint2 wv = s.wqT[c2 * 32 + lane];
+          const float x0 = s.qv[warp][2 * c2], x1 = s.qv[warp][2 * c2 + 1];
+          const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+          const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+          a0 = fmaf(x0, w0.x, a0);
+          a0 = fmaf(x1, w0.y, a0);
+          a1 = fmaf(x0, w1.x, a1);
+          a1 = fmaf(x1, w1.y, a1);
         }
-        s.qm[warp][n] = fp16r(__fadd_rn(fp16r(a), s.bin[n]));
+        s.qm[warp][2 * lane] = fp16r(__fadd_rn(fp16r(a0), s.bin[2 * lane]));
+        s.qm[warp][2 * lane + 1] = fp16r(__fadd_rn(fp16r(a1), s.bin[2 * lane + 1]));
       }
       // ---- 3. top-32 over 187 logits, value desc / index asc ------------------------------
       uint32_t key[6];
@@ -209,7 +226,7 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
 #pragma unroll
       for (int q = 0; q < 9; ++q) {
         const int ih = oh + q / 3 - 1, iw = ow + q % 3 - 1;
-        uint8_t* dst = s.a1 + q * 2048 + r * 16;
+        uint8_t* dst = s.a12 + q * (kTailRows * 16) + r * 16;
         if (ih >= 0 && ih < kH2 && iw >= 0 && iw < kW2)
           cp_async16(dst, p.z8 + (env * kTok + ih * kW2 + iw) * 16);
         else
@@ -218,24 +235,27 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     } else {
 #pragma unroll
       for (int q = 0; q < 9; ++q)
-        *reinterpret_cast<uint4*>(s.a1 + q * 2048 + r * 16) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(s.a12 + q * (kTailRows * 16) + r * 16) = make_uint4(0, 0, 0, 0);
     }
     cp_async_commit();
     cp_async_wait_all();
     fence_async_smem();
+    tc_fence_before();
     __syncthreads();
 
-    // ---- 5. conv2 recompute for the 128 selected rows ------------------------------------
+    // ---- 5. conv2 recompute for the 256 selected rows (two M=128 tiles) -------------------
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t ab = smem_u32(s.a1), wb = smem_u32(s.w2s);
+      const uint32_t ab = smem_u32(s.a12), wb = smem_u32(s.w2s);
       constexpr uint32_t idesc = idesc_i8(128, 64);
 #pragma unroll
-      for (int pr = 0; pr < 5; ++pr) {
-        const uint64_t ad = smem_desc(ab + pr * 2 * 2048, 2048, 128);
-        const uint64_t bd = smem_desc(wb + pr * 2048, 1024, 128);
-        mma_i8(tmem, ad, bd, idesc, pr > 0 ? 1u : 0u);
-      }
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int pr = 0; pr < 5; ++pr) {
+          const uint64_t ad = smem_desc(ab + pr * 2 * (kTailRows * 16) + t * 2048, kTailRows * 16, 128);
+          const uint64_t bd = smem_desc(wb + pr * 2048, 1024, 128);
+          mma_i8(tmem + t * 128, ad, bd, idesc, pr > 0 ? 1u : 0u);
+        }
       mma_commit(&s.mbar);
     }
     bool ok = mbar_wait_bounded(&s.mbar, phase);
@@ -245,36 +265,49 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     __syncthreads();
     if (s.abort_flag) break;
 
-    // ---- 6. local features (fp16) -> A operand of the K|V projection ---------------------
+    // ---- 6. local features (fp16) -> A operand of the K|V projection (over the im2col bytes)
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       uint32_t rr[16];
-      tmem_ld16(tmem + lane_base + cb * 16, rr);
+      tmem_ld16(tcol + cb * 16, rr);
       tmem_ld_wait();
-      __half h[16];
+      uint32_t hw[8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 16; j += 4) {
         const int c = cb * 16 + j;
-        h[j] = conv2_out((int32_t)rr[j], s.dq[c], s.b2[c], s.a2c[c], s.c2[c]);
+        const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
+        const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
+        const float4 a24 = *reinterpret_cast<const float4*>(&s.a2c[c]);
+        const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
+        const __half2 h01 = __halves2half2(conv2_out((int32_t)rr[j], dq4.x, b24.x, a24.x, c24.x),
+                                           conv2_out((int32_t)rr[j + 1], dq4.y, b24.y, a24.y, c24.y));
+        const __half2 h23 = __halves2half2(conv2_out((int32_t)rr[j + 2], dq4.z, b24.z, a24.z, c24.z),
+                                           conv2_out((int32_t)rr[j + 3], dq4.w, b24.w, a24.w, c24.w));
+        hw[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
+        hw[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
       }
-      *reinterpret_cast<uint4*>(s.a2 + (2 * cb) * 2048 + r * 16) = *reinterpret_cast<uint4*>(&h[0]);
-      *reinterpret_cast<uint4*>(s.a2 + (2 * cb + 1) * 2048 + r * 16) = *reinterpret_cast<uint4*>(&h[8]);
+      *reinterpret_cast<uint4*>(s.a12 + (2 * cb) * (kTailRows * 16) + r * 16) =
+          make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(s.a12 + (2 * cb + 1) * (kTailRows * 16) + r * 16) =
+          make_uint4(hw[4], hw[5], hw[6], hw[7]);
     }
     tc_fence_before();
     fence_async_smem();
     __syncthreads();
 
-    // ---- 7. K|V = local @ in_proj[64:192]^T (fp32 accumulate in TMEM) -------------------
+    // ---- 7. K|V = local @ in_proj[64:192]^T (fp32 accumulate in TMEM, over conv2's columns)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t ab = smem_u32(s.a2), bb = smem_u32(s.bkv);
+      const uint32_t ab = smem_u32(s.a12), bb = smem_u32(s.bkv);
       constexpr uint32_t idesc = idesc_f16(128, 128);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t ad = smem_desc(ab + kk * 2 * 2048, 2048, 128);
-        const uint64_t bd = smem_desc(bb + kk * 2 * 2048, 2048, 128);
-        mma_f16(tmem + 64, ad, bd, idesc, kk > 0 ? 1u : 0u);
-      }
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = smem_desc(ab + kk * 2 * (kTailRows * 16) + t * 2048, kTailRows * 16, 128);
+          const uint64_t bd = smem_desc(bb + kk * 2 * 2048, 2048, 128);
+          mma_f16(tmem + t * 128, ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
       mma_commit(&s.mbar);
     }
     ok = mbar_wait_bounded(&s.mbar, phase);
@@ -284,66 +317,73 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     __syncthreads();
     if (s.abort_flag) break;
 
-    // ---- 8. attention: thread = (env, token slot) --------------------------------------
-    float kf[64], vf[64];
+    // ---- 8. attention: thread = (env, token slot), 16 channels (4 heads) at a time ------------
+    float sc[kHeads];
 #pragma unroll
-    for (int cb = 0; cb < 8; ++cb) {
+    for (int cb = 0; cb < 4; ++cb) {
       uint32_t rr[16];
-      tmem_ld16(tmem + lane_base + 64 + cb * 16, rr);
+      tmem_ld16(tcol + cb * 16, rr);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int c = cb * 16 + j;             // 0..127: K then V
-        const float v = fp16r(__fadd_rn(fp16r(__uint_as_float(rr[j])), s.bin[64 + c]));
-        if (c < 64) kf[c] = v; else vf[c - 64] = v;
+      for (int hh = 0; hh < 4; ++hh) {
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 16 * cb + 4 * hh + e;
+          const float kv = fp16r(__fadd_rn(fp16r(__uint_as_float(rr[4 * hh + e])), s.bin[64 + c]));
+          d = fmaf(s.qm[warp][c], kv, d);
+        }
+        sc[4 * cb + hh] = fp16r(__fmul_rn(fp16r(d), 0.5f));
       }
     }
-    tc_fence_before();
     float asum = 0.0f;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) {
-      float d = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) d = fmaf(s.qm[warp][4 * h + e], kf[4 * h + e], d);
-      const float sc = fp16r(__fmul_rn(fp16r(d), 0.5f));
-      const float mx = warp_max(sc);
-      const float ex = expf(sc - mx);
+      const float mx = warp_max(sc[h]);
+      const float ex = expf(sc[h] - mx);
       const float sm = warp_sum(ex);
       const float a = fp16r(__fdiv_rn(ex, sm));
       asum += a;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vf[4 * h + e] = a * vf[4 * h + e];
+      sc[h] = a;
     }
     if (have && p.attn_w_out) p.attn_w_out[env * kTopK + lane] = __float2half_rn(asum / 16.0f);
-    warp_reduce64(vf, lane);
-    {
-      const int c0 = reduce64_channel(lane);
-      s.om[warp][c0] = fp16r(vf[0]);
-      s.om[warp][c0 + 1] = fp16r(vf[1]);
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      uint32_t rr[16];
+      tmem_ld16(tcol + 64 + cb * 16, rr);
+      tmem_ld_wait();
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = 16 * cb + j;
+        v[j] = sc[4 * cb + (j >> 2)] * fp16r(__fadd_rn(fp16r(__uint_as_float(rr[j])), s.bin[128 + c]));
+      }
+      const float o = warp_reduce16(v, lane);    // lanes L, L^16: channel 16*cb + (L & 15)
+      if (lane < 16) s.om[warp][16 * cb + lane] = fp16r(o);
     }
+    tc_fence_before();
     __syncwarp();
     // ---- 9. foothold = out_proj(o), encoded[:, 0:64] ---------------------------------------
     if (have) {
-      float f2[2];
+      float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = 2 * lane + h;
-        float a = 0.0f;
-        const __half2* wr = reinterpret_cast<const __half2*>(s.wo + n * 64);
-#pragma unroll
-        for (int c2 = 0; c2 < 32; ++c2) {
-          const float2 w = __half22float2(wr[c2]);
-          a = fmaf(s.om[warp][2 * c2], w.x, a);
-          a = fmaf(s.om[warp][2 * c2 + 1], w.y, a);
-        }
-        f2[h] = fp16r(__fadd_rn(fp16r(a), s.bout[n]));
+      for (int c2 = 0; c2 < 32; ++c2) {
+        const uint2 wv = s.woT[c2 * 32 + lane];
+        const float x0 = s.om[warp][2 * c2], x1 = s.om[warp][2 * c2 + 1];
+        const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+        const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+        a0 = fmaf(x0, w0.x, a0);
+        a0 = fmaf(x1, w0.y, a0);
+        a1 = fmaf(x0, w1.x, a1);
+        a1 = fmaf(x1, w1.y, a1);
       }
-      __half2 fh = __floats2half2_rn(f2[0], f2[1]);
-      reinterpret_cast<__half2*>(p.enc + env * p.ld_enc)[lane] = fh;
+      const float f0 = fp16r(__fadd_rn(fp16r(a0), s.bout[2 * lane]));
+      const float f1 = fp16r(__fadd_rn(fp16r(a1), s.bout[2 * lane + 1]));
+      reinterpret_cast<__half2*>(p.enc + env * p.ld_enc)[lane] = __floats2half2_rn(f0, f1);
       if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
         // |alpha*encoded + beta| for actor.0's dynamic s_z
-        float zm = fmaxf(aq_a0.absz(f2[0], s.a0_a[2 * lane], s.a0_b[2 * lane]),
-                         aq_a0.absz(f2[1], s.a0_a[2 * lane + 1], s.a0_b[2 * lane + 1]));
+        float zm = fmaxf(aq_a0.absz(f0, s.a0_a[2 * lane], s.a0_b[2 * lane]),
+                         aq_a0.absz(f1, s.a0_a[2 * lane + 1], s.a0_b[2 * lane + 1]));
         for (int k = 64 + lane; k < enc_w; k += 32)
           zm = fmaxf(zm, aq_a0.absz(__half2float(p.enc[env * p.ld_enc + k]), s.a0_a[k], s.a0_b[k]));
         zmax_a0 = fmaxf(zmax_a0, zm);
@@ -357,7 +397,7 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
     if (lane == 0 && m > 0.0f) atomic_max_nonneg(&p.slots[2], m);
   }
   if (s.abort_flag) {
-    mbar_wait_bounded(&s.mbar, phase);
+    mbar_wait_bounded(&s.mbar, phase ^ 1);
     if (tid == 0) atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrMmaTimeout);
   }
   tc_fence_before();
@@ -370,12 +410,18 @@ __global__ void __launch_bounds__(128, 2) tail_kernel(const __grid_constant__ Ta
 
 size_t tail_smem_bytes() { return sizeof(TailSmem) + 128; }
 
+// Persistent grid: one CTA per group of environments, at most two per SM.
+int tail_grid(int64_t B, int sms) {
+  const int64_t groups = (B + kTailEnvs - 1) / kTailEnvs;
+  return (int)(groups < (int64_t)sms * 2 ? groups : (int64_t)sms * 2);
+}
+
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl) {
   const size_t smem = tail_smem_bytes();
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)tail_kernel, done);
   if (e != cudaSuccess) return e;
-  return launch_k(tail_kernel, dim3(grid), dim3(128), smem, st, pdl, p);
+  return launch_k(tail_kernel, dim3(grid), dim3(kTailThreads), smem, st, pdl, p);
 }
 
 }  // namespace glad
