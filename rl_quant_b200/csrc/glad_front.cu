@@ -645,11 +645,12 @@ struct __align__(128) FusedSmem {
   alignas(16) float b2[64];
   alignas(16) float a2[64];
   alignas(16) float c2[64];
-  alignas(16) float wg[64];
-  alignas(16) float ws[64];
-  float2 lpart[2][2][128];
-  __half wt16[2][128];
-  float pool[2][4][64];
+  // fp16 local features of one environment [tile][8-channel chunk][128 rows][16 B]:
+  // A operand (K-major) of the logits GEMM and (M-major) of the pooling GEMM
+  alignas(128) uint8_t local16[2 * 8 * 128 * 16];
+  alignas(128) uint8_t blog[8 * 16 * 16];     // logits B: [chunk][n: gps, scorer, 0...][16 B]
+  alignas(128) uint8_t bpool[16 * 16 * 16];   // pooling B: [8-row chunk][n: tile 0, tile 1, 0...][16 B]
+  float poolv[128];                           // pooled partial sums, row = tile*64 + channel
   float wmax[8], wsum[8];
   __half prop16[2][128];
   __half pe16[2][64];
@@ -663,7 +664,11 @@ struct __align__(128) FusedSmem {
   uint64_t c1_bdesc[8];
   uint64_t c2_adesc[10];               // [tile*5 + K-step]
   uint64_t c2_bdesc[5];
-  uint64_t bar1, bar2;                 // conv1 / conv2 completion
+  uint64_t lg_adesc[2][4];             // logits GEMM [tile][K-step]
+  uint64_t lg_bdesc[4];
+  uint64_t pl_adesc[8];                // pooling GEMM [K-step]
+  uint64_t pl_bdesc[8];
+  uint64_t bar1, bar2;                 // conv1 / (conv2, logits, pooling) completion
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -719,9 +724,16 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       s.b2[tid] = p.conv.b2f[tid];
       s.a2[tid] = p.conv.a2[tid];
       s.c2[tid] = p.conv.c2[tid];
-      s.wg[tid] = __half2float(p.gps_w[tid]);
-      s.ws[tid] = __half2float(p.scorer_w[tid]);
     }
+    // logits B operand: row 0 = global_pool_selector weight, row 1 = scorer weight (local half)
+    for (int idx = tid; idx < 8 * 16 * 8; idx += NT) {
+      const int c = idx >> 7, n = (idx >> 3) & 15, e = idx & 7;
+      __half v = __float2half(0.0f);
+      if (n == 0) v = p.gps_w[8 * c + e];
+      if (n == 1) v = p.scorer_w[8 * c + e];
+      reinterpret_cast<__half*>(s.blog)[idx] = v;
+    }
+    for (int i = tid; i < 16 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.bpool)[i] = make_uint4(0, 0, 0, 0);
   }
   const int P = p.prop_dim;
   grid_dep_wait();
@@ -768,6 +780,17 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         s.c2_adesc[t * 5 + pr] = smem_desc(sb + (t * 128 + o0) * 16, (o1 - o0) * 16, 128);
       }
     for (int pr = 0; pr < 5; ++pr) s.c2_bdesc[pr] = smem_desc(smem_u32(s.w2s) + pr * 2048, 1024, 128);
+    // logits: A = local16 tile t, K-major (chunk stride 2048 B, 8-row groups 128 B)
+    const uint32_t lb = smem_u32(s.local16);
+    for (int t = 0; t < 2; ++t)
+      for (int kk = 0; kk < 4; ++kk) s.lg_adesc[t][kk] = smem_desc(lb + t * 16384 + kk * 2 * 2048, 2048, 128);
+    for (int kk = 0; kk < 4; ++kk) s.lg_bdesc[kk] = smem_desc(smem_u32(s.blog) + kk * 2 * 256, 256, 128);
+    // pooling: A = local16 read M-major (M = tile*64 + channel: 8-channel blocks 2048 B apart,
+    // K = row: 8-row blocks 128 B apart), B = softmax weights, K-major
+    for (int kk = 0; kk < 8; ++kk) {
+      s.pl_adesc[kk] = smem_desc(lb + kk * 256, 128, 2048);
+      s.pl_bdesc[kk] = smem_desc(smem_u32(s.bpool) + kk * 2 * 256, 256, 128);
+    }
   }
   fence_async_smem();
   tc_fence_before();
@@ -944,63 +967,75 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     __syncthreads();
     if (s.abort_flag) break;
 
-    uint32_t loc[2][16];
-    const int c0 = 32 * half;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    // fp16 local features -> local16 (operand of the logits and pooling GEMMs)
+    {
+      const int c0 = 32 * half;
       const int i = 32 * quarter + lane;
-      if (t * 128 + 32 * quarter < 11 * kStripCols) {
-        float l0 = 0.0f, l1 = 0.0f;
 #pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          uint32_t r[16];
-          tmem_ld16(tmem + lane_base + t * 64 + c0 + 16 * hb, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const int c = c0 + 16 * hb + j;
-            const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
-            const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
-            const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
-            const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
-            const float y0 = conv2_val((int32_t)r[j], dq4.x, b24.x, a24.x, c24.x);
-            const float y1 = conv2_val((int32_t)r[j + 1], dq4.y, b24.y, a24.y, c24.y);
-            const float y2 = conv2_val((int32_t)r[j + 2], dq4.z, b24.z, a24.z, c24.z);
-            const float y3 = conv2_val((int32_t)r[j + 3], dq4.w, b24.w, a24.w, c24.w);
-            __half2 h01 = __floats2half2_rn(y0, y1), h23 = __floats2half2_rn(y2, y3);
-            loc[t][8 * hb + (j >> 1)] = *reinterpret_cast<uint32_t*>(&h01);
-            loc[t][8 * hb + (j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h23);
-            const float4 wg4 = *reinterpret_cast<const float4*>(&s.wg[c]);
-            const float4 ws4 = *reinterpret_cast<const float4*>(&s.ws[c]);
-            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-            l0 = fmaf(f01.x, wg4.x, l0);
-            l0 = fmaf(f01.y, wg4.y, l0);
-            l0 = fmaf(f23.x, wg4.z, l0);
-            l0 = fmaf(f23.y, wg4.w, l0);
-            l1 = fmaf(f01.x, ws4.x, l1);
-            l1 = fmaf(f01.y, ws4.y, l1);
-            l1 = fmaf(f23.x, ws4.z, l1);
-            l1 = fmaf(f23.y, ws4.w, l1);
-          }
-        }
-        s.lpart[t][half][i] = make_float2(l0, l1);
-        if (p.feat_out) {
+      for (int t = 0; t < 2; ++t) {
+        uint8_t* lrow = s.local16 + t * 16384 + i * 16;
+        if (t * 128 + 32 * quarter < 11 * kStripCols) {
           const int m = t * 128 + i;
           const int oh = m / kStripCols, ow = m - oh * kStripCols;
-          if (oh < kH2 && ow < kW2) {
-            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh * kW2 + ow) * kD + c0);
+          const bool valid = oh < kH2 && ow < kW2;
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              dst[q4] = make_uint4(loc[t][4 * q4], loc[t][4 * q4 + 1], loc[t][4 * q4 + 2], loc[t][4 * q4 + 3]);
+          for (int hb = 0; hb < 2; ++hb) {
+            uint32_t r[16];
+            tmem_ld16(tmem + lane_base + t * 64 + c0 + 16 * hb, r);
+            tmem_ld_wait();
+            uint32_t hw[8];
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const int c = c0 + 16 * hb + j;
+              const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
+              const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
+              const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
+              const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
+              const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)r[j], dq4.x, b24.x, a24.x, c24.x),
+                                                    conv2_val((int32_t)r[j + 1], dq4.y, b24.y, a24.y, c24.y));
+              const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)r[j + 2], dq4.z, b24.z, a24.z, c24.z),
+                                                    conv2_val((int32_t)r[j + 3], dq4.w, b24.w, a24.w, c24.w));
+              hw[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
+              hw[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+            }
+            const int ch = (c0 + 16 * hb) >> 3;
+            const uint4 v0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            const uint4 v1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            *reinterpret_cast<uint4*>(lrow + ch * 2048) = v0;
+            *reinterpret_cast<uint4*>(lrow + (ch + 1) * 2048) = v1;
+            if (valid && p.feat_out) {
+              uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh * kW2 + ow) * kD + c0 + 16 * hb);
+              dst[0] = v0;
+              dst[1] = v1;
+            }
           }
-        }
-      } else {
+        } else {
+          // rows past the grid: zero (their pooling weight is 0, the operand must be finite)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) loc[t][j] = 0;
+          for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<uint4*>(lrow + ((c0 >> 3) + k) * 2048) = make_uint4(0, 0, 0, 0);
+        }
       }
     }
     tc_fence_before();
+    fence_async_smem();
     __syncthreads();
+    // logits of both heads for every row: [gps, scorer-local] = local @ [w_g; w_s]^T (fp32 in TMEM)
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16(128, 16);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16(tmem + 160 + 16 * t, s.lg_adesc[t][kk], s.lg_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+      mma_commit(&s.bar2);
+    }
+    if (!mbar_wait_bounded(&s.bar2, ph2)) s.abort_flag = 1;
+    ph2 ^= 1;
+    tc_fence_after();
+    __syncthreads();
+    if (s.abort_flag) break;
     // logits (qrt/encoder_opt.py:69-73) and the softmax over the 187 tokens (:75)
     float my_logit;
     int my_tok = -1;
@@ -1008,15 +1043,20 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       const int t = half, i = 32 * quarter + lane;
       const int m = t * 128 + i;
       const int oh = m / kStripCols, ow = m - oh * kStripCols;
+      uint32_t l0 = 0, l1 = 0;
+      if (t * 128 + 32 * quarter < 11 * kStripCols) {
+        tmem_ld2(tmem + lane_base + 160 + 16 * t, l0, l1);
+        tmem_ld_wait();
+      }
       float g = -INFINITY;
       if (oh < kH2 && ow < kW2) {
         my_tok = oh * kW2 + ow;
-        const float2 a = s.lpart[t][0][i], c = s.lpart[t][1][i];
-        g = fp16r(__fadd_rn(fp16r(a.x + c.x), gb));
-        p.score_local[env * kTok + my_tok] = __float2half_rn(a.y + c.y);
+        g = fp16r(__fadd_rn(fp16r(__uint_as_float(l0)), gb));
+        p.score_local[env * kTok + my_tok] = __float2half_rn(__uint_as_float(l1));
       }
       my_logit = g;
     }
+    tc_fence_before();
     float mx = warp_max(my_logit);
     if (lane == 0) s.wmax[warp] = mx;
     __syncthreads();
@@ -1032,38 +1072,39 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     for (int w = 0; w < 8; ++w) sm += s.wsum[w];
     {
       const __half wh = __float2half_rn(__fdiv_rn(ex, sm));
-      s.wt16[half][32 * quarter + lane] = my_tok < 0 ? __float2half(0.0f) : wh;
+      const int i = 32 * quarter + lane;
+      // pooling B: column n = tile, K = row within the tile
+      reinterpret_cast<__half*>(s.bpool + (i >> 3) * 256 + half * 16)[i & 7] =
+          my_tok < 0 ? __float2half(0.0f) : wh;
       if (my_tok >= 0 && p.gc_w_out) p.gc_w_out[env * kTok + my_tok] = wh;
     }
+    fence_async_smem();
     __syncthreads();
-    // pooled global context, gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77)
+    // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77): row
+    // tile*64 + c of the pooling GEMM, column `tile`
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16_amajor_m(128, 16);
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      if (t * 128 + 32 * quarter < 11 * kStripCols) {
-        const float wt = __half2float(s.wt16[t][32 * quarter + lane]);
-#pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float2 ff = __half22float2(*reinterpret_cast<const __half2*>(&loc[t][8 * hb + j]));
-            v[2 * j] = wt * ff.x;
-            v[2 * j + 1] = wt * ff.y;
-          }
-          const float r = warp_reduce16(v, lane);
-          if (lane < 16) s.pool[t][quarter][c0 + 16 * hb + lane] = r;
-        }
-      } else {
-        s.pool[t][quarter][c0 + lane] = 0.0f;
-      }
+      for (int kk = 0; kk < 8; ++kk) mma_f16(tmem + 192, s.pl_adesc[kk], s.pl_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+      mma_commit(&s.bar2);
     }
+    if (!mbar_wait_bounded(&s.bar2, ph2)) s.abort_flag = 1;
+    ph2 ^= 1;
+    tc_fence_after();
+    __syncthreads();
+    if (s.abort_flag) break;
+    if (warp < 4) {
+      uint32_t d0, d1;
+      tmem_ld2(tmem + lane_base + 192, d0, d1);
+      tmem_ld_wait();
+      const int mrow = 32 * warp + lane;
+      s.poolv[mrow] = __uint_as_float(mrow < 64 ? d0 : d1);
+    }
+    tc_fence_before();
     __syncthreads();
     if (tid < kD) {
-      float g = 0.0f;
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) g += s.pool[t][q][tid];
+      const float g = s.poolv[tid] + s.poolv[64 + tid];
       const __half gh = __float2half_rn(g);
       s.gc16[tid] = gh;
       p.enc[env * p.ld_enc + 64 + tid] = gh;

@@ -198,6 +198,18 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
          ((uint32_t)(M >> 4) << 24);
 }
 
+// kind::f16 with the A operand stored M-major (bit 15: "transpose A"); B stays K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_amajor_m(int M, int N) {
+  return idesc_f16(M, N) | (1u << 15);
+}
+
+// Warp-collective: 2 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(taddr));
+}
+
 // ---- cp.async (Ampere-style, 4- and 16-byte) ------------------------------------
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src)
