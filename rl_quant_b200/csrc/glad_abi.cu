@@ -107,6 +107,8 @@ int check_conv(const GladConvWeights* w, bool c1, bool c2) {
     return fail(GLAD_ERR_INVALID_ARG, "conv1 buffers (w1p, b1f, qa, qc) must be set");
   if (c2 && (!w->w8 || !w->dq || !w->b2f || !w->a2 || !w->c2))
     return fail(GLAD_ERR_INVALID_ARG, "conv2 buffers (w8, dq, b2f, a2, c2) must be set");
+  if ((c1 && !aligned(w->w1p, 16)) || (c2 && !aligned(w->w8, 16)))
+    return fail(GLAD_ERR_INVALID_ARG, "conv weights w1p / w8 must be 16-byte aligned");
   return GLAD_OK;
 }
 

@@ -88,13 +88,17 @@ __device__ __forceinline__ int conv2_tap_off(int q) {
   return (q / 3) * kStripCols + (q % 3);
 }
 
-// One observation row lives partly in shared memory: the 16-byte aligned
-// body arrives by cp.async, the ragged head/tail bytes are read from global.
+// One observation row staged in shared memory: the 16-byte aligned body
+// arrives by cp.async (16 B), the 4-byte words before and after it by 4-byte
+// cp.async; row byte j sits at stage[j] for j in [lo, hi). A row that is not
+// 4-byte aligned (fp16 rows at an odd element offset) stages only its body and
+// reads the ragged ends from global memory.
 struct RowStage {
   const uint8_t* src;    // first byte of the row in global memory
-  uint32_t body_lo;      // first staged byte (relative to src)
-  uint32_t body_hi;      // one past the last staged byte
-  const uint8_t* stage;  // shared copy of [body_lo, body_hi)
+  uint32_t lo, hi;       // staged byte range of the row
+  uint32_t body_lo;      // 16-byte aligned body [body_lo, body_hi)
+  uint32_t body_hi;
+  uint8_t* stage;        // shared copy, indexed by row byte
 };
 
 __device__ __forceinline__ RowStage row_stage(const void* base, int64_t row, int64_t ld,
@@ -102,24 +106,35 @@ __device__ __forceinline__ RowStage row_stage(const void* base, int64_t row, int
   RowStage r;
   r.src = reinterpret_cast<const uint8_t*>(base) + row * ld * esz;
   const uintptr_t a = reinterpret_cast<uintptr_t>(r.src);
-  const uintptr_t lo = (a + 15) & ~uintptr_t(15);
-  const uintptr_t hi = (a + (uintptr_t)nelem * esz) & ~uintptr_t(15);
-  r.body_lo = (uint32_t)(lo - a);
-  r.body_hi = hi > lo ? (uint32_t)(hi - a) : r.body_lo;
-  r.stage = stage;
+  const uint32_t nbytes = (uint32_t)nelem * esz;
+  r.stage = stage + (a & 15);                          // same alignment as the source
+  const uintptr_t lo16 = (a + 15) & ~uintptr_t(15);
+  const uintptr_t hi16 = (a + nbytes) & ~uintptr_t(15);
+  r.body_lo = (uint32_t)(lo16 - a);
+  r.body_hi = hi16 > lo16 ? (uint32_t)(hi16 - a) : r.body_lo;
+  if (nbytes >= 32 && (a & 3) == 0) {
+    r.lo = 0;
+    r.hi = nbytes & ~3u;
+  } else {
+    r.lo = r.body_lo;
+    r.hi = r.body_hi;
+  }
   return r;
 }
 
 __device__ __forceinline__ void row_issue(const RowStage& r, int tid, int nthr) {
   const uint32_t n16 = (r.body_hi - r.body_lo) >> 4;
   for (uint32_t i = tid; i < n16; i += nthr)
-    cp_async16((void*)(r.stage + i * 16), r.src + r.body_lo + i * 16);
+    cp_async16(r.stage + r.body_lo + i * 16, r.src + r.body_lo + i * 16);
+  const int nh = (int)(r.body_lo - r.lo) >> 2, nt = (int)(r.hi - r.body_hi) >> 2;   // <= 3 each
+  if (tid < nh) cp_async4(r.stage + r.lo + 4 * tid, r.src + r.lo + 4 * tid);
+  else if (tid < nh + nt) cp_async4(r.stage + r.body_hi + 4 * (tid - nh), r.src + r.body_hi + 4 * (tid - nh));
 }
 
 template <int ESZ>
 __device__ __forceinline__ float row_elem(const RowStage& r, int i) {
   const uint32_t b = (uint32_t)i * ESZ;
-  const uint8_t* p = (b >= r.body_lo && b < r.body_hi) ? r.stage + (b - r.body_lo) : r.src + b;
+  const uint8_t* p = (b >= r.lo && b < r.hi) ? r.stage + b : r.src + b;
   if (ESZ == 4) return *reinterpret_cast<const float*>(p);
   return __half2float(*reinterpret_cast<const __half*>(p));
 }
@@ -411,8 +426,7 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
       for (int t = tid; t < kTok; t += NT) {
         const int oh = t / kW2, ow = t - oh * kW2;
         const uint32_t b = (uint32_t)t * 16;
-        const uint8_t* src = (b >= rs.body_lo && b + 16 <= rs.body_hi) ? rs.stage + (b - rs.body_lo)
-                                                                        : rs.src + b;
+        const uint8_t* src = (b >= rs.body_lo && b + 16 <= rs.body_hi) ? rs.stage + b : rs.src + b;
         *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) =
             *reinterpret_cast<const uint4*>(src);
       }
@@ -691,13 +705,28 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     fence_mbar_init();
     s.abort_flag = 0;
   }
+  // raw conv weights -> scratch (the local-feature tile is unused until the loop) with
+  // 16-byte copies, then re-laid shared -> shared into the MMA operand layouts
+  uint8_t* scratch = s.local16;
+  for (int i = tid; i < 3 * 64 * 64 / 16; i += NT)
+    cp_async16(scratch + 16 * i, reinterpret_cast<const uint4*>(p.conv.w8) + i);
+  for (int i = tid; i < 128 * 16 * 2 / 16; i += NT)
+    cp_async16(scratch + 12288 + 16 * i, reinterpret_cast<const uint4*>(p.conv.w1p) + i);
+  cp_async_commit();
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = tid; i < 2 * kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
     for (int i = tid; i < kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(s.strip)[i] = z;
   }
   {
-    const __half* w1p = reinterpret_cast<const __half*>(p.conv.w1p);
+    if (tid < 16) {
+      s.b1[tid] = p.conv.b1f[tid];
+      s.qa[tid] = p.conv.qa[tid];
+      s.qc[tid] = p.conv.qc[tid];
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const __half* w1p = reinterpret_cast<const __half*>(scratch + 12288);
     __half* dst = reinterpret_cast<__half*>(s.w1s);
     for (int idx = tid; idx < kW1sBytes / 2; idx += NT) {
       const int pr = idx >> 8, c = (idx >> 7) & 1, n = (idx >> 3) & 15, e = idx & 7;
@@ -712,12 +741,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     for (int idx = tid; idx < kW2sBytes; idx += NT) {
       const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
       const int q = 2 * pr + c;
-      s.w2s[idx] = q < 9 ? (uint8_t)p.conv.w8[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
-    }
-    if (tid < 16) {
-      s.b1[tid] = p.conv.b1f[tid];
-      s.qa[tid] = p.conv.qa[tid];
-      s.qc[tid] = p.conv.qc[tid];
+      s.w2s[idx] = q < 9 ? scratch[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
     }
     if (tid < 64) {
       s.dq[tid] = p.conv.dq[tid];
@@ -744,11 +768,21 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const float gb = __half2float(p.gps_b[0]);
   if (p.pe_f16) {
     __half* dst = reinterpret_cast<__half*>(s.pe_w);
-    for (int i = tid; i < kD * P; i += NT) dst[i] = p.pe16_w[i];
+    if ((kD * P) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pe16_w) & 15) == 0) {
+      for (int i = tid; i < kD * P / 8; i += NT)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(p.pe16_w)[i];
+    } else {
+      for (int i = tid; i < kD * P; i += NT) dst[i] = p.pe16_w[i];
+    }
     if (tid < kD) s.pe_bp[tid] = p.pe16_b ? __half2float(p.pe16_b[tid]) : 0.0f;
   } else {
-    for (int i = tid; i < kD * P / 4; i += NT)
-      reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
+    if ((kD * P) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.pe.w8) & 15) == 0) {
+      for (int i = tid; i < kD * P / 16; i += NT)
+        reinterpret_cast<uint4*>(s.pe_w)[i] = reinterpret_cast<const uint4*>(p.pe.w8)[i];
+    } else {
+      for (int i = tid; i < kD * P / 4; i += NT)
+        reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
+    }
     for (int k = tid; k < P; k += NT) {
       s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
       s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;

@@ -70,30 +70,47 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     fence_mbar_init();
     s.abort_flag = 0;
   }
-  // ---- constants -------------------------------------------------------------------
+  // ---- constants: raw weights -> scratch (the im2col buffer) by 16-byte copies, then
+  //      re-laid shared -> shared --------------------------------------------------------------
+  uint8_t* scratch = s.a12;
+  {
+    const uint4* w8 = reinterpret_cast<const uint4*>(p.conv.w8);        // [3*64*64] int8
+    const uint4* wi = reinterpret_cast<const uint4*>(p.in_w);           // rows 0..63: [64*64] fp16
+    const uint4* wo = reinterpret_cast<const uint4*>(p.out_w);          // [64*64] fp16
+    const uint4* wq = reinterpret_cast<const uint4*>(p.qp.w8);          // [64*128] int8
+    for (int i = tid; i < 768; i += NT) cp_async16(scratch + 16 * i, w8 + i);
+    for (int i = tid; i < 512; i += NT) {
+      cp_async16(scratch + 12288 + 16 * i, wi + i);
+      cp_async16(scratch + 20480 + 16 * i, wo + i);
+      cp_async16(scratch + 28672 + 16 * i, wq + i);
+    }
+    for (int idx = tid; idx < 128 * 64 / 8; idx += NT) {
+      // bkv[c][n][8 halves] <- in_proj_weight[64 + n][8c .. 8c+8)
+      const int n = idx >> 3, c = idx & 7;
+      cp_async16(s.bkv + (c * 128 + n) * 16, p.in_w + (64 + n) * 64 + 8 * c);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+  }
   for (int idx = tid; idx < 5 * 2048; idx += NT) {
     const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
     const int q = 2 * pr + c;
-    s.w2s[idx] = q < 9 ? (uint8_t)p.conv.w8[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
-  }
-  for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9
-    reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
-  for (int idx = tid; idx < 128 * 64 / 8; idx += NT) {
-    // bkv[c][n][8 halves] <- in_proj_weight[64 + n][8c .. 8c+8)
-    const int n = idx >> 3, c = idx & 7;
-    reinterpret_cast<uint4*>(s.bkv)[c * 128 + n] =
-        reinterpret_cast<const uint4*>(p.in_w + (64 + n) * 64)[c];
+    s.w2s[idx] = q < 9 ? scratch[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
   }
   for (int idx = tid; idx < 32 * 32; idx += NT) {
     // [k pair c2][n pair np]: (W[2np][2c2..], W[2np+1][2c2..]) as two half2
     const int c2 = idx >> 5, np = idx & 31;
-    const uint32_t* wi = reinterpret_cast<const uint32_t*>(p.in_w);
-    const uint32_t* wo = reinterpret_cast<const uint32_t*>(p.out_w);
+    const uint32_t* wi = reinterpret_cast<const uint32_t*>(scratch + 12288);
+    const uint32_t* wo = reinterpret_cast<const uint32_t*>(scratch + 20480);
+    const int* w8 = reinterpret_cast<const int*>(scratch + 28672);
     s.wqT[idx] = make_uint2(wi[(2 * np) * 32 + c2], wi[(2 * np + 1) * 32 + c2]);
     s.woT[idx] = make_uint2(wo[(2 * np) * 32 + c2], wo[(2 * np + 1) * 32 + c2]);
-    const int* w8 = reinterpret_cast<const int*>(p.qp.w8);
     s.w8qpT[idx] = make_int2(w8[(2 * np) * 32 + c2], w8[(2 * np + 1) * 32 + c2]);
   }
+  __syncthreads();                      // scratch is the im2col buffer again from here
+  for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9
+    reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
   grid_dep_wait();                      // outputs of the front kernel are visible from here
   const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
   for (int k = tid; k < 128; k += NT) {
