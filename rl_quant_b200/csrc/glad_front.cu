@@ -697,7 +697,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   constexpr int NT = kFrontThreads;
   grid_dep_launch();
 
-  // ---- one-time set-up ------------------------------------------------------------------
+  // ---- one-time set-up: every global read is issued before the first wait -----------------
   if (warp == 0) tmem_alloc(&s.tmem_base, kFusedTmemCols);
   if (tid == 0) {
     mbar_init(&s.bar1, 1);
@@ -705,27 +705,89 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     fence_mbar_init();
     s.abort_flag = 0;
   }
-  // raw conv weights -> scratch (the local-feature tile is unused until the loop) with
-  // 16-byte copies, then re-laid shared -> shared into the MMA operand layouts
+  const int P = p.prop_dim;
+  const int esz = p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2;
+  const int row_elems = P + kMap;
+  const bool dyn = p.act_mode == GLAD_ACT_DYNAMIC;
+  // raw conv weights -> scratch (the local-feature tile is unused until the loop)
   uint8_t* scratch = s.local16;
   for (int i = tid; i < 3 * 64 * 64 / 16; i += NT)
     cp_async16(scratch + 16 * i, reinterpret_cast<const uint4*>(p.conv.w8) + i);
   for (int i = tid; i < 128 * 16 * 2 / 16; i += NT)
     cp_async16(scratch + 12288 + 16 * i, reinterpret_cast<const uint4*>(p.conv.w1p) + i);
+  for (int i = tid; i < 16; i += NT) {
+    cp_async4(&s.b1[i], p.conv.b1f + i);
+    cp_async4(&s.qa[i], p.conv.qa + i);
+    cp_async4(&s.qc[i], p.conv.qc + i);
+  }
+  for (int i = tid; i < 64; i += NT) {
+    cp_async4(&s.dq[i], p.conv.dq + i);
+    cp_async4(&s.b2[i], p.conv.b2f + i);
+    cp_async4(&s.a2[i], p.conv.a2 + i);
+    cp_async4(&s.c2[i], p.conv.c2 + i);
+  }
+  // proprio embedding weights and constants
+  bool pe_w_async = false;
+  if (p.pe_f16) {
+    pe_w_async = (kD * P) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pe16_w) & 15) == 0;
+    if (pe_w_async)
+      for (int i = tid; i < kD * P / 8; i += NT)
+        cp_async16(s.pe_w + 16 * i, reinterpret_cast<const uint4*>(p.pe16_w) + i);
+  } else {
+    pe_w_async = (kD * P) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.pe.w8) & 15) == 0;
+    if (pe_w_async)
+      for (int i = tid; i < kD * P / 16; i += NT)
+        cp_async16(s.pe_w + 16 * i, reinterpret_cast<const uint4*>(p.pe.w8) + i);
+    for (int k = tid; k < P; k += NT) {
+      if (p.pe.alpha) {
+        cp_async4(&s.pe_a[k], p.pe.alpha + k);
+        cp_async4(&s.pe_b[k], p.pe.beta + k);
+      } else {
+        s.pe_a[k] = 0.0f;
+        s.pe_b[k] = 0.0f;
+      }
+    }
+    for (int i = tid; i < kD; i += NT) {
+      cp_async4(&s.pe_scale[i], (dyn ? p.pe.s_w : p.pe.dq_scale) + i);   // raw; scaled below
+      cp_async4(&s.pe_bp[i], p.pe.b_prime + i);
+    }
+  }
+  for (int k = tid; k < 128; k += NT) {
+    if (p.qp.alpha) {
+      cp_async4(&s.qp_a[k], p.qp.alpha + k);
+      cp_async4(&s.qp_b[k], p.qp.beta + k);
+    } else {
+      s.qp_a[k] = 0.0f;
+      s.qp_b[k] = 0.0f;
+    }
+  }
+  // the first environment's observation row
+  int64_t env = blockIdx.x;
+  if (env < p.B) row_issue(row_stage(p.in, env, p.ld, esz, row_elems, s.stage), tid, NT);
   cp_async_commit();
+  // small fp16 vectors through registers: logits operand rows, biases
+  __half lgw = __float2half(0.0f);
+  if (tid < 2 * kD) lgw = tid < kD ? p.gps_w[tid] : p.scorer_w[tid - kD];
+  const float gb = __half2float(p.gps_b[0]);
+  float pe16b = 0.0f;
+  if (p.pe_f16 && tid < kD && p.pe16_b) pe16b = __half2float(p.pe16_b[tid]);
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = tid; i < 2 * kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
     for (int i = tid; i < kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(s.strip)[i] = z;
+    for (int i = tid; i < 16 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.bpool)[i] = z;
+    for (int i = tid; i < 8 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.blog)[i] = z;
   }
+  grid_dep_wait();                      // slots written by the preceding kernel are visible from here
+  ActQuant aq_pe{};
+  ActQuant aq_qp{};
+  if (!p.pe_f16) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
+  aq_qp.let = p.qp.alpha != nullptr;
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- derived operands ------------------------------------------------------------------
   {
-    if (tid < 16) {
-      s.b1[tid] = p.conv.b1f[tid];
-      s.qa[tid] = p.conv.qa[tid];
-      s.qc[tid] = p.conv.qc[tid];
-    }
-    cp_async_wait_all();
-    __syncthreads();
     const __half* w1p = reinterpret_cast<const __half*>(scratch + 12288);
     __half* dst = reinterpret_cast<__half*>(s.w1s);
     for (int idx = tid; idx < kW1sBytes / 2; idx += NT) {
@@ -743,86 +805,53 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       const int q = 2 * pr + c;
       s.w2s[idx] = q < 9 ? scratch[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
     }
-    if (tid < 64) {
-      s.dq[tid] = p.conv.dq[tid];
-      s.b2[tid] = p.conv.b2f[tid];
-      s.a2[tid] = p.conv.a2[tid];
-      s.c2[tid] = p.conv.c2[tid];
-    }
     // logits B operand: row 0 = global_pool_selector weight, row 1 = scorer weight (local half)
-    for (int idx = tid; idx < 8 * 16 * 8; idx += NT) {
-      const int c = idx >> 7, n = (idx >> 3) & 15, e = idx & 7;
-      __half v = __float2half(0.0f);
-      if (n == 0) v = p.gps_w[8 * c + e];
-      if (n == 1) v = p.scorer_w[8 * c + e];
-      reinterpret_cast<__half*>(s.blog)[idx] = v;
+    if (tid < 2 * kD) {
+      const int n = tid >> 6, c = (tid & 63) >> 3, e = tid & 7;
+      reinterpret_cast<__half*>(s.blog)[(c * 16 + n) * 8 + e] = lgw;
     }
-    for (int i = tid; i < 16 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.bpool)[i] = make_uint4(0, 0, 0, 0);
-  }
-  const int P = p.prop_dim;
-  grid_dep_wait();
-  ActQuant aq_pe{};
-  ActQuant aq_qp{};
-  if (!p.pe_f16) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
-  aq_qp.let = p.qp.alpha != nullptr;
-  const float gb = __half2float(p.gps_b[0]);
-  if (p.pe_f16) {
-    __half* dst = reinterpret_cast<__half*>(s.pe_w);
-    if ((kD * P) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pe16_w) & 15) == 0) {
-      for (int i = tid; i < kD * P / 8; i += NT)
-        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(p.pe16_w)[i];
-    } else {
-      for (int i = tid; i < kD * P; i += NT) dst[i] = p.pe16_w[i];
-    }
-    if (tid < kD) s.pe_bp[tid] = p.pe16_b ? __half2float(p.pe16_b[tid]) : 0.0f;
-  } else {
-    if ((kD * P) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.pe.w8) & 15) == 0) {
-      for (int i = tid; i < kD * P / 16; i += NT)
-        reinterpret_cast<uint4*>(s.pe_w)[i] = reinterpret_cast<const uint4*>(p.pe.w8)[i];
-    } else {
-      for (int i = tid; i < kD * P / 4; i += NT)
-        reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
-    }
-    for (int k = tid; k < P; k += NT) {
-      s.pe_a[k] = aq_pe.let ? p.pe.alpha[k] : 0.0f;
-      s.pe_b[k] = aq_pe.let ? p.pe.beta[k] : 0.0f;
-    }
-    if (tid < kD) {
-      s.pe_scale[tid] = out_scale(p.pe, aq_pe, tid);
-      s.pe_bp[tid] = p.pe.b_prime[tid];
-    }
-  }
-  if (tid < 128) {
-    s.qp_a[tid] = aq_qp.let ? p.qp.alpha[tid] : 0.0f;
-    s.qp_b[tid] = aq_qp.let ? p.qp.beta[tid] : 0.0f;
-  }
-  if (tid == 0) {
-    // every MMA descriptor of the loop, built once
-    for (int b = 0; b < 2; ++b) {
-      const uint32_t pb = smem_u32(s.planes[b]);
-      for (int t = 0; t < 2; ++t)
-        for (int pr = 0; pr < 8; ++pr) {
-          const uint32_t c0 = conv1_chunk_off(2 * pr), c1 = conv1_chunk_off(2 * pr + 1);
-          s.c1_adesc[b][t * 8 + pr] = smem_desc(pb + c0 + t * 128 * 16, c1 - c0, 128);
-        }
-    }
-    for (int pr = 0; pr < 8; ++pr) s.c1_bdesc[pr] = smem_desc(smem_u32(s.w1s) + pr * 512, 256, 128);
-    const uint32_t sb = smem_u32(s.strip);
-    for (int t = 0; t < 2; ++t)
-      for (int pr = 0; pr < 5; ++pr) {
-        const int o0 = conv2_tap_off(2 * pr), o1 = conv2_tap_off(2 * pr + 1);
-        s.c2_adesc[t * 5 + pr] = smem_desc(sb + (t * 128 + o0) * 16, (o1 - o0) * 16, 128);
+    if (p.pe_f16) {
+      if (!pe_w_async) {
+        __half* dw = reinterpret_cast<__half*>(s.pe_w);
+        for (int i = tid; i < kD * P; i += NT) dw[i] = p.pe16_w[i];
       }
-    for (int pr = 0; pr < 5; ++pr) s.c2_bdesc[pr] = smem_desc(smem_u32(s.w2s) + pr * 2048, 1024, 128);
-    // logits: A = local16 tile t, K-major (chunk stride 2048 B, 8-row groups 128 B)
+      if (tid < kD) s.pe_bp[tid] = pe16b;
+    } else {
+      if (!pe_w_async)
+        for (int i = tid; i < kD * P / 4; i += NT)
+          reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
+      if (dyn && tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
+    }
+    // every MMA descriptor of the loop, one per thread
     const uint32_t lb = smem_u32(s.local16);
-    for (int t = 0; t < 2; ++t)
-      for (int kk = 0; kk < 4; ++kk) s.lg_adesc[t][kk] = smem_desc(lb + t * 16384 + kk * 2 * 2048, 2048, 128);
-    for (int kk = 0; kk < 4; ++kk) s.lg_bdesc[kk] = smem_desc(smem_u32(s.blog) + kk * 2 * 256, 256, 128);
-    // pooling: A = local16 read M-major (M = tile*64 + channel: 8-channel blocks 2048 B apart,
-    // K = row: 8-row blocks 128 B apart), B = softmax weights, K-major
-    for (int kk = 0; kk < 8; ++kk) {
+    if (tid < 32) {
+      const int bb = tid >> 4, t = (tid >> 3) & 1, pr = tid & 7;
+      const uint32_t c0 = conv1_chunk_off(2 * pr), c1 = conv1_chunk_off(2 * pr + 1);
+      s.c1_adesc[bb][t * 8 + pr] = smem_desc(smem_u32(s.planes[bb]) + c0 + t * 128 * 16, c1 - c0, 128);
+    } else if (tid < 40) {
+      const int pr = tid - 32;
+      s.c1_bdesc[pr] = smem_desc(smem_u32(s.w1s) + pr * 512, 256, 128);
+    } else if (tid < 50) {
+      const int t = (tid - 40) / 5, pr = (tid - 40) % 5;
+      const int o0 = conv2_tap_off(2 * pr), o1 = conv2_tap_off(2 * pr + 1);
+      s.c2_adesc[t * 5 + pr] = smem_desc(smem_u32(s.strip) + (t * 128 + o0) * 16, (o1 - o0) * 16, 128);
+    } else if (tid < 55) {
+      const int pr = tid - 50;
+      s.c2_bdesc[pr] = smem_desc(smem_u32(s.w2s) + pr * 2048, 1024, 128);
+    } else if (tid < 63) {
+      // logits: A = local16 tile t, K-major (chunk stride 2048 B, 8-row groups 128 B)
+      const int t = (tid - 55) >> 2, kk = (tid - 55) & 3;
+      s.lg_adesc[t][kk] = smem_desc(lb + t * 16384 + kk * 2 * 2048, 2048, 128);
+    } else if (tid < 67) {
+      const int kk = tid - 63;
+      s.lg_bdesc[kk] = smem_desc(smem_u32(s.blog) + kk * 2 * 256, 256, 128);
+    } else if (tid < 75) {
+      // pooling: A = local16 read M-major (M = tile*64 + channel: 8-channel blocks 2048 B
+      // apart, K = row: 8-row blocks 128 B apart), B = softmax weights, K-major
+      const int kk = tid - 67;
       s.pl_adesc[kk] = smem_desc(lb + kk * 256, 128, 2048);
+    } else if (tid < 83) {
+      const int kk = tid - 75;
       s.pl_bdesc[kk] = smem_desc(smem_u32(s.bpool) + kk * 2 * 256, 256, 128);
     }
   }
@@ -836,12 +865,24 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   uint32_t ph1 = 0, ph2 = 0;
   float zmax_qp = 0.0f;
 
-  const int esz = p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2;
-  const int row_elems = P + kMap;
-
   // convert the staged row of `e` into planes[b] / prop16[b]
   auto convert = [&](int64_t e, int b) {
     const RowStage rs = row_stage(p.in, e, p.ld, esz, row_elems, s.stage);
+    if (esz == 4 && rs.lo == 0 && rs.hi == (uint32_t)row_elems * 4) {
+      // the whole fp32 row is in shared memory
+      const float* st = reinterpret_cast<const float*>(s.stage + (rs.stage - s.stage));
+      for (int px = tid; px < kH1 * kW1; px += NT) {
+        const int ih = px / kW1, iw = px - ih * kW1;
+        const float v0 = st[P + px * 3], v1 = st[P + px * 3 + 1], v2 = st[P + px * 3 + 2];
+        const int pl = ih & 1, r = ((ih - pl) >> 1) + 1, slot = iw + 2;
+        const __half2 h01 = __floats2half2_rn(v0, v1);
+        const __half2 h2z = __floats2half2_rn(v2, 0.0f);
+        *reinterpret_cast<uint2*>(s.planes[b] + pl * kPlaneBytes + r * kRowBytes + slot * 8) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h2z));
+      }
+      for (int k = tid; k < P; k += NT) s.prop16[b][k] = __float2half_rn(st[k]);
+      return;
+    }
     for (int px = tid; px < kH1 * kW1; px += NT) {
       const int ih = px / kW1, iw = px - ih * kW1;
       float v0, v1, v2;
@@ -907,13 +948,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   };
 
   // ---- prologue: first environment through conv1 issue ---------------------------------
-  int64_t env = blockIdx.x;
   if (env < p.B) {
-    row_issue(row_stage(p.in, env, p.ld, esz, row_elems, s.stage), tid, NT);
-    cp_async_commit();
-    cp_async_wait_all();
-    __syncthreads();
-    convert(env, 0);
+    convert(env, 0);                    // its row was staged with the set-up copies
     fence_async_smem();
     tc_fence_before();
     __syncthreads();

@@ -169,33 +169,50 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     fence_mbar_init();
     *abort_flag = 0;
   }
-  // weight slices of all four layers, in flight while the input is quantised
-  mlp_load_w(sm + kOffW0, p.L[0].w8, 224, (int)rank * 128, 128, tid);
-  mlp_load_w(sm + kOffW1, p.L[1].w8, 512, (int)rank * 64, 64, tid);
-  mlp_load_w(sm + kOffW2, p.L[2].w8, 256, (int)rank * 32, 32, tid);
-  if (rank == 0) mlp_load_w(sm + kOffW3, p.L[3].w8, 128, 0, 32, tid);
-  cp_async_commit();
 
-  ActQuant aq = make_act_quant(p.L[0], p.act_mode, p.slots, 2);   // input of the running layer
+  // per-column constants, copied asynchronously with the weights
   for (int k = tid; k < 224; k += kMlpThreads) {
-    F[kFInA + k] = aq.let ? p.L[0].alpha[k] : 0.0f;
-    F[kFInB + k] = aq.let ? p.L[0].beta[k] : 0.0f;
+    if (p.L[0].alpha) {
+      cp_async4(&F[kFInA + k], p.L[0].alpha + k);
+      cp_async4(&F[kFInB + k], p.L[0].beta + k);
+    } else {
+      F[kFInA + k] = 0.0f;
+      F[kFInB + k] = 0.0f;
+    }
   }
   for (int l = 0; l < 4; ++l) {
     const GladQLinear& L = p.L[l];
     const int nj = mlp_nj(l), n0 = l < 3 ? (int)rank * nj : 0;
     for (int j = tid; j < nj; j += kMlpThreads) {
       const int n = n0 + j;
-      const bool in = n < mlp_n(l);
-      F[kFSw + mlp_cb(l) + j] = in ? (dyn ? L.s_w[n] : L.dq_scale[n]) : 0.0f;
-      F[kFBp + mlp_cb(l) + j] = in ? L.b_prime[n] : 0.0f;
+      if (n < mlp_n(l)) {
+        cp_async4(&F[kFSw + mlp_cb(l) + j], (dyn ? L.s_w : L.dq_scale) + n);
+        cp_async4(&F[kFBp + mlp_cb(l) + j], L.b_prime + n);
+      } else {
+        F[kFSw + mlp_cb(l) + j] = 0.0f;
+        F[kFBp + mlp_cb(l) + j] = 0.0f;
+      }
       if (l < 3) {
         const GladQLinear& Ln = p.L[l + 1];
-        F[kFNa + mlp_cb(l) + j] = Ln.alpha ? Ln.alpha[n] : 0.0f;
-        F[kFNb + mlp_cb(l) + j] = Ln.alpha ? Ln.beta[n] : 0.0f;
+        if (Ln.alpha) {
+          cp_async4(&F[kFNa + mlp_cb(l) + j], Ln.alpha + n);
+          cp_async4(&F[kFNb + mlp_cb(l) + j], Ln.beta + n);
+        } else {
+          F[kFNa + mlp_cb(l) + j] = 0.0f;
+          F[kFNb + mlp_cb(l) + j] = 0.0f;
+        }
       }
     }
   }
+  cp_async_commit();
+  // weight slices of all four layers, in flight while the input is quantised
+  mlp_load_w(sm + kOffW0, p.L[0].w8, 224, (int)rank * 128, 128, tid);
+  mlp_load_w(sm + kOffW1, p.L[1].w8, 512, (int)rank * 64, 64, tid);
+  mlp_load_w(sm + kOffW2, p.L[2].w8, 256, (int)rank * 32, 32, tid);
+  if (rank == 0) mlp_load_w(sm + kOffW3, p.L[3].w8, 128, 0, 32, tid);
+  cp_async_commit();
+  ActQuant aq = make_act_quant(p.L[0], p.act_mode, p.slots, 2);   // input of the running layer
+  cp_async_wait_group<1>();             // constants landed; the weights may still be in flight
   __syncthreads();
   tc_fence_before();
   cluster_sync_all();                            // every CTA of the cluster runs before DSMEM stores

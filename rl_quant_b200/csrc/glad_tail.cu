@@ -70,9 +70,12 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     fence_mbar_init();
     s.abort_flag = 0;
   }
-  // ---- constants: raw weights -> scratch (the im2col buffer) by 16-byte copies, then
-  //      re-laid shared -> shared --------------------------------------------------------------
+  // ---- constants: every global read is issued before the first wait. Raw weights go to
+  //      scratch (the im2col buffer) and are re-laid shared -> shared afterwards. ----------------
   uint8_t* scratch = s.a12;
+  const bool dyn = p.act_mode == GLAD_ACT_DYNAMIC;
+  const bool a0_let = p.a0_alpha != nullptr;
+  const int enc_w = 128 + p.prop_dim;
   {
     const uint4* w8 = reinterpret_cast<const uint4*>(p.conv.w8);        // [3*64*64] int8
     const uint4* wi = reinterpret_cast<const uint4*>(p.in_w);           // rows 0..63: [64*64] fp16
@@ -89,10 +92,45 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       const int n = idx >> 3, c = idx & 7;
       cp_async16(s.bkv + (c * 128 + n) * 16, p.in_w + (64 + n) * 64 + 8 * c);
     }
+    for (int k = tid; k < 128; k += NT) {
+      if (p.qp.alpha) {
+        cp_async4(&s.qp_a[k], p.qp.alpha + k);
+        cp_async4(&s.qp_b[k], p.qp.beta + k);
+      } else {
+        s.qp_a[k] = 0.0f;
+        s.qp_b[k] = 0.0f;
+      }
+    }
+    for (int i = tid; i < 64; i += NT) {
+      cp_async4(&s.qp_scale[i], (dyn ? p.qp.s_w : p.qp.dq_scale) + i);   // raw; scaled below
+      cp_async4(&s.qp_bp[i], p.qp.b_prime + i);
+      cp_async4(&s.dq[i], p.conv.dq + i);
+      cp_async4(&s.b2[i], p.conv.b2f + i);
+      cp_async4(&s.a2c[i], p.conv.a2 + i);
+      cp_async4(&s.c2[i], p.conv.c2 + i);
+    }
+    for (int k = tid; k < enc_w; k += NT) {
+      if (a0_let) {
+        cp_async4(&s.a0_a[k], p.a0_alpha + k);
+        cp_async4(&s.a0_b[k], p.a0_beta + k);
+      } else {
+        s.a0_a[k] = 0.0f;
+        s.a0_b[k] = 0.0f;
+      }
+    }
     cp_async_commit();
-    cp_async_wait_all();
-    __syncthreads();
   }
+  // fp16 vectors through registers
+  float r_bout = 0.0f, r_wsq = 0.0f;
+  if (tid < 64) {
+    r_bout = __half2float(p.out_b[tid]);
+    r_wsq = __half2float(p.scorer_w[64 + tid]);
+  }
+  float r_bin = tid < 192 ? __half2float(p.in_b[tid]) : 0.0f;
+  grid_dep_wait();                      // outputs of the front kernel are visible from here
+  const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
+  cp_async_wait_all();
+  __syncthreads();
   for (int idx = tid; idx < 5 * 2048; idx += NT) {
     const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
     const int q = 2 * pr + c;
@@ -108,32 +146,15 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     s.woT[idx] = make_uint2(wo[(2 * np) * 32 + c2], wo[(2 * np + 1) * 32 + c2]);
     s.w8qpT[idx] = make_int2(w8[(2 * np) * 32 + c2], w8[(2 * np + 1) * 32 + c2]);
   }
+  if (tid < 64) {
+    if (dyn) s.qp_scale[tid] = __fmul_rn(s.qp_scale[tid], aq.s);      // s_w * s_z
+    s.bout[tid] = r_bout;
+    s.wsq[tid] = r_wsq;
+  }
+  if (tid < 192) s.bin[tid] = r_bin;
   __syncthreads();                      // scratch is the im2col buffer again from here
   for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9
     reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
-  grid_dep_wait();                      // outputs of the front kernel are visible from here
-  const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
-  for (int k = tid; k < 128; k += NT) {
-    s.qp_a[k] = aq.let ? p.qp.alpha[k] : 0.0f;
-    s.qp_b[k] = aq.let ? p.qp.beta[k] : 0.0f;
-  }
-  if (tid < 64) {
-    s.qp_scale[tid] = out_scale(p.qp, aq, tid);
-    s.qp_bp[tid] = p.qp.b_prime[tid];
-    s.dq[tid] = p.conv.dq[tid];
-    s.b2[tid] = p.conv.b2f[tid];
-    s.a2c[tid] = p.conv.a2[tid];
-    s.c2[tid] = p.conv.c2[tid];
-    s.bout[tid] = __half2float(p.out_b[tid]);
-    s.wsq[tid] = __half2float(p.scorer_w[64 + tid]);
-  }
-  for (int k = tid; k < 192; k += NT) s.bin[k] = __half2float(p.in_b[k]);
-  const bool a0_let = p.a0_alpha != nullptr;
-  const int enc_w = 128 + p.prop_dim;
-  for (int k = tid; k < enc_w; k += NT) {
-    s.a0_a[k] = a0_let ? p.a0_alpha[k] : 0.0f;
-    s.a0_b[k] = a0_let ? p.a0_beta[k] : 0.0f;
-  }
   const float sb = __half2float(p.scorer_b[0]);
   fence_async_smem();
   tc_fence_before();
