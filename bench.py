@@ -41,6 +41,10 @@ INT8_PATHS = ["actor.0", "actor.2", "actor.4", "actor.6", "actor_proprio_embeddi
 BYTES_PER_ENV_FWD = 8816          # obs read (fp32) + action mean write, fused ideal
 MACS_PER_ENV = 2.55e6             # conv1 .. actor MLP (int8 2.02 M + fp16 0.53 M)
 OBS_BYTES_PER_ENV = 2175 * 4      # what the front kernel must read per env
+# DRAM bytes (read + write) per front_fused_kernel launch per environment, from the ncu
+# capture summarised in profiles/front_fused_kernel_glad_b4096.md (35.763 MB read +
+# 0.040 MB written at B=4096); traffic grows with the environments processed.
+FRONT_DRAM_BYTES_PER_ENV = (35.763456e6 + 0.03968e6) / 4096
 N_STAGES = ("absmax", "front", "tail", "actor.0", "actor.2", "actor.4", "actor.6")
 
 
@@ -363,7 +367,8 @@ def run_ours(args):
                     "d2h_bytes_per_step": B * 29 * 4},
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": (achieved / hbm_peak) if achieved else None,
-                         "traffic": None, "peak_source": peak_src,
+                         "traffic": (FRONT_DRAM_BYTES_PER_ENV * B if dom_name == "front" else None),
+                         "peak_source": peak_src,
                          "algorithmic_bytes_per_env": OBS_BYTES_PER_ENV if alg_bytes else None},
             "forward_roofline": {"bytes_per_env": BYTES_PER_ENV_FWD, "achieved_gbs": fwd_gbs,
                                  "frac_hbm": fwd_gbs / hbm_peak, "macs_per_env": MACS_PER_ENV,

@@ -199,6 +199,23 @@ __device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
   return r + __shfl_xor_sync(0xffffffffu, r, 16);
 }
 
+// conv2 weights w8 [3][64 (kw*16 + c)][64 n] (qrt/qconv.py:270-284) -> the MMA B operand
+// [5 K-steps][2 taps][64 n][16 c] (tap q = kh*3 + kw; tap 9 is zero filler). One thread
+// builds one 4-byte word; a warp reads 32 consecutive n (no bank conflicts in shared
+// memory, coalesced in global memory).
+__device__ __forceinline__ void conv2_b_relayout(uint8_t* dst, const uint8_t* w8, int tid, int nthr) {
+  for (int j = tid; j < 5 * 2 * 64 * 4; j += nthr) {
+    const int n = j & 63, g = (j >> 6) & 3, q = j >> 8;     // q = 2*pr + c
+    uint32_t word = 0;
+    if (q < 9) {
+      const uint8_t* src = w8 + ((q / 3) * 64 + (q % 3) * 16 + 4 * g) * 64 + n;
+      word = (uint32_t)src[0] | ((uint32_t)src[64] << 8) | ((uint32_t)src[128] << 16) |
+             ((uint32_t)src[192] << 24);
+    }
+    *reinterpret_cast<uint32_t*>(dst + q * 1024 + n * 16 + 4 * g) = word;
+  }
+}
+
 // ---- kernel parameter blocks -------------------------------------------------------
 enum FrontMode : int { kModeConv1 = 0, kModeConv2 = 1, kModeChain = 2, kModeFront = 3 };
 

@@ -225,13 +225,7 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
     }
   }
   if (kConv2) {
-    for (int idx = tid; idx < kW2sBytes; idx += NT) {
-      const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
-      const int q = 2 * pr + c;
-      int8_t v = 0;
-      if (q < 9) v = p.conv.w8[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n];
-      s.w2s[idx] = (uint8_t)v;
-    }
+    conv2_b_relayout(s.w2s, reinterpret_cast<const uint8_t*>(p.conv.w8), tid, NT);
     if (tid < 64) {
       s.dq[tid] = p.conv.dq[tid];
       s.b2[tid] = p.conv.b2f[tid];
@@ -800,11 +794,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       }
       dst[idx] = v;
     }
-    for (int idx = tid; idx < kW2sBytes; idx += NT) {
-      const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
-      const int q = 2 * pr + c;
-      s.w2s[idx] = q < 9 ? scratch[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
-    }
+    conv2_b_relayout(s.w2s, scratch, tid, NT);
     // logits B operand: row 0 = global_pool_selector weight, row 1 = scorer weight (local half)
     if (tid < 2 * kD) {
       const int n = tid >> 6, c = (tid & 63) >> 3, e = tid & 7;

@@ -131,11 +131,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
   cp_async_wait_all();
   __syncthreads();
-  for (int idx = tid; idx < 5 * 2048; idx += NT) {
-    const int pr = idx >> 11, c = (idx >> 10) & 1, n = (idx >> 4) & 63, e = idx & 15;
-    const int q = 2 * pr + c;
-    s.w2s[idx] = q < 9 ? scratch[((q / 3) * 64 + (q % 3) * 16 + e) * 64 + n] : 0;
-  }
+  conv2_b_relayout(s.w2s, scratch, tid, NT);
   for (int idx = tid; idx < 32 * 32; idx += NT) {
     // [k pair c2][n pair np]: (W[2np][2c2..], W[2np+1][2c2..]) as two half2
     const int c2 = idx >> 5, np = idx & 31;
