@@ -639,6 +639,8 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
 // [128,160), conv2's in [0,128). All MMA descriptors are built once.
 // ============================================================================================
 constexpr int kFusedTmemCols = 256;
+constexpr int kIssuer = 7 * 32;          // lane 0 of warp 7 issues the conv MMAs
+constexpr int kConverters = 7 * 32;      // warps 0-6 stage and convert observation rows
 
 struct __align__(128) FusedSmem {
   uint8_t planes[2][kPlanesBytes];
@@ -856,12 +858,12 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   float zmax_qp = 0.0f;
 
   // convert the staged row of `e` into planes[b] / prop16[b]
-  auto convert = [&](int64_t e, int b) {
+  auto convert = [&](int64_t e, int b, int nthr) {
     const RowStage rs = row_stage(p.in, e, p.ld, esz, row_elems, s.stage);
     if (esz == 4 && rs.lo == 0 && rs.hi == (uint32_t)row_elems * 4) {
       // the whole fp32 row is in shared memory
       const float* st = reinterpret_cast<const float*>(s.stage + (rs.stage - s.stage));
-      for (int px = tid; px < kH1 * kW1; px += NT) {
+      for (int px = tid; px < kH1 * kW1; px += nthr) {
         const int ih = px / kW1, iw = px - ih * kW1;
         const float v0 = st[P + px * 3], v1 = st[P + px * 3 + 1], v2 = st[P + px * 3 + 2];
         const int pl = ih & 1, r = ((ih - pl) >> 1) + 1, slot = iw + 2;
@@ -870,10 +872,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         *reinterpret_cast<uint2*>(s.planes[b] + pl * kPlaneBytes + r * kRowBytes + slot * 8) =
             make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h2z));
       }
-      for (int k = tid; k < P; k += NT) s.prop16[b][k] = __float2half_rn(st[k]);
+      for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(st[k]);
       return;
     }
-    for (int px = tid; px < kH1 * kW1; px += NT) {
+    for (int px = tid; px < kH1 * kW1; px += nthr) {
       const int ih = px / kW1, iw = px - ih * kW1;
       float v0, v1, v2;
       if (esz == 4) {
@@ -893,11 +895,11 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       pk.y = *reinterpret_cast<uint32_t*>(&h2z);
       *reinterpret_cast<uint2*>(s.planes[b] + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
     }
-    for (int k = tid; k < P; k += NT)
+    for (int k = tid; k < P; k += nthr)
       s.prop16[b][k] = __float2half_rn(esz == 4 ? row_elem<4>(rs, k) : row_elem<2>(rs, k));
   };
-  auto issue_conv1 = [&](int b) {
-    if (tid == 0) {
+  auto issue_conv1 = [&](int b) {      // by lane 0 of warp 7
+    if (tid == kIssuer) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(128, 16);
 #pragma unroll
@@ -921,11 +923,12 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         a += __shfl_xor_sync(0xffffffffu, a, 1);
         if (part == 0) s.pe16[b][n] = __float2half_rn(a + s.pe_bp[n]);
       }
-    } else {
-      for (int k = tid; k < P; k += NT)
+    } else if (tid < 2 * kD) {
+      // warps 0-3 only (named barrier 3), so warp 7 can issue MMAs meanwhile
+      for (int k = tid; k < P; k += 2 * kD)
         s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[b][k]), s.pe_a[k], s.pe_b[k]);
-      __syncthreads();
-      if (tid < 2 * kD) {
+      named_bar_sync(3, 2 * kD);
+      {
         const int n = tid >> 1, part = tid & 1;
         const int* wrow = reinterpret_cast<const int*>(s.pe_w + n * P) + part * (P / 8);
         const int* qw = reinterpret_cast<const int*>(s.q8) + part * (P / 8);
@@ -938,13 +941,16 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   };
 
   // ---- prologue: first environment through conv1 issue ---------------------------------
+  // In the loop, warps 0-6 stage and convert observation rows (named barrier 1) while
+  // lane 0 of warp 7 issues the conv MMAs; only warps 0-6 own cp.async groups there.
   if (env < p.B) {
-    convert(env, 0);                    // its row was staged with the set-up copies
+    convert(env, 0, NT);                // its row was staged with the set-up copies
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     const int64_t nx = env + gridDim.x;
-    if (nx < p.B) row_issue(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), tid, NT);
+    if (nx < p.B && tid < kConverters)
+      row_issue(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), tid, kConverters);
     cp_async_commit();
     issue_conv1(0);
     proprio_emb(0);
@@ -994,7 +1000,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     tc_fence_before();
     fence_async_smem();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == kIssuer) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_i8(128, 64);
 #pragma unroll
@@ -1005,19 +1011,25 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       mma_commit(&s.bar2);
     }
 
-    // ---- next environment: convert, prefetch, issue its conv1 (overlaps conv2(e)) ---------
+    // ---- next environment: warps 0-6 convert and prefetch while warp 7 issues; then
+    //      warp 7 issues its conv1 and warps 0-3 compute its proprio embedding ---------------
     if (nxt < p.B) {
-      cp_async_wait_all();
-      __syncthreads();
-      convert(nxt, b ^ 1);
-      fence_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      const int64_t nn = nxt + gridDim.x;
-      if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, NT);
-      cp_async_commit();
-      issue_conv1(b ^ 1);
-      proprio_emb(b ^ 1);
+      if (warp == 7) {
+        named_bar_sync(2, NT);            // planes of e+1 written by warps 0-6
+        issue_conv1(b ^ 1);
+      } else {
+        cp_async_wait_all();
+        named_bar_sync(1, kConverters);   // the staged row of e+1 is complete
+        convert(nxt, b ^ 1, kConverters);
+        fence_async_smem();
+        tc_fence_before();
+        named_bar_arrive(2, NT);          // planes ready for the issuer
+        named_bar_sync(1, kConverters);   // every converter is done with the stage buffer
+        const int64_t nn = nxt + gridDim.x;
+        if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, kConverters);
+        cp_async_commit();
+        proprio_emb(b ^ 1);
+      }
     }
 
     // ---- conv2(e) done -> local features -> logits, softmax pool ---------------------------
@@ -1027,53 +1039,74 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     __syncthreads();
     if (s.abort_flag) break;
 
-    // fp16 local features -> local16 (operand of the logits and pooling GEMMs)
+    // fp16 local features -> local16 (operand of the logits and pooling GEMMs). A thread
+    // owns row i of both tiles and 32 channels; each channel's constants serve both tiles.
     {
       const int c0 = 32 * half;
       const int i = 32 * quarter + lane;
+      const bool live1 = 128 + 32 * quarter < 11 * kStripCols;   // tile-1 rows of this warp in the grid
+      const int m1 = 128 + i;
+      const int oh0 = i / kStripCols, ow0 = i - oh0 * kStripCols;
+      const int oh1 = m1 / kStripCols, ow1 = m1 - oh1 * kStripCols;
+      const bool valid0 = oh0 < kH2 && ow0 < kW2;
+      const bool valid1 = oh1 < kH2 && ow1 < kW2;
+      uint8_t* lrow0 = s.local16 + i * 16;
+      uint8_t* lrow1 = s.local16 + 16384 + i * 16;
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        uint8_t* lrow = s.local16 + t * 16384 + i * 16;
-        if (t * 128 + 32 * quarter < 11 * kStripCols) {
-          const int m = t * 128 + i;
-          const int oh = m / kStripCols, ow = m - oh * kStripCols;
-          const bool valid = oh < kH2 && ow < kW2;
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(tmem + lane_base + c0 + 16 * hb, r0);
+        if (live1) tmem_ld16(tmem + lane_base + 64 + c0 + 16 * hb, r1);
+        tmem_ld_wait();
+        uint32_t hw0[8], hw1[8];
 #pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            uint32_t r[16];
-            tmem_ld16(tmem + lane_base + t * 64 + c0 + 16 * hb, r);
-            tmem_ld_wait();
-            uint32_t hw[8];
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const int c = c0 + 16 * hb + j;
-              const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
-              const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
-              const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
-              const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
-              const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)r[j], dq4.x, b24.x, a24.x, c24.x),
-                                                    conv2_val((int32_t)r[j + 1], dq4.y, b24.y, a24.y, c24.y));
-              const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)r[j + 2], dq4.z, b24.z, a24.z, c24.z),
-                                                    conv2_val((int32_t)r[j + 3], dq4.w, b24.w, a24.w, c24.w));
-              hw[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
-              hw[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
-            }
-            const int ch = (c0 + 16 * hb) >> 3;
-            const uint4 v0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            const uint4 v1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-            *reinterpret_cast<uint4*>(lrow + ch * 2048) = v0;
-            *reinterpret_cast<uint4*>(lrow + (ch + 1) * 2048) = v1;
-            if (valid && p.feat_out) {
-              uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh * kW2 + ow) * kD + c0 + 16 * hb);
-              dst[0] = v0;
-              dst[1] = v1;
-            }
+        for (int j = 0; j < 16; j += 4) {
+          const int c = c0 + 16 * hb + j;
+          const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
+          const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
+          const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
+          const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
+          {
+            const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)r0[j], dq4.x, b24.x, a24.x, c24.x),
+                                                  conv2_val((int32_t)r0[j + 1], dq4.y, b24.y, a24.y, c24.y));
+            const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)r0[j + 2], dq4.z, b24.z, a24.z, c24.z),
+                                                  conv2_val((int32_t)r0[j + 3], dq4.w, b24.w, a24.w, c24.w));
+            hw0[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
+            hw0[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
           }
-        } else {
-          // rows past the grid: zero (their pooling weight is 0, the operand must be finite)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            *reinterpret_cast<uint4*>(lrow + ((c0 >> 3) + k) * 2048) = make_uint4(0, 0, 0, 0);
+          if (live1) {
+            const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)r1[j], dq4.x, b24.x, a24.x, c24.x),
+                                                  conv2_val((int32_t)r1[j + 1], dq4.y, b24.y, a24.y, c24.y));
+            const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)r1[j + 2], dq4.z, b24.z, a24.z, c24.z),
+                                                  conv2_val((int32_t)r1[j + 3], dq4.w, b24.w, a24.w, c24.w));
+            hw1[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
+            hw1[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+          } else {
+            // rows past the grid: zero (their pooling weight is 0, the operand must be finite)
+            hw1[j >> 1] = 0u;
+            hw1[(j >> 1) + 1] = 0u;
+          }
+        }
+        const int ch = (c0 + 16 * hb) >> 3;
+        const uint4 v00 = make_uint4(hw0[0], hw0[1], hw0[2], hw0[3]);
+        const uint4 v01 = make_uint4(hw0[4], hw0[5], hw0[6], hw0[7]);
+        const uint4 v10 = make_uint4(hw1[0], hw1[1], hw1[2], hw1[3]);
+        const uint4 v11 = make_uint4(hw1[4], hw1[5], hw1[6], hw1[7]);
+        *reinterpret_cast<uint4*>(lrow0 + ch * 2048) = v00;
+        *reinterpret_cast<uint4*>(lrow0 + (ch + 1) * 2048) = v01;
+        *reinterpret_cast<uint4*>(lrow1 + ch * 2048) = v10;
+        *reinterpret_cast<uint4*>(lrow1 + (ch + 1) * 2048) = v11;
+        if (p.feat_out) {
+          if (valid0) {
+            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh0 * kW2 + ow0) * kD + c0 + 16 * hb);
+            dst[0] = v00;
+            dst[1] = v01;
+          }
+          if (valid1) {
+            uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh1 * kW2 + ow1) * kD + c0 + 16 * hb);
+            dst[0] = v10;
+            dst[1] = v11;
+          }
         }
       }
     }

@@ -203,6 +203,14 @@ __host__ __device__ constexpr uint32_t idesc_f16_amajor_m(int M, int N) {
   return idesc_f16(M, N) | (1u << 15);
 }
 
+// Named CTA barriers (id 1..15; `nthreads` a multiple of 32). arrive does not wait.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Warp-collective: 2 consecutive 32-bit columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t& r0, uint32_t& r1) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
