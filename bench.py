@@ -234,7 +234,9 @@ def run_ours(args):
     if mlp_fused:                       # one kernel for the four MLP layers
         stage_names = stage_names[:3] + ["mlp"]
         stage_ms = stage_ms[:3] + [sum(stage_ms[3:])]
-    n_kernels = (3 if args.act_mode == "dynamic" else 2) + (1 if mlp_fused else 4)
+    n_kernels = N.load().glad_actor_kernel_count(B, N.ACT_MODES[args.act_mode])
+    if stage_ms[0] < 1e-3:              # the proprio absmax runs inside the front kernel
+        stage_names, stage_ms = stage_names[1:], stage_ms[1:]
 
     # actor + critic forward (one PPO rollout step of both heads)
     n_ac = min(4, args.nbuf)

@@ -100,6 +100,7 @@ SIGNATURES = {
                                            c_void_p, c_void_p, POINTER(GladActorAux), c_void_p]),
     "glad_actor_stage_events": (c_int, [POINTER(c_void_p), c_int]),
     "glad_actor_mlp_fused": (c_int, [c_int64, c_int]),
+    "glad_actor_kernel_count": (c_int, [c_int64, c_int]),
     "glad_workspace_status": (c_int, [c_void_p, POINTER(c_uint32), c_void_p]),
     "glad_requant_qlinear": (c_int, [POINTER(GladQLinearSrc), c_int, c_void_p]),
     "glad_requant_qcnn": (c_int, [POINTER(GladQCNNSrc), c_void_p]),

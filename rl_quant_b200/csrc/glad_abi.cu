@@ -18,6 +18,7 @@ cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool p
 size_t tail_smem_bytes();
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl = false);
 int tail_grid(int64_t B, int sms);
+int front_fused_blocks_per_sm();
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
 template <int NT>
@@ -386,8 +387,13 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
 
   stage_mark(0, st);
   GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
-  const bool front_pdl = act_mode == GLAD_ACT_DYNAMIC;
-  if (act_mode == GLAD_ACT_DYNAMIC)
+  // Dynamic s_z of the proprio embedding: reduced inside the front kernel (grid
+  // barrier) when its whole grid fits on the device at once, else by a separate pass.
+  const int front_per_sm = front_fused_blocks_per_sm();
+  const bool pe_absmax_in_front = act_mode == GLAD_ACT_DYNAMIC && front_per_sm > 0;
+  const int fgrid = front_grid(B, d, front_per_sm > 0 && front_per_sm < 2 ? front_per_sm : 2);
+  const bool front_pdl = act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front;
+  if (act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb.alpha,
                                   w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st),
                     "absmax launch");
@@ -413,7 +419,8 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.enc = enc;
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
-  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st, front_pdl), "front launch");
+  fp.pe_absmax = pe_absmax_in_front ? 1 : 0;
+  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, fgrid, st, front_pdl), "front launch");
   stage_mark(2, st);
 
   TailParams tp{};
@@ -657,6 +664,19 @@ int glad_actor_mlp_fused(int64_t B, int act_mode) {
   int rc = device_info(&d);
   if (rc) return rc;
   return use_fused_mlp(B, act_mode, 0) ? 1 : 0;
+}
+
+int glad_actor_kernel_count(int64_t B, int act_mode) {
+  g_err[0] = 0;
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
+    return fail(GLAD_ERR_INVALID_ARG, "unknown act_mode %d", act_mode);
+  DeviceInfo d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  if (B == 0) return 0;
+  const bool absmax_pass = act_mode == GLAD_ACT_DYNAMIC && front_fused_blocks_per_sm() <= 0;
+  return 2 + (absmax_pass ? 1 : 0) + (use_fused_mlp(B, act_mode, 0) ? 1 : 4);
 }
 
 int glad_actor_stage_events(void* const* events, int n) {

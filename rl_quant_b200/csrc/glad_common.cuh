@@ -26,6 +26,10 @@ constexpr int kActions = 29;
 //   4 actor.4, 5 actor.6
 // slots[8]    : device status word (DeviceError bits)
 constexpr int kSlotStatus = 8;
+// slots[16..18] : arrival counters of the fused MLP's grid barriers
+// slots[19]     : arrival counter of the front kernel's proprio-absmax grid barrier
+constexpr int kSlotMlpBarrier = 16;
+constexpr int kSlotFrontBarrier = 19;
 constexpr int kSlotsBytes = 256;
 
 __device__ __forceinline__ float fp16r(float x) { return __half2float(__float2half_rn(x)); }
@@ -234,6 +238,7 @@ struct FrontParams {
   const __half* pe16_w;    // fp16 proprio embedding [64, prop_dim] (pe_f16 != 0)
   const __half* pe16_b;    // [64]
   int pe_f16;
+  int pe_absmax;           // dynamic int8 embedding: reduce slot 0 in-kernel (grid barrier)
   GladQLinear qp;          // only alpha/beta are read (absmax of its input)
   int act_mode;
   int ld_enc;              // row stride of `enc` (>= 128 + prop_dim)

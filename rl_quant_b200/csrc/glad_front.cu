@@ -761,6 +761,25 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   int64_t env = blockIdx.x;
   if (env < p.B) row_issue(row_stage(p.in, env, p.ld, esz, row_elems, s.stage), tid, NT);
   cp_async_commit();
+  // dynamic int8 proprio embedding: this CTA's part of the batch absmax of
+  // |alpha*fp16(x) + beta| over the proprio columns (qrt/qlinear.py:124-128)
+  const bool grid_absmax = dyn && !p.pe_f16 && p.pe_absmax;
+  if (grid_absmax) {
+    // warp w takes this CTA's environments w, w+8, ...; lanes walk the proprio columns
+    float m = 0.0f;
+    for (int64_t row = (int64_t)blockIdx.x + (int64_t)warp * gridDim.x; row < p.B;
+         row += (int64_t)8 * gridDim.x) {
+#pragma unroll 4
+      for (int k = lane; k < P; k += 32) {
+        const float x = esz == 4 ? reinterpret_cast<const float*>(p.in)[row * p.ld + k]
+                                 : __half2float(reinterpret_cast<const __half*>(p.in)[row * p.ld + k]);
+        const float xr = fp16r(x);
+        m = fmaxf(m, p.pe.alpha ? fabsf(__fadd_rn(__fmul_rn(xr, p.pe.alpha[k]), p.pe.beta[k])) : fabsf(xr));
+      }
+    }
+    m = warp_max(m);
+    if (lane == 0) s.wmax[warp] = m;
+  }
   // small fp16 vectors through registers: logits operand rows, biases
   __half lgw = __float2half(0.0f);
   if (tid < 2 * kD) lgw = tid < kD ? p.gps_w[tid] : p.scorer_w[tid - kD];
@@ -777,10 +796,19 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   grid_dep_wait();                      // slots written by the preceding kernel are visible from here
   ActQuant aq_pe{};
   ActQuant aq_qp{};
-  if (!p.pe_f16) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
+  if (!p.pe_f16 && !grid_absmax) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
   aq_qp.let = p.qp.alpha != nullptr;
   cp_async_wait_all();
   __syncthreads();
+  if (grid_absmax && tid == 0) {
+    // publish this CTA's maximum and arrive; the wait comes just before the first use
+    float m = s.wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, s.wmax[w]);
+    if (m > 0.0f) atomic_max_nonneg(&p.slots[0], m);
+    __threadfence();
+    atomicAdd(reinterpret_cast<uint32_t*>(&p.slots[kSlotFrontBarrier]), 1u);
+  }
 
   // ---- derived operands ------------------------------------------------------------------
   {
@@ -812,7 +840,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       if (!pe_w_async)
         for (int i = tid; i < kD * P / 4; i += NT)
           reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
-      if (dyn && tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
+      if (dyn && !grid_absmax && tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
     }
     // every MMA descriptor of the loop, one per thread
     const uint32_t lb = smem_u32(s.local16);
@@ -953,6 +981,30 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       row_issue(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), tid, kConverters);
     cp_async_commit();
     issue_conv1(0);
+    if (grid_absmax) {
+      // every CTA has added its part of the proprio absmax (bounded spin, 2 s)
+      if (tid == 0) {
+        const uint32_t* ctr = reinterpret_cast<const uint32_t*>(&p.slots[kSlotFrontBarrier]);
+        const uint64_t t0 = global_timer_ns();
+        while (ld_acquire_gpu(ctr) < gridDim.x) {
+          if (global_timer_ns() - t0 > 2000000000ull) {
+            s.abort_flag = 1;
+            atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrBarrierTimeout);
+            break;
+          }
+          __nanosleep(64);
+        }
+        __threadfence();
+      }
+      __syncthreads();
+      aq_pe.let = p.pe.alpha != nullptr;
+      aq_pe.dyn = true;
+      aq_pe.s = dyn_scale(ld_relaxed_gpu(&p.slots[0]), aq_pe.let);
+      aq_pe.rcp = __fdiv_rn(1.0f, aq_pe.s);
+      aq_pe.inv = 0.0f;
+      if (tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
+      __syncthreads();
+    }
     proprio_emb(0);
   }
 
@@ -1232,6 +1284,40 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
 }
 
 size_t front_smem_bytes() { return sizeof(FrontSmem) + 128; }
+
+// Resident CTAs of the fused front kernel per SM (its in-kernel grid barrier needs
+// the whole grid resident), cached per device. Computed from the kernel's own
+// resources -- shared memory, registers, threads and TMEM columns (512 per SM) --
+// because the runtime's occupancy query answers 1 for this kernel while two CTAs
+// per SM run side by side.
+int front_fused_blocks_per_sm() {
+  static int cached[64];
+  static bool have[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (have[dev]) return cached[dev];
+  static bool done[64] = {false};
+  if (allow_max_smem((const void*)front_fused_kernel, done) != cudaSuccess) return 0;
+  cudaFuncAttributes a;
+  cudaDeviceProp pr;
+  if (cudaFuncGetAttributes(&a, (const void*)front_fused_kernel) != cudaSuccess ||
+      cudaGetDeviceProperties(&pr, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const size_t smem = sizeof(FusedSmem) + 128 + a.sharedSizeBytes + pr.reservedSharedMemPerBlock;
+  const int by_smem = (int)(pr.sharedMemPerMultiprocessor / smem);
+  const int regs_warp = ((a.numRegs * 32 + 255) / 256) * 256;           // 256-register granules
+  const int by_regs = pr.regsPerMultiprocessor / (regs_warp * (kFrontThreads / 32));
+  const int by_threads = pr.maxThreadsPerMultiProcessor / kFrontThreads;
+  const int by_tmem = 512 / kFusedTmemCols;
+  int n = by_smem < by_regs ? by_smem : by_regs;
+  n = n < by_threads ? n : by_threads;
+  n = n < by_tmem ? n : by_tmem;
+  cached[dev] = n;
+  have[dev] = true;
+  return n;
+}
 
 template <int MODE>
 cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl) {

@@ -25,7 +25,6 @@ namespace glad {
 
 constexpr int kMlpCluster = 4;
 constexpr int kMlpThreads = 512;                 // 16 warps: 4 per TMEM lane quarter
-constexpr int kSlotBarrier = 16;                 // slots[16..18]: grid-barrier arrival counters
 
 // shared memory (bytes)
 constexpr int kOffA0 = 0;                        // A of layers 0 and 2: [K/16][128 rows][16 B], K <= 256
@@ -297,7 +296,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     if (dyn) {
       zmax = warp_max(zmax);
       if (lane == 0 && zmax > 0.0f) atomic_max_nonneg(&p.slots[3 + l], zmax);
-      mlp_grid_barrier(abort_flag, reinterpret_cast<uint32_t*>(&p.slots[kSlotBarrier + l]), gridDim.x,
+      mlp_grid_barrier(abort_flag, reinterpret_cast<uint32_t*>(&p.slots[kSlotMlpBarrier + l]), gridDim.x,
                        status);
       aq.let = nlet;
       aq.dyn = true;
