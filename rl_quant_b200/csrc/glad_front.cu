@@ -806,8 +806,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
 #pragma unroll
     for (int w = 1; w < 8; ++w) m = fmaxf(m, s.wmax[w]);
     if (m > 0.0f) atomic_max_nonneg(&p.slots[0], m);
-    __threadfence();
-    atomicAdd(reinterpret_cast<uint32_t*>(&p.slots[kSlotFrontBarrier]), 1u);
+    red_release_add(reinterpret_cast<uint32_t*>(&p.slots[kSlotFrontBarrier]), 1u);
   }
 
   // ---- derived operands ------------------------------------------------------------------
@@ -992,9 +991,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
             atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrBarrierTimeout);
             break;
           }
-          __nanosleep(64);
         }
-        __threadfence();
       }
       __syncthreads();
       aq_pe.let = p.pe.alpha != nullptr;
@@ -1270,8 +1267,17 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     mbar_wait_bounded(&s.bar2, ph2);
   }
   if (p.act_mode == GLAD_ACT_DYNAMIC) {
+    // one atomic per CTA on the query projector's absmax slot
     const float m = warp_max(zmax_qp);
-    if (lane == 0 && m > 0.0f) atomic_max_nonneg(&p.slots[1], m);
+    __syncthreads();
+    if (lane == 0) s.wmax[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+      float mm = s.wmax[0];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) mm = fmaxf(mm, s.wmax[w]);
+      if (mm > 0.0f) atomic_max_nonneg(&p.slots[1], mm);
+    }
   }
   if (s.abort_flag && tid == 0 && p.slots)
     atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrMmaTimeout);

@@ -43,8 +43,9 @@ constexpr int kFNa = 960;                        // [224] LET alpha / beta of th
 constexpr int kFNb = 1184;
 constexpr int kFSc = 1408;                       // [256] output scale of the running layer
 constexpr int kFCount = 1664;
-constexpr int kOffBar = kOffF + kFCount * 4;
-constexpr int kMlpSmem = kOffBar + 64;
+constexpr int kOffBar = kOffF + kFCount * 4;        // mbarrier, TMEM slot, abort flag
+constexpr int kOffRed = kOffBar + 64;                // per-warp maxima [16]
+constexpr int kMlpSmem = kOffRed + 64;
 constexpr uint32_t kMlpTmemCols = 128;
 static_assert(kMlpSmem + 128 <= 227 * 1024, "shared memory");
 
@@ -119,14 +120,18 @@ __device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mb
   __syncthreads();
 }
 
-// Grid-wide barrier on counter `ctr` (one arrival per CTA). The spin gives up
-// after 2 s (status bit, abort flag); an aborted CTA still arrives.
-__device__ __forceinline__ void mlp_grid_barrier(int* abort_flag, uint32_t* ctr, uint32_t expected,
-                                                 uint32_t* status) {
+// Grid-wide barrier on counter `ctr` (one arrival per CTA), folded with the batch
+// absmax: the CTA's warps leave their maxima in `red`, thread 0 adds one atomic max
+// to `slot`, arrives with a release add and spins with acquire loads. The spin gives
+// up after 2 s (status bit, abort flag); an aborted CTA still arrives.
+__device__ __forceinline__ void mlp_grid_barrier(int* abort_flag, float* red, float* slot, uint32_t* ctr,
+                                                 uint32_t expected, uint32_t* status) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(ctr, 1u);
+    float m = red[0];
+    for (int w = 1; w < kMlpThreads / 32; ++w) m = fmaxf(m, red[w]);
+    if (m > 0.0f) atomic_max_nonneg(slot, m);
+    red_release_add(ctr, 1u);
     if (!*abort_flag) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_gpu(ctr) < expected) {
@@ -135,10 +140,8 @@ __device__ __forceinline__ void mlp_grid_barrier(int* abort_flag, uint32_t* ctr,
           atomicOr(status, kDevErrBarrierTimeout);
           break;
         }
-        __nanosleep(100);
       }
     }
-    __threadfence();
   }
   __syncthreads();
 }
@@ -150,6 +153,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffBar + 8);
   int* abort_flag = reinterpret_cast<int*>(sm + kOffBar + 12);
+  float* red = reinterpret_cast<float*>(sm + kOffRed);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, part = warp >> 2;   // TMEM lane quarter, column-chunk phase
   const int row = 32 * quarter + lane;              // tile row of this thread in the epilogues
@@ -295,9 +299,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     tc_fence_before();
     if (dyn) {
       zmax = warp_max(zmax);
-      if (lane == 0 && zmax > 0.0f) atomic_max_nonneg(&p.slots[3 + l], zmax);
-      mlp_grid_barrier(abort_flag, reinterpret_cast<uint32_t*>(&p.slots[kSlotMlpBarrier + l]), gridDim.x,
-                       status);
+      if (lane == 0) red[warp] = zmax;
+      mlp_grid_barrier(abort_flag, red, &p.slots[3 + l],
+                       reinterpret_cast<uint32_t*>(&p.slots[kSlotMlpBarrier + l]), gridDim.x, status);
       aq.let = nlet;
       aq.dyn = true;
       aq.s = dyn_scale(ld_relaxed_gpu(&p.slots[3 + l]), nlet);

@@ -427,8 +427,16 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   }
 
   if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
+    // one atomic per CTA on actor.0's absmax slot
     const float m = warp_max(zmax_a0);
-    if (lane == 0 && m > 0.0f) atomic_max_nonneg(&p.slots[2], m);
+    if (lane == 0) s.qv[warp][0] = m;            // the query rows are free after the last group
+    __syncthreads();
+    if (tid == 0) {
+      float mm = s.qv[0][0];
+#pragma unroll
+      for (int w = 1; w < kTailEnvs; ++w) mm = fmaxf(mm, s.qv[w][0]);
+      if (mm > 0.0f) atomic_max_nonneg(&p.slots[2], mm);
+    }
   }
   if (s.abort_flag) {
     mbar_wait_bounded(&s.mbar, phase ^ 1);
