@@ -178,6 +178,21 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Train-mode rollout forward (qrt/encoder_opt.py:87-91 with qrt's default
+ * rollout_training=True): as glad_actor_forward, with the Gumbel term drawn
+ * inside the kernel instead of read from memory. Token i of environment e
+ * uses word (i & 3) of Philox4x32-10 (Salmon et al., SC 2011) with counter
+ * {i >> 2, e, e >> 32, offset} and key {seed, seed >> 32}; U = (word >> 21) /
+ * 2048 and the noise is -log(-log(U)) evaluated in fp16 steps like the
+ * reference. `gumbel_offset` is a device word holding this call's offset; the
+ * call adds one to it on the device, so replays of a captured graph draw
+ * fresh noise. The reference draws with torch.rand: equal in distribution,
+ * not bit for bit.                                                          */
+int glad_actor_forward_train(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                             int64_t ld_obs, int act_mode, uint64_t gumbel_seed,
+                             unsigned long long* gumbel_offset, float* mean_out, const GladActorAux* aux,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* The compiled critic function of qrt full mode (qrt/integration.py:133-135):
  * the same encoder over the critic observation group, then the fp16 critic
  * MLP. obs [B, P+2079] (P <= 104), value_out f32 [B,1] (the fp16 output

@@ -208,6 +208,45 @@ def linear16(x, w, b):
 
 
 # -- top-k ----------------------------------------------------------------------
+def philox4x32_10(ctr, key):
+    """Philox4x32 with 10 rounds (Salmon, Moraes, Dror, Shaw, "Parallel random
+    numbers: as easy as 1, 2, 3", SC 2011), vectorised: ctr is four uint32
+    arrays, key two uint32 scalars; returns the four output words."""
+    c0, c1, c2, c3 = (np.asarray(x, dtype=np.uint32).copy() for x in ctr)
+    k0, k1 = np.uint32(key[0]), np.uint32(key[1])
+    m0, m1 = np.uint64(0xD2511F53), np.uint64(0xCD9E8D57)
+    with np.errstate(over="ignore"):
+        for r in range(10):
+            if r > 0:
+                k0 = np.uint32((int(k0) + 0x9E3779B9) & 0xFFFFFFFF)
+                k1 = np.uint32((int(k1) + 0xBB67AE85) & 0xFFFFFFFF)
+            p0 = m0 * c0.astype(np.uint64)
+            p1 = m1 * c2.astype(np.uint64)
+            hi0, lo0 = (p0 >> np.uint64(32)).astype(np.uint32), (p0 & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+            hi1, lo1 = (p1 >> np.uint64(32)).astype(np.uint32), (p1 & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+            c0, c1, c2, c3 = hi1 ^ c1 ^ k0, lo1, hi0 ^ c3 ^ k1, lo0
+    return c0, c1, c2, c3
+
+
+def gumbel16(seed, offset, B, n_tok=187):
+    """The Gumbel term glad_actor_forward_train adds to the top-k logits: token i
+    of env e takes word (i & 3) of philox({i>>2, e, e>>32, offset}, {seed,
+    seed>>32}); U = (word >> 21) / 2048 (the fp16 grid of torch.rand on fp16,
+    qrt/encoder_opt.py:88); noise = -log(-log(U + 1e-10) + 1e-10) in fp16 steps
+    (each log evaluated in fp32 and rounded to fp16; the 1e-10 terms vanish)."""
+    env = np.arange(B, dtype=np.uint64)[:, None] * np.ones((1, n_tok), np.uint64)
+    tok = np.arange(n_tok, dtype=np.uint64)[None, :] * np.ones((B, 1), np.uint64)
+    ctr = [(tok >> np.uint64(2)).astype(np.uint32), (env & np.uint64(0xFFFFFFFF)).astype(np.uint32),
+           (env >> np.uint64(32)).astype(np.uint32), np.full(env.shape, offset & 0xFFFFFFFF, np.uint32)]
+    words = np.stack(philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)))
+    w = np.take_along_axis(words, (tok & np.uint64(3)).astype(np.int64)[None], axis=0)[0]
+    u = (w >> np.uint32(21)).astype(np.float32) / np.float32(2048.0)
+    with np.errstate(divide="ignore"):
+        a = np.log(u).astype(np.float16).astype(np.float32)
+        b = np.log(-a).astype(np.float16).astype(np.float32)
+    return -b
+
+
 def topk_lowest_index(logits, k):
     """Top-k indices ordered by value descending, ties by index ascending."""
     lg = np.asarray(logits).astype(f32)

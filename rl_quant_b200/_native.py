@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 
 import torch
 
@@ -93,6 +93,9 @@ SIGNATURES = {
     "glad_actor_workspace_size": (c_size_t, [c_int64]),
     "glad_actor_forward": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int, c_void_p,
                                    c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
+    "glad_actor_forward_train": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int,
+                                         c_uint64, c_void_p, c_void_p, POINTER(GladActorAux), c_void_p,
+                                         c_size_t, c_void_p]),
     "glad_critic_workspace_size": (c_size_t, [c_int64]),
     "glad_critic_forward": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                     c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),

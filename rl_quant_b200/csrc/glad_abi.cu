@@ -35,7 +35,7 @@ cudaError_t launch_requant_qcnn(const GladQCNNSrc& s, cudaStream_t st);
 cudaError_t launch_cast_copy(const GladCastCopy* items, int n, cudaStream_t st);
 int mlp_max_tiles(int act_mode, cudaStream_t st);
 cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x, int64_t M, int64_t ldx,
-                       float* mean, int64_t ldm, float* slots, cudaStream_t st);
+                       float* mean, int64_t ldm, float* slots, cudaStream_t st, bool pdl = false);
 }  // namespace glad
 
 using namespace glad;
@@ -336,11 +336,43 @@ int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int 
 
 size_t glad_actor_workspace_size(int64_t B) { return actor_ws(nullptr, B < 0 ? 0 : B).bytes; }
 
+namespace {
+struct GumbelArgs {
+  uint64_t seed;
+  unsigned long long* offset;
+};
+int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                       int64_t ld_obs, int act_mode, const float* topk_noise, const GumbelArgs* gumbel,
+                       float* mean_out, const GladActorAux* aux, void* workspace,
+                       size_t workspace_bytes, void* stream);
+}  // namespace
+
 int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
                        int64_t ld_obs, int act_mode, const float* topk_noise, float* mean_out,
                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                        void* stream) {
   g_err[0] = 0;
+  return actor_forward_impl(w, obs, obs_dtype, B, ld_obs, act_mode, topk_noise, nullptr, mean_out, aux,
+                            workspace, workspace_bytes, stream);
+}
+
+int glad_actor_forward_train(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                             int64_t ld_obs, int act_mode, uint64_t gumbel_seed,
+                             unsigned long long* gumbel_offset, float* mean_out, const GladActorAux* aux,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!gumbel_offset) return fail(GLAD_ERR_INVALID_ARG, "gumbel_offset (device word) must be set");
+  if (!aligned(gumbel_offset, 8)) return fail(GLAD_ERR_INVALID_ARG, "gumbel_offset must be 8-byte aligned");
+  const GumbelArgs g{gumbel_seed, gumbel_offset};
+  return actor_forward_impl(w, obs, obs_dtype, B, ld_obs, act_mode, nullptr, &g, mean_out, aux, workspace,
+                            workspace_bytes, stream);
+}
+
+namespace {
+int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
+                       int64_t ld_obs, int act_mode, const float* topk_noise, const GumbelArgs* gumbel,
+                       float* mean_out, const GladActorAux* aux, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   if (!w) return fail(GLAD_ERR_INVALID_ARG, "weights are NULL");
   if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
   if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
@@ -440,6 +472,9 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.ld_enc = kEnc;
   tp.prop_dim = P;
   tp.noise = topk_noise;
+  tp.gumbel = gumbel ? 1 : 0;
+  tp.gumbel_seed = gumbel ? gumbel->seed : 0;
+  tp.gumbel_offset = gumbel ? gumbel->offset : nullptr;
   tp.z8 = z8;
   tp.score_local = score_local;
   tp.pe = ws.pe;
@@ -459,7 +494,7 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
     bool w_ok = true;
     for (int i = 0; i < 4; ++i) w_ok = w_ok && aligned(w->mlp[i].w8, 16);
     if (w_ok && use_fused_mlp(B, act_mode, st)) {
-      GLAD_CHECK_CUDA(launch_mlp(w->mlp, act_mode, enc, B, kEnc, mean_out, kActions, ws.slots, st),
+      GLAD_CHECK_CUDA(launch_mlp(w->mlp, act_mode, enc, B, kEnc, mean_out, kActions, ws.slots, st, true),
                       "fused actor MLP launch");
       fused_mlp = true;
       for (int i = 0; i < 4; ++i) stage_mark(4 + i, st);
@@ -508,6 +543,8 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
   }
   return GLAD_OK;
 }
+
+}  // namespace
 
 constexpr int kCriticEnc = 232;   // encoded row stride of the critic (128 + P <= 232)
 

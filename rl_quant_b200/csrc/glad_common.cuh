@@ -30,6 +30,7 @@ constexpr int kSlotStatus = 8;
 // slots[19]     : arrival counter of the front kernel's proprio-absmax grid barrier
 constexpr int kSlotMlpBarrier = 16;
 constexpr int kSlotFrontBarrier = 19;
+constexpr int kSlotTailDone = 20;       // CTAs of the tail kernel that finished (Gumbel offset)
 constexpr int kSlotsBytes = 256;
 
 __device__ __forceinline__ float fp16r(float x) { return __half2float(__float2half_rn(x)); }
@@ -220,6 +221,41 @@ __device__ __forceinline__ void conv2_b_relayout(uint8_t* dst, const uint8_t* w8
   }
 }
 
+// ---- Gumbel noise for train-mode rollouts (qrt/encoder_opt.py:87-91) ------------------
+// Counter-based generator: Philox4x32 with 10 rounds, the published method of Salmon,
+// Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC 2011).
+// Token i of environment e draws word (i & 3) of philox(counter = {i >> 2, e_lo, e_hi,
+// offset}, key = {seed_lo, seed_hi}); the word's top 11 bits give U on the fp16 grid
+// k * 2^-11 in [0, 1), and the noise follows the reference's fp16 steps
+// -log(-log(U + 1e-10) + 1e-10) (the 1e-10 terms vanish in fp16).
+__host__ __device__ __forceinline__ void philox4x32_10(uint32_t (&c)[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+  }
+}
+
+__device__ __forceinline__ float gumbel16(uint64_t seed, uint64_t offset, int64_t env, int tok) {
+  uint32_t c[4] = {(uint32_t)(tok >> 2), (uint32_t)env, (uint32_t)((uint64_t)env >> 32), (uint32_t)offset};
+  philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+  const uint32_t w = c[tok & 3];
+  const float u = (float)(w >> 21) * (1.0f / 2048.0f);
+  const float a = fp16r(logf(u));          // log(0) = -inf
+  const float b = fp16r(logf(-a));
+  return -b;
+}
+
 // ---- kernel parameter blocks -------------------------------------------------------
 enum FrontMode : int { kModeConv1 = 0, kModeConv2 = 1, kModeChain = 2, kModeFront = 3 };
 
@@ -270,6 +306,9 @@ struct TailParams {
   int ld_enc;              // row stride of `enc`
   int prop_dim;            // proprio columns of `enc` (from column 128)
   const float* noise;      // [B,187] or null
+  int gumbel;              // draw the noise in-kernel (Philox4x32-10) instead of reading `noise`
+  uint64_t gumbel_seed;
+  unsigned long long* gumbel_offset;   // device word: this call's counter offset; advanced by one per call
   const int8_t* z8;        // [B*187,16]
   const __half* score_local;
   const __half* pe;        // [B,64]

@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   mlp_load_w(sm + kOffW2, p.L[2].w8, 256, (int)rank * 32, 32, tid);
   if (rank == 0) mlp_load_w(sm + kOffW3, p.L[3].w8, 128, 0, 32, tid);
   cp_async_commit();
+  grid_dep_wait();                      // encoded rows and slot 2 of the preceding kernel
   ActQuant aq = make_act_quant(p.L[0], p.act_mode, p.slots, 2);   // input of the running layer
   cp_async_wait_group<1>();             // constants landed; the weights may still be in flight
   __syncthreads();
@@ -403,7 +404,7 @@ int mlp_max_tiles(int act_mode, cudaStream_t st) {
 }
 
 cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x, int64_t M, int64_t ldx,
-                       float* mean, int64_t ldm, float* slots, cudaStream_t st) {
+                       float* mean, int64_t ldm, float* slots, cudaStream_t st, bool pdl) {
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)mlp_kernel, done);
   if (e != cudaSuccess) return e;
@@ -418,17 +419,19 @@ cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x,
   p.slots = slots;
   const int tiles = (int)((M + 127) / 128);
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kMlpCluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3((unsigned)(tiles * kMlpCluster));
   cfg.blockDim = dim3(kMlpThreads);
   cfg.dynamicSmemBytes = kMlpSmem + 128;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, mlp_kernel, p);
 }
 

@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9
     reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
   const float sb = __half2float(p.scorer_b[0]);
+  const uint64_t g_offset = p.gumbel ? (uint64_t)*p.gumbel_offset : 0ull;
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -221,7 +222,8 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         key[j] = 0;
         if (i < kTok) {
           float lg = fp16r(__fadd_rn(__half2float(p.score_local[env * kTok + i]), sq));
-          if (p.noise) lg = fp16r(__fadd_rn(lg, p.noise[env * kTok + i]));
+          if (p.gumbel) lg = fp16r(__fadd_rn(lg, gumbel16(p.gumbel_seed, g_offset, env, i)));
+          else if (p.noise) lg = fp16r(__fadd_rn(lg, p.noise[env * kTok + i]));
           const __half lh = __float2half_rn(lg);
           if (p.topk_logits_out) p.topk_logits_out[env * kTok + i] = lh;
           key[j] = (ord16(lh) << 16) | (uint32_t)(0xFFFF - i);
@@ -437,6 +439,12 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       for (int w = 1; w < kTailEnvs; ++w) mm = fmaxf(mm, s.qv[w][0]);
       if (mm > 0.0f) atomic_max_nonneg(&p.slots[2], mm);
     }
+  }
+  if (p.gumbel && tid == 0) {
+    // the last CTA to finish advances the offset for the next call (every CTA has read it)
+    __threadfence();
+    if (atomicAdd(reinterpret_cast<unsigned int*>(&p.slots[kSlotTailDone]), 1u) == gridDim.x - 1)
+      atomicAdd(p.gumbel_offset, 1ull);
   }
   if (s.abort_flag) {
     mbar_wait_bounded(&s.mbar, phase ^ 1);

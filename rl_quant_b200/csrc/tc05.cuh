@@ -74,10 +74,11 @@ __device__ __forceinline__ void grid_dep_launch() {
 
 // GLAD_PDL=1 in the environment turns programmatic dependent launch on for the
 // fused forwards' kernel chains (read once per process; off by default).
+// On by default; GLAD_PDL=0 launches every kernel after its predecessor completes.
 inline bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("GLAD_PDL");
-    return v != nullptr && v[0] == '1';
+    return !(v != nullptr && v[0] == '0');
   }();
   return on;
 }

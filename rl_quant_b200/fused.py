@@ -84,19 +84,36 @@ class FusedActor:
         return ws
 
     def run(self, obs: torch.Tensor, mean: torch.Tensor | None, aux: N.GladActorAux | None = None,
-            noise: torch.Tensor | None = None) -> None:
-        """Launch the fused forward on the current stream (no host sync)."""
+            noise: torch.Tensor | None = None, gumbel: tuple | None = None) -> None:
+        """Launch the fused forward on the current stream (no host sync).
+
+        ``noise``: f32 [B,187] added to the top-k logits. ``gumbel = (seed, offset)``
+        instead draws the train-mode Gumbel term inside the kernel; ``offset`` is an
+        int64 device tensor of one element that every call advances by one."""
         N.require_cuda(obs)
         if obs.dim() != 2 or obs.stride(1) != 1:
             raise ValueError("obs must be a row-major [B, 96+2079] tensor")
         if obs.dtype not in (torch.float32, torch.float16):
             raise TypeError("obs must be float32 or float16")
+        if noise is not None and gumbel is not None:
+            raise ValueError("pass either noise or gumbel")
         B = obs.shape[0]
         ws = self.workspace(B, obs.device)
+        dt = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
+        if gumbel is not None:
+            seed, offset = gumbel
+            N.require_cuda(offset)
+            if offset.dtype != torch.int64 or offset.numel() != 1:
+                raise ValueError("gumbel offset must be a one-element int64 CUDA tensor")
+            rc = N.load().glad_actor_forward_train(
+                self.weights(), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode],
+                int(seed) & 0xFFFFFFFFFFFFFFFF, offset.data_ptr(), N.ptr(mean), aux, ws.data_ptr(), ws.numel(),
+                N.stream_handle(obs.device))
+            N.check(rc, "glad_actor_forward_train")
+            return
         rc = N.load().glad_actor_forward(
-            self.weights(), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
-            B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise), N.ptr(mean), aux,
-            ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
+            self.weights(), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise),
+            N.ptr(mean), aux, ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
         N.check(rc, "glad_actor_forward")
 
     def act(self, obs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -82,6 +82,9 @@ class InferenceRunner:
             except FusedUnsupported as e:
                 warnings.warn(f"[rl_quant_b200] fused GLAD critic unavailable ({e}); running op by op")
         self._graphs: dict[tuple, _Graph] = {}
+        # Gumbel stream of train-mode rollouts: seed from torch's default generator
+        self._gumbel_seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+        self._gumbel_offset = None
         self._g_refresh = None
         self._g_sync = None
         self._sync_items = None
@@ -90,9 +93,14 @@ class InferenceRunner:
     def _act_fn(self, po):
         if self._fused is not None:
             mean = torch.empty(po.shape[0], 29, dtype=torch.float32, device=po.device)
-            # train-mode rollouts keep the Gumbel top-k exploration (qrt/encoder_opt.py:87-91)
-            noise = _gumbel_noise((po.shape[0], 187), po.device) if self.model.training else None
-            self._fused.run(po, mean, noise=noise)
+            if self.model.training:
+                # train-mode rollouts keep the Gumbel top-k exploration (qrt/encoder_opt.py:87-91),
+                # drawn inside the kernel; the device offset advances on every (replayed) call
+                if self._gumbel_offset is None or self._gumbel_offset.device != po.device:
+                    self._gumbel_offset = torch.zeros(1, dtype=torch.int64, device=po.device)
+                self._fused.run(po, mean, gumbel=(self._gumbel_seed, self._gumbel_offset))
+            else:
+                self._fused.run(po, mean)
             return mean
         return self.model.act_inference({"policy_obs": po})[0]
 

@@ -136,3 +136,25 @@ def actor_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, noise=Non
     N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
     torch.cuda.synchronize()
     return mean, aux_t
+
+
+def actor_forward_train(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, seed: int, offset: torch.Tensor):
+    """glad_actor_forward_train (in-kernel Gumbel); returns (mean, aux)."""
+    B, dev = obs.shape[0], obs.device
+    mean = torch.empty(B, 29, dtype=torch.float32, device=dev)
+    aux_t = {"topk_logits": torch.empty(B, 187, dtype=torch.float16, device=dev),
+             "topk_idx": torch.empty(B, 32, dtype=torch.int64, device=dev)}
+    aux = N.GladActorAux()
+    for k, v in aux_t.items():
+        setattr(aux, k, v.data_ptr())
+    lib = N.load()
+    nbytes = lib.glad_actor_workspace_size(B)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dtype = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
+    N.check(lib.glad_actor_forward_train(dw.actor(), obs.data_ptr(), dtype, B, obs.stride(0),
+                                         N.ACT_MODES[act_mode], seed, offset.data_ptr(), mean.data_ptr(), aux,
+                                         ws.data_ptr(), nbytes, N.stream_handle()), "glad_actor_forward_train")
+    st = N.c_uint32(0)
+    N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
+    torch.cuda.synchronize()
+    return mean, aux_t

@@ -12,7 +12,7 @@ import torch
 from oracle import glad_oracle as O
 from rl_quant_b200.synthetic import glad_obs
 
-from gpu_util import DeviceWeights, actor_forward, fp16_ulp_close
+from gpu_util import DeviceWeights, actor_forward, actor_forward_train, fp16_ulp_close
 
 pytestmark = pytest.mark.gpu
 
@@ -125,3 +125,26 @@ def test_fused_mlp_equals_per_layer_kernels(dw, mode, B, monkeypatch):
     layered, _ = actor_forward(dw, obs, mode, with_aux=False)
     assert torch.isfinite(fused).all()
     assert torch.equal(fused, layered)
+
+
+@pytest.mark.parametrize("B", [7, 300])
+def test_actor_train_mode_gumbel_in_kernel(dw, B):
+    """glad_actor_forward_train: perturbed logits = fp16(clean + Philox4x32-10 Gumbel of
+    the oracle), the device offset advances by one per call, top-32 on the perturbed
+    logits, a new offset draws new noise."""
+    obs = glad_obs(B, seed=21 + B).cuda()
+    _, clean = actor_forward(dw, obs, "dynamic")
+    offset = torch.tensor([5], dtype=torch.int64, device="cuda")
+    mean, pert = actor_forward_train(dw, obs, "dynamic", seed=99, offset=offset)
+    assert int(offset.item()) == 6
+    assert torch.isfinite(mean).all()
+    expect = (clean["topk_logits"].cpu().numpy().astype(np.float32) + O.gumbel16(99, 5, B)).astype(np.float16)
+    got = pert["topk_logits"].cpu().numpy()
+    fin = np.isfinite(expect)
+    assert np.array_equal(np.isfinite(got), fin)
+    fp16_ulp_close(got[fin], expect[fin])
+    lg = got.astype(np.float32)
+    assert np.array_equal(pert["topk_idx"].cpu().numpy(), O.topk_lowest_index(lg, 32))
+    _, pert2 = actor_forward_train(dw, obs, "dynamic", seed=99, offset=offset)
+    assert int(offset.item()) == 7
+    assert not torch.equal(pert2["topk_logits"], pert["topk_logits"])

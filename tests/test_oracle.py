@@ -81,3 +81,20 @@ def test_topk_tie_rule():
     lg = np.array([[1.0, 3.0, 3.0, 2.0, 3.0]], np.float16)
     assert O.topk_lowest_index(lg, 3).tolist() == [[1, 2, 4]]
     assert O.topk_lowest_index(lg, 2).tolist() == [[1, 2]]
+
+
+def test_philox4x32_10_known_answer():
+    """Philox4x32-10 with a zero counter and key (the Random123 known-answer vector)."""
+    out = O.philox4x32_10([np.zeros(1, np.uint32)] * 4, (0, 0))
+    assert [int(x[0]) for x in out] == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+
+
+def test_gumbel16_distribution():
+    """The in-kernel Gumbel term: fp16 values with the Gumbel(0, 1) mean and spread."""
+    g = O.gumbel16(seed=1234, offset=0, B=2048)
+    fin = g[np.isfinite(g)]
+    assert np.isinf(g).mean() < 1e-3            # U == 0 (1/2048) gives -inf, never selected
+    assert abs(fin.mean() - 0.5772) < 0.02       # Euler-Mascheroni constant
+    assert abs(fin.std() - np.pi / np.sqrt(6.0)) < 0.03
+    assert np.array_equal(fin, fin.astype(np.float16).astype(np.float32))
+    assert not np.array_equal(g, O.gumbel16(seed=1234, offset=1, B=2048))
