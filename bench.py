@@ -58,6 +58,7 @@ def parse():
     p.add_argument("--act-mode", choices=("dynamic", "static"), default="dynamic")
     p.add_argument("--nbuf", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-conv-chain", action="store_true", help="skip the conv-only (QuantCNN chain) measurement")
     return p.parse_args()
 
 
@@ -140,6 +141,43 @@ def build_inference_copy(device, act_mode: str):
     swap_cnn(infer, calib_cnn_scale(infer, fn_factory(), n_batches=8))
     patch_encoder(infer)
     return model, infer.eval()
+
+
+def bench_conv_chain(device, hbm_peak, conv_w, reps=50):
+    """The QuantCNN chain alone (x_nhwc fp16 -> z8 + fp16 local features) at the
+    conv-only batch sizes: CUDA-event time per call over rotating buffers larger
+    than L2, algorithmic bytes = fp16 input 4,158 B + fp16 features 23,936 B per env."""
+    from rl_quant_b200 import _native as N
+    from rl_quant_b200.synthetic import glad_obs
+    lib = N.load()
+    out = {}
+    w = None
+    for B in (1024, 4096, 16384):
+        per_buf = B * (4158 + 23936 + 2992)
+        nbuf = max(2, -(-200_000_000 // per_buf))
+        x0 = glad_obs(B, seed=77)[:, 96:].half().reshape(B, 21, 33, 3).contiguous().to(device)
+        xs = [x0] + [x0.roll(k, 0) for k in range(1, nbuf)]
+        feats = [torch.empty(B * 187, 64, dtype=torch.float16, device=device) for _ in range(nbuf)]
+        z8s = [torch.empty(B * 187, 16, dtype=torch.int8, device=device) for _ in range(nbuf)]
+        if w is None:
+            w = conv_w
+        for k in range(3):
+            N.check(lib.glad_conv_chain(xs[k % nbuf].data_ptr(), B, w, feats[k % nbuf].data_ptr(),
+                                        z8s[k % nbuf].data_ptr(), N.stream_handle(device)))
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for k in range(reps):
+            lib.glad_conv_chain(xs[k % nbuf].data_ptr(), B, w, feats[k % nbuf].data_ptr(),
+                                z8s[k % nbuf].data_ptr(), N.stream_handle(device))
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / reps
+        gbs = B * 28094 / (ms / 1e3) / 1e9
+        out[str(B)] = {"ms": ms, "env_per_s": B / (ms / 1e3), "achieved_gbs": gbs,
+                       "frac_hbm": gbs / hbm_peak, "bytes_per_env": 28094}
+        del xs, feats, z8s
+    return out
 
 
 def run_ours(args):
@@ -347,6 +385,9 @@ def run_ours(args):
         achieved = (alg_bytes / (stage_ms[dom] / 1e3) / 1e9) if alg_bytes else None
         fwd_gbs = BYTES_PER_ENV_FWD * B / (ms_step / 1e3) / 1e9
         tops = MACS_PER_ENV * 2 * B / (ms_step / 1e3) / 1e12
+        conv_chain = None
+        if not args.no_conv_chain:
+            conv_chain = bench_conv_chain(device, hbm_peak, fused.weights().conv)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_fp32 import time_fp32_forward
@@ -382,6 +423,9 @@ def run_ours(args):
                             "collective": "nccl broadcast of one packed blob" if world > 1 else "none (1 GPU)",
                             "steps": "cast-copy fp32 master -> fp16 copy + requantise (one CUDA graph) + broadcast",
                             "ranks_identical": checks_ok},
+            "conv_chain": ({"workload": "QuantCNN chain alone (glad_conv_chain): x_nhwc fp16 -> z8 + fp16 "
+                                        "local features; rotating buffers > L2; events per call",
+                            "per_batch": conv_chain} if conv_chain else None),
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * n_kernels,
         }

@@ -19,6 +19,7 @@ size_t tail_smem_bytes();
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl = false);
 int tail_grid(int64_t B, int sms);
 int front_fused_blocks_per_sm();
+cudaError_t launch_chain(const FrontParams& p, int grid, cudaStream_t st);
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
 template <int NT>
@@ -266,8 +267,7 @@ int glad_conv_chain(const void* x_nhwc, int64_t B, const GladConvWeights* w, voi
   p.conv = *w;
   p.feat_out = reinterpret_cast<__half*>(feat_out);
   p.z8_out = z8_out;
-  GLAD_CHECK_CUDA(launch_front<kModeChain>(p, front_grid(B, d, 2), (cudaStream_t)stream),
-                  "conv chain launch");
+  GLAD_CHECK_CUDA(launch_chain(p, front_grid(B, d, 2), (cudaStream_t)stream), "conv chain launch");
   return GLAD_OK;
 }
 

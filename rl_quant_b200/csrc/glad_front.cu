@@ -683,6 +683,9 @@ struct __align__(128) FusedSmem {
   int abort_flag;
 };
 
+// FULL = false: the QuantCNN chain alone (x_nhwc -> z8 -> fp16 local features), the same
+// pipeline without the pooling / embedding stages.
+template <bool FULL>
 __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS)
 front_fused_kernel(const __grid_constant__ FrontParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -724,7 +727,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   }
   // proprio embedding weights and constants
   bool pe_w_async = false;
-  if (p.pe_f16) {
+  if (!FULL) {
+  } else if (p.pe_f16) {
     pe_w_async = (kD * P) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pe16_w) & 15) == 0;
     if (pe_w_async)
       for (int i = tid; i < kD * P / 8; i += NT)
@@ -749,7 +753,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     }
   }
   for (int k = tid; k < 128; k += NT) {
-    if (p.qp.alpha) {
+    if (FULL && p.qp.alpha) {
       cp_async4(&s.qp_a[k], p.qp.alpha + k);
       cp_async4(&s.qp_b[k], p.qp.beta + k);
     } else {
@@ -763,7 +767,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   cp_async_commit();
   // dynamic int8 proprio embedding: this CTA's part of the batch absmax of
   // |alpha*fp16(x) + beta| over the proprio columns (qrt/qlinear.py:124-128)
-  const bool grid_absmax = dyn && !p.pe_f16 && p.pe_absmax;
+  const bool grid_absmax = FULL && dyn && !p.pe_f16 && p.pe_absmax;
   if (grid_absmax) {
     // warp w takes this CTA's environments w, w+8, ...; lanes walk the proprio columns
     float m = 0.0f;
@@ -782,10 +786,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   }
   // small fp16 vectors through registers: logits operand rows, biases
   __half lgw = __float2half(0.0f);
-  if (tid < 2 * kD) lgw = tid < kD ? p.gps_w[tid] : p.scorer_w[tid - kD];
-  const float gb = __half2float(p.gps_b[0]);
+  if (FULL && tid < 2 * kD) lgw = tid < kD ? p.gps_w[tid] : p.scorer_w[tid - kD];
+  const float gb = FULL ? __half2float(p.gps_b[0]) : 0.0f;
   float pe16b = 0.0f;
-  if (p.pe_f16 && tid < kD && p.pe16_b) pe16b = __half2float(p.pe16_b[tid]);
+  if (FULL && p.pe_f16 && tid < kD && p.pe16_b) pe16b = __half2float(p.pe16_b[tid]);
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = tid; i < 2 * kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
@@ -796,8 +800,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   grid_dep_wait();                      // slots written by the preceding kernel are visible from here
   ActQuant aq_pe{};
   ActQuant aq_qp{};
-  if (!p.pe_f16 && !grid_absmax) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
-  aq_qp.let = p.qp.alpha != nullptr;
+  if (FULL && !p.pe_f16 && !grid_absmax) aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
+  aq_qp.let = FULL && p.qp.alpha != nullptr;
   cp_async_wait_all();
   __syncthreads();
   if (grid_absmax && tid == 0) {
@@ -829,7 +833,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       const int n = tid >> 6, c = (tid & 63) >> 3, e = tid & 7;
       reinterpret_cast<__half*>(s.blog)[(c * 16 + n) * 8 + e] = lgw;
     }
-    if (p.pe_f16) {
+    if (!FULL) {
+    } else if (p.pe_f16) {
       if (!pe_w_async) {
         __half* dw = reinterpret_cast<__half*>(s.pe_w);
         for (int i = tid; i < kD * P; i += NT) dw[i] = p.pe16_w[i];
@@ -1002,7 +1007,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       if (tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
       __syncthreads();
     }
-    proprio_emb(0);
+    if (FULL) proprio_emb(0);
   }
 
   int b = 0;
@@ -1042,7 +1047,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
           }
           const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
-          reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;
+          if (p.z8_out) reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;   // optional for the chain
         }
       }
     }
@@ -1077,7 +1082,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         const int64_t nn = nxt + gridDim.x;
         if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, kConverters);
         cp_async_commit();
-        proprio_emb(b ^ 1);
+        if (FULL) proprio_emb(b ^ 1);
       }
     }
 
@@ -1141,10 +1146,12 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         const uint4 v01 = make_uint4(hw0[4], hw0[5], hw0[6], hw0[7]);
         const uint4 v10 = make_uint4(hw1[0], hw1[1], hw1[2], hw1[3]);
         const uint4 v11 = make_uint4(hw1[4], hw1[5], hw1[6], hw1[7]);
-        *reinterpret_cast<uint4*>(lrow0 + ch * 2048) = v00;
-        *reinterpret_cast<uint4*>(lrow0 + (ch + 1) * 2048) = v01;
-        *reinterpret_cast<uint4*>(lrow1 + ch * 2048) = v10;
-        *reinterpret_cast<uint4*>(lrow1 + (ch + 1) * 2048) = v11;
+        if (FULL) {
+          *reinterpret_cast<uint4*>(lrow0 + ch * 2048) = v00;
+          *reinterpret_cast<uint4*>(lrow0 + (ch + 1) * 2048) = v01;
+          *reinterpret_cast<uint4*>(lrow1 + ch * 2048) = v10;
+          *reinterpret_cast<uint4*>(lrow1 + (ch + 1) * 2048) = v11;
+        }
         if (p.feat_out) {
           if (valid0) {
             uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (env * kTok + oh0 * kW2 + ow0) * kD + c0 + 16 * hb);
@@ -1158,6 +1165,12 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
           }
         }
       }
+    }
+    if constexpr (!FULL) {
+      // chain only: the next iteration's barriers order these TMEM reads before the next MMA
+      tc_fence_before();
+      __syncthreads();
+      continue;
     }
     tc_fence_before();
     fence_async_smem();
@@ -1266,7 +1279,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     mbar_wait_bounded(&s.bar1, ph1);
     mbar_wait_bounded(&s.bar2, ph2);
   }
-  if (p.act_mode == GLAD_ACT_DYNAMIC) {
+  if (FULL && p.act_mode == GLAD_ACT_DYNAMIC) {
     // one atomic per CTA on the query projector's absmax slot
     const float m = warp_max(zmax_qp);
     __syncthreads();
@@ -1303,10 +1316,10 @@ int front_fused_blocks_per_sm() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (have[dev]) return cached[dev];
   static bool done[64] = {false};
-  if (allow_max_smem((const void*)front_fused_kernel, done) != cudaSuccess) return 0;
+  if (allow_max_smem((const void*)front_fused_kernel<true>, done) != cudaSuccess) return 0;
   cudaFuncAttributes a;
   cudaDeviceProp pr;
-  if (cudaFuncGetAttributes(&a, (const void*)front_fused_kernel) != cudaSuccess ||
+  if (cudaFuncGetAttributes(&a, (const void*)front_fused_kernel<true>) != cudaSuccess ||
       cudaGetDeviceProperties(&pr, dev) != cudaSuccess) {
     cudaGetLastError();
     return 0;
@@ -1325,14 +1338,23 @@ int front_fused_blocks_per_sm() {
   return n;
 }
 
+// The QuantCNN chain through the pipelined kernel (x_nhwc rows, P = 0).
+cudaError_t launch_chain(const FrontParams& p, int grid, cudaStream_t st) {
+  static bool done_c[64] = {false};
+  cudaError_t e = allow_max_smem((const void*)front_fused_kernel<false>, done_c);
+  if (e != cudaSuccess) return e;
+  return launch_k(front_fused_kernel<false>, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
+                  false, p);
+}
+
 template <int MODE>
 cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool pdl) {
   if constexpr (MODE == kModeFront) {
     // the fused forward's front runs the pipelined kernel
     static bool done_f[64] = {false};
-    cudaError_t e = allow_max_smem((const void*)front_fused_kernel, done_f);
+    cudaError_t e = allow_max_smem((const void*)front_fused_kernel<true>, done_f);
     if (e != cudaSuccess) return e;
-    return launch_k(front_fused_kernel, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
+    return launch_k(front_fused_kernel<true>, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
                     pdl, p);
   } else {
     const size_t smem = front_smem_bytes();

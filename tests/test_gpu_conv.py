@@ -93,3 +93,36 @@ def test_conv_rejects_bad_arguments(dw):
     with pytest.raises(ValueError):
         N.check(lib.glad_conv1_fused_q(None, 4, dw.conv(), None, N.stream_handle()))
     assert lib.glad_conv1_fused_q(None, 0, dw.conv(), None, N.stream_handle()) == 0
+
+
+def test_conv_chain_large_batch(dw, golden_weights):
+    """B=16384 (the largest conv-only batch): sampled environments equal the oracle
+    (z8 within one step at ties, fp16 features within one ulp given the kernel's z8)
+    and equal the same environments run as a small batch."""
+    B = 16384
+    x = _x_nhwc(B, 2024).cuda()
+    feat = torch.empty(B * 187, 64, dtype=torch.float16, device="cuda")
+    z8 = torch.empty(B * 187, 16, dtype=torch.int8, device="cuda")
+    N.check(N.load().glad_conv_chain(x.data_ptr(), B, dw.conv(), feat.data_ptr(), z8.data_ptr(),
+                                     N.stream_handle()))
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(0)
+    envs = np.sort(rng.choice(B, size=24, replace=False))
+    xs = x[torch.from_numpy(envs).cuda()].contiguous()
+    w = golden_weights
+    ref_z8 = O.conv1_fused_q(xs.cpu().numpy(), w["map_cnn.w1p"], w["map_cnn.b1f"], w["map_cnn.qa"],
+                             w["map_cnn.qc"])
+    got_z8 = z8.view(B, 187, 16)[torch.from_numpy(envs).cuda()].reshape(-1, 16).cpu().numpy()
+    d = np.abs(got_z8.astype(np.int16) - ref_z8.astype(np.int16))
+    assert d.max() <= 1 and (d > 0).mean() < 1e-3
+    ref_feat = O.conv2_int8_fused(got_z8, w["map_cnn.w8"], w["map_cnn.dq"], w["map_cnn.b2f"],
+                                  w["map_cnn.a2"], w["map_cnn.c2"])
+    got_feat = feat.view(B, 187, 64)[torch.from_numpy(envs).cuda()].reshape(-1, 64).cpu().numpy()
+    fp16_ulp_close(got_feat, ref_feat)
+    f2 = torch.empty(len(envs) * 187, 64, dtype=torch.float16, device="cuda")
+    z2 = torch.empty(len(envs) * 187, 16, dtype=torch.int8, device="cuda")
+    N.check(N.load().glad_conv_chain(xs.data_ptr(), len(envs), dw.conv(), f2.data_ptr(), z2.data_ptr(),
+                                     N.stream_handle()))
+    torch.cuda.synchronize()
+    assert np.array_equal(z2.cpu().numpy(), got_z8)
+    assert np.array_equal(f2.cpu().numpy(), got_feat)
