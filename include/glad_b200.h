@@ -247,6 +247,32 @@ int glad_actor_forward_noalloc(const GladActorWeights* w, const void* obs, int o
  * (0 = fine; bits = a bounded wait ran out). Synchronises `stream`.        */
 int glad_workspace_status(const void* workspace, uint32_t* status, void* stream);
 
+/* ---- W4A16 actor MLP (no reference implementation: INT4 is named only as
+ * future work in the reference, README.md:259) ------------------------------
+ * Format: q int4 in [-8, 7], packed two per byte along K (q[n,2j] in the low
+ * nibble of byte j of row n), one fp16 scale per 64 consecutive inputs of a
+ * row (the last group of a row may be shorter); W'[n,k] = fp16(q * s). The
+ * layer computes y = fp16(x @ W'^T + b) with fp32 accumulation; hidden layers
+ * apply ELU in fp16. Shapes are those of the actor MLP: 224->512->256->128->29. */
+typedef struct GladW4Linear {
+  const void* packed;   /* uint8 [N, K/2], 16-byte aligned */
+  const void* scales;   /* fp16 [N, ceil(K/64)] */
+  const void* bias;     /* fp16 [N] or NULL */
+  int in_features, out_features;
+} GladW4Linear;
+
+/* The four W4A16 layers on fp16 rows x [M, ldx] (K = 224) -> mean f32 [M, 29]
+ * (float of the fp16 head output). Any M; no workspace. */
+int glad_w4a16_mlp_forward(const GladW4Linear* mlp, const void* x, int64_t M, int64_t ldx,
+                           float* mean_out, void* stream);
+
+/* The actor forward with the INT8 encoder of glad_actor_forward (its
+ * weights from `w`; w->mlp is not read) and the W4A16 MLP `mlp[4]`. The
+ * workspace is glad_actor_workspace_size(B) bytes.                          */
+int glad_actor_forward_w4a16(const GladActorWeights* w, const GladW4Linear* mlp, const void* obs,
+                             int obs_dtype, int64_t B, int64_t ld_obs, int act_mode, float* mean_out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- weight refresh (qrt/runtime.py:195-271) ------------------------------- */
 
 /* QuantLinear.requantize_ (qrt/qlinear.py:84-102) in place, for `n` layers in

@@ -376,3 +376,47 @@ def critic_forward(obs, Wt: GladWeights, act_mode="dynamic", aux=None):
         if i < 3:
             h = _elu16(h)
     return h.astype(f32)
+
+
+# -- W4A16 actor MLP ----------------------------------------------------------------
+# No reference implementation exists (INT4 is future work in README.md:259); this is
+# the restatement of the format documented in include/glad_b200.h (GladW4Linear).
+def w4_quantize(W, group=64):
+    """W [N,K] -> (packed uint8 [N,K/2], scales fp16 [N,ceil(K/group)]): s = absmax/7
+    (fp16), q = clamp(rint(W / s), -8, 7), even k in the low nibble."""
+    W = np.asarray(W, np.float32)
+    n, K = W.shape
+    G = -(-K // group)
+    Wp = np.zeros((n, G * group), np.float32)
+    Wp[:, :K] = W
+    s16 = (np.abs(Wp.reshape(n, G, group)).max(axis=-1) / np.float32(7.0)).astype(np.float16)
+    sf = s16.astype(np.float32)
+    sf = np.where(sf > 0, sf, np.float32(1.0))
+    q = np.clip(np.rint(Wp.reshape(n, G, group) / sf[..., None]), -8, 7).astype(np.int16).reshape(n, -1)[:, :K]
+    q = (q & 0xF).astype(np.uint8)
+    return (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8), s16
+
+
+def w4_dequant(packed, scales, K, group=64):
+    """fp16 W' = fp16(q * s)."""
+    lo = (packed & 0xF).astype(np.int16)
+    hi = (packed >> 4).astype(np.int16)
+    q = np.empty((packed.shape[0], K), np.int16)
+    q[:, 0::2] = np.where(lo >= 8, lo - 16, lo)
+    q[:, 1::2] = np.where(hi >= 8, hi - 16, hi)
+    s = np.asarray(scales, np.float16).astype(np.float32)[:, np.arange(K) // group]
+    return (q.astype(np.float32) * s).astype(np.float16)
+
+
+def w4a16_mlp(x16, layers):
+    """layers: 4 x (packed, scales, bias fp16, K). Hidden: fp16(x W'^T + b) then ELU in
+    fp16; head: float(fp16(x W'^T + b)). Accumulation in float64 (the kernel: fp32)."""
+    h = np.asarray(x16, np.float16)
+    for i, (packed, scales, bias, K) in enumerate(layers):
+        Wd = w4_dequant(packed, scales, K).astype(np.float64)
+        y = (h[:, :K].astype(np.float64) @ Wd.T + np.asarray(bias, np.float16).astype(np.float64)).astype(np.float16)
+        if i < 3:
+            yf = y.astype(np.float32)
+            y = np.where(yf > 0, yf, np.expm1(yf)).astype(np.float16)
+        h = y
+    return h.astype(np.float32)

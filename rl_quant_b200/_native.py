@@ -75,6 +75,11 @@ class GladQCNNSrc(Structure):
         ("dtype", c_int32), ("alpha", c_void_p), ("beta", c_void_p)]
 
 
+class GladW4Linear(Structure):
+    _fields_ = [("packed", c_void_p), ("scales", c_void_p), ("bias", c_void_p), ("in_features", c_int),
+                ("out_features", c_int)]
+
+
 class GladCastCopy(Structure):
     _fields_ = [("src", c_void_p), ("dst", c_void_p), ("n", c_int64), ("src_dtype", c_int32),
                 ("dst_dtype", c_int32)]
@@ -96,6 +101,9 @@ SIGNATURES = {
     "glad_actor_forward_train": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                          c_uint64, c_void_p, c_void_p, POINTER(GladActorAux), c_void_p,
                                          c_size_t, c_void_p]),
+    "glad_w4a16_mlp_forward": (c_int, [POINTER(GladW4Linear), c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+    "glad_actor_forward_w4a16": (c_int, [POINTER(GladActorWeights), POINTER(GladW4Linear), c_void_p, c_int,
+                                         c_int64, c_int64, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "glad_critic_workspace_size": (c_size_t, [c_int64]),
     "glad_critic_forward": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                     c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),

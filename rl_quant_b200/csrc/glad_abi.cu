@@ -20,6 +20,8 @@ cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl
 int tail_grid(int64_t B, int sms);
 int front_fused_blocks_per_sm();
 cudaError_t launch_chain(const FrontParams& p, int grid, cudaStream_t st);
+cudaError_t launch_w4mlp(const GladW4Linear (&L)[4], const __half* x, int64_t M, int64_t ldx, float* mean,
+                         int64_t ldm, unsigned int* status, cudaStream_t st, bool pdl);
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
 template <int NT>
@@ -689,6 +691,66 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
     }
     GLAD_CHECK_CUDA(le, "critic MLP launch");
   }
+  return GLAD_OK;
+}
+
+namespace {
+int check_w4(const GladW4Linear* mlp) {
+  if (!mlp) return fail(GLAD_ERR_INVALID_ARG, "W4A16 layers are NULL");
+  const int mk[4] = {224, 512, 256, 128}, mn[4] = {512, 256, 128, kActions};
+  for (int i = 0; i < 4; ++i) {
+    const GladW4Linear& L = mlp[i];
+    if (!L.packed || !L.scales)
+      return fail(GLAD_ERR_INVALID_ARG, "W4A16 layer %d: packed weights and scales must be set", i);
+    if (L.in_features != mk[i] || L.out_features != mn[i])
+      return fail(GLAD_ERR_INVALID_ARG, "W4A16 layer %d: %dx%d, expected %dx%d", i, L.out_features,
+                  L.in_features, mn[i], mk[i]);
+    if (!aligned(L.packed, 16) || !aligned(L.scales, 2) || (L.bias && !aligned(L.bias, 2)))
+      return fail(GLAD_ERR_INVALID_ARG, "W4A16 layer %d: packed weights must be 16-byte aligned", i);
+  }
+  return GLAD_OK;
+}
+}  // namespace
+
+int glad_w4a16_mlp_forward(const GladW4Linear* mlp, const void* x, int64_t M, int64_t ldx, float* mean_out,
+                           void* stream) {
+  g_err[0] = 0;
+  int rc = check_w4(mlp);
+  if (rc) return rc;
+  if (M < 0) return fail(GLAD_ERR_INVALID_ARG, "M must be >= 0");
+  if (M == 0) return GLAD_OK;
+  if (!x || !mean_out) return fail(GLAD_ERR_INVALID_ARG, "x and mean_out must be set");
+  if (ldx < 224 || ldx % 8 != 0 || !aligned(x, 16))
+    return fail(GLAD_ERR_INVALID_ARG, "x: 16-byte aligned rows, ldx a multiple of 8 and >= 224");
+  DeviceInfo d;
+  if ((rc = device_info(&d))) return rc;
+  GladW4Linear L[4] = {mlp[0], mlp[1], mlp[2], mlp[3]};
+  GLAD_CHECK_CUDA(launch_w4mlp(L, reinterpret_cast<const __half*>(x), M, ldx, mean_out, kActions, nullptr,
+                               (cudaStream_t)stream, false),
+                  "W4A16 MLP launch");
+  return GLAD_OK;
+}
+
+int glad_actor_forward_w4a16(const GladActorWeights* w, const GladW4Linear* mlp, const void* obs,
+                             int obs_dtype, int64_t B, int64_t ld_obs, int act_mode, float* mean_out,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  int rc = check_w4(mlp);
+  if (rc) return rc;
+  if (!mean_out) return fail(GLAD_ERR_INVALID_ARG, "mean_out must be set");
+  if (B <= 0) return B == 0 ? GLAD_OK : fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  // the INT8 encoder writes `encoded` into the workspace; then the W4A16 MLP reads it
+  const ActorWs ws = actor_ws(workspace, B);
+  GladActorAux ax{};
+  ax.encoded = ws.enc;
+  if ((rc = actor_forward_impl(w, obs, obs_dtype, B, ld_obs, act_mode, nullptr, nullptr, nullptr, &ax,
+                               workspace, workspace_bytes, stream)))
+    return rc;
+  GladW4Linear L[4] = {mlp[0], mlp[1], mlp[2], mlp[3]};
+  GLAD_CHECK_CUDA(launch_w4mlp(L, ws.enc, B, kEnc, mean_out, kActions,
+                               reinterpret_cast<unsigned int*>(&ws.slots[kSlotStatus]), (cudaStream_t)stream,
+                               true),
+                  "W4A16 MLP launch");
   return GLAD_OK;
 }
 

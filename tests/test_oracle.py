@@ -98,3 +98,21 @@ def test_gumbel16_distribution():
     assert abs(fin.std() - np.pi / np.sqrt(6.0)) < 0.03
     assert np.array_equal(fin, fin.astype(np.float16).astype(np.float32))
     assert not np.array_equal(g, O.gumbel16(seed=1234, offset=1, B=2048))
+
+
+def test_w4_quantize_host_matches_oracle():
+    """The package's W4A16 quantiser (torch) equals the oracle's restatement; the
+    dequantised weights stay within half a scale step of the source."""
+    import torch
+    from rl_quant_b200.w4a16 import quantize_w4
+    rng = np.random.default_rng(3)
+    W = (rng.standard_normal((29, 224)) * 0.05).astype(np.float32)
+    W[3, 64:128] = 0.0                                   # an all-zero group
+    p_ref, s_ref = O.w4_quantize(W)
+    p, s = quantize_w4(torch.from_numpy(W))
+    assert np.array_equal(p.numpy(), p_ref)
+    assert np.array_equal(s.numpy(), s_ref)
+    Wd = O.w4_dequant(p_ref, s_ref, 224).astype(np.float32)
+    step = s_ref.astype(np.float32)[:, np.arange(224) // 64]
+    assert np.all(np.abs(Wd - W) <= step * 0.5 + 1e-3 * step + 1e-8)
+    assert np.all(Wd[3, 64:128] == 0.0)
