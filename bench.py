@@ -59,6 +59,7 @@ def parse():
     p.add_argument("--nbuf", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-conv-chain", action="store_true", help="skip the conv-only (QuantCNN chain) measurement")
+    p.add_argument("--no-w4a16", action="store_true", help="skip the W4A16 large-batch measurement")
     return p.parse_args()
 
 
@@ -177,6 +178,40 @@ def bench_conv_chain(device, hbm_peak, conv_w, reps=50):
         out[str(B)] = {"ms": ms, "env_per_s": B / (ms / 1e3), "achieved_gbs": gbs,
                        "frac_hbm": gbs / hbm_peak, "bytes_per_env": 28094}
         del xs, feats, z8s
+    return out
+
+
+def bench_w4a16(device, hbm_peak, fused, infer, reps=20):
+    """The GLAD actor with a W4A16 actor MLP (int4 weights from seed 3, group 64, fp16
+    activations) at B = 4096 / 16384 / 65536 per GPU: CUDA-event time per call with the
+    obs resident (one buffer per call, each > L2), against 8,816 B/env."""
+    import torch.nn as nn
+    from rl_quant_b200.synthetic import glad_obs
+    from rl_quant_b200.w4a16 import W4A16MLP
+    torch.manual_seed(3)
+    actor = nn.Sequential(nn.Linear(224, 512), nn.ELU(), nn.Linear(512, 256), nn.ELU(), nn.Linear(256, 128),
+                          nn.ELU(), nn.Linear(128, 29)).to(device)
+    mlp = W4A16MLP.from_actor(actor)
+    out = {}
+    for B in (4096, 16384, 65536):
+        nbuf = 4 if B == 4096 else 2
+        base = glad_obs(B, seed=6006).to(device)
+        obs = [base] + [base.roll(k, 0) for k in range(1, nbuf)]
+        mean = torch.empty(B, 29, dtype=torch.float32, device=device)
+        for k in range(3):
+            mlp.actor_forward(fused, obs[k % nbuf], out=mean)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for k in range(reps):
+            mlp.actor_forward(fused, obs[k % nbuf], out=mean)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / reps
+        gbs = B * BYTES_PER_ENV_FWD / (ms / 1e3) / 1e9
+        out[str(B)] = {"ms": ms, "env_per_s": B / (ms / 1e3), "achieved_gbs": gbs, "frac_hbm": gbs / hbm_peak}
+        del obs, base
+        torch.cuda.empty_cache()
     return out
 
 
@@ -388,6 +423,9 @@ def run_ours(args):
         conv_chain = None
         if not args.no_conv_chain:
             conv_chain = bench_conv_chain(device, hbm_peak, fused.weights().conv)
+        w4 = None
+        if not args.no_w4a16:
+            w4 = bench_w4a16(device, hbm_peak, fused, infer)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_fp32 import time_fp32_forward
@@ -426,6 +464,9 @@ def run_ours(args):
             "conv_chain": ({"workload": "QuantCNN chain alone (glad_conv_chain): x_nhwc fp16 -> z8 + fp16 "
                                         "local features; rotating buffers > L2; events per call",
                             "per_batch": conv_chain} if conv_chain else None),
+            "w4a16": ({"workload": "GLAD actor, INT8 encoder + W4A16 actor MLP (int4 weights from seed 3, "
+                                   "group 64, fp16 activations), dynamic s_z, obs resident, events per call",
+                       "per_batch": w4} if w4 else None),
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * n_kernels,
         }
