@@ -22,6 +22,8 @@ int front_fused_blocks_per_sm();
 cudaError_t launch_chain(const FrontParams& p, int grid, cudaStream_t st);
 cudaError_t launch_w4mlp(const GladW4Linear (&L)[4], const __half* x, int64_t M, int64_t ldx, float* mean,
                          int64_t ldm, unsigned int* status, cudaStream_t st, bool pdl);
+cudaError_t launch_f16mlp(const GladLinear16 (&L)[4], const __half* x, int64_t M, int64_t ldx, float* value,
+                          int64_t ldv, unsigned int* status, cudaStream_t st, bool pdl);
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
 template <int NT>
@@ -665,31 +667,12 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   tp.slots = ws.slots;
   GLAD_CHECK_CUDA(launch_tail(tp, tail_grid(B, d.sms), st, true), "tail launch");
 
-  const __half* xs[4] = {enc, ws.h1, ws.h2, ws.h3};
-  const int64_t lds[4] = {kCriticEnc, 512, 256, 128};
-  __half* ys[3] = {ws.h1, ws.h2, ws.h3};
-  for (int i = 0; i < 4; ++i) {
-    HGemmParams g{};
-    g.w = reinterpret_cast<const __half*>(w->mlp[i].weight);
-    g.b = reinterpret_cast<const __half*>(w->mlp[i].bias);
-    g.K = hk[i];
-    g.N = hn[i];
-    g.x = xs[i];
-    g.M = B;
-    g.ldx = lds[i];
-    cudaError_t le;
-    if (i < 3) {
-      g.y = ys[i];
-      g.ldy = hn[i];
-      g.elu = 1;
-      le = hn[i] >= 512 ? launch_hgemm<128>(g, st, true) : hn[i] >= 256 ? launch_hgemm<64>(g, st, true)
-                                                                         : launch_hgemm<32>(g, st, true);
-    } else {
-      g.y32 = value_out;
-      g.ldy32 = 1;
-      le = launch_hgemm<32>(g, st, true);
-    }
-    GLAD_CHECK_CUDA(le, "critic MLP launch");
+  // fp16 critic MLP: one cluster kernel (fp16 activations, tcgen05 kind::f16)
+  {
+    GladLinear16 L[4] = {w->mlp[0], w->mlp[1], w->mlp[2], w->mlp[3]};
+    GLAD_CHECK_CUDA(launch_f16mlp(L, enc, B, kCriticEnc, value_out, 1,
+                                  reinterpret_cast<unsigned int*>(&ws.slots[kSlotStatus]), st, true),
+                    "critic MLP launch");
   }
   return GLAD_OK;
 }
