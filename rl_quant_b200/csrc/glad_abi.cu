@@ -26,9 +26,6 @@ cudaError_t launch_f16mlp(const GladLinear16 (&L)[4], const __half* x, int64_t M
                           int64_t ldv, unsigned int* status, cudaStream_t st, bool pdl);
 template <int NT>
 cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false);
-template <int NT>
-cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st, bool pdl = false);
-size_t hgemm_smem_bytes(int K, int NT);
 size_t qgemm_smem_bytes(int K, int NT);
 cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
                           const float* alpha, const float* beta, int round16, float* slot,

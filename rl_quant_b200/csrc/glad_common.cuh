@@ -319,20 +319,6 @@ struct TailParams {
   float* slots;
 };
 
-// fp16 Linear (+ bias, optional ELU) as a tcgen05 kind::f16 GEMM.
-struct HGemmParams {
-  const __half* w;         // [N, K] row-major
-  const __half* b;         // [N] or null
-  int K, N;
-  const __half* x;         // [M, K] row stride ldx
-  int64_t M, ldx;
-  __half* y;               // [M, ldy] fp16 out (or null)
-  int64_t ldy;
-  float* y32;              // [M, ldy32] float(fp16 out) (or null)
-  int64_t ldy32;
-  int elu;
-};
-
 struct GemmParams {
   GladQLinear L;
   int act_mode;

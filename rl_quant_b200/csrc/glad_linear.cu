@@ -226,169 +226,6 @@ template cudaError_t launch_qgemm<128>(const GemmParams&, cudaStream_t, bool);
 template cudaError_t launch_qgemm<64>(const GemmParams&, cudaStream_t, bool);
 template cudaError_t launch_qgemm<32>(const GemmParams&, cudaStream_t, bool);
 
-// ---- fp16 Linear on tcgen05 (kind::f16) -------------------------------------------
-// The critic MLP is not quantised (qrt/integration.py:42-43): y = x W^T + b in
-// fp32 with one rounding to fp16, then ELU. Same tiling as the int8 GEMM:
-//   A: [Kp/8 chunks][128 rows][16 B]  B: [Kp/8 chunks][NT rows][16 B]
-template <int NT>
-__global__ void __launch_bounds__(kGemmThreads, 1) hgemm_kernel(const __grid_constant__ HGemmParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const int K = p.K;
-  const int Kp = (K + 15) & ~15;         // MMA K-step of 16 halves (zero fill)
-  uint8_t* As = base;
-  uint8_t* Bs = As + (size_t)Kp * 2 * 128;
-  float* cbias = reinterpret_cast<float*>(Bs + (size_t)Kp * 2 * NT);
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(cbias + NT);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
-  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t m0 = (int64_t)blockIdx.x * 128;
-  const int n0 = blockIdx.y * NT;
-  const int N = p.N;
-  grid_dep_launch();
-  constexpr uint32_t kCols = NT < 32 ? 32 : NT;
-
-  if (warp == 0) tmem_alloc(tmem_slot, kCols);
-  if (tid == 0) {
-    mbar_init(mbar, 1);
-    fence_mbar_init();
-    *abort_flag = 0;
-  }
-  const int kc8 = Kp / 8;
-  // weights
-  for (int idx = tid; idx < NT * kc8; idx += kGemmThreads) {
-    const int c = idx / NT, n = idx - c * NT;
-    __align__(16) __half v[8];
-    const __half* src = p.w + (int64_t)(n0 + n) * K + c * 8;
-    const bool row = n0 + n < N;
-    if (row && c * 8 + 8 <= K && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-      *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(src);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = (row && c * 8 + e < K) ? src[e] : __float2half(0.0f);
-    }
-    *reinterpret_cast<uint4*>(Bs + c * (NT * 16) + n * 16) = *reinterpret_cast<const uint4*>(v);
-  }
-  for (int j = tid; j < NT; j += kGemmThreads)
-    cbias[j] = (p.b && n0 + j < N) ? __half2float(p.b[n0 + j]) : 0.0f;
-  grid_dep_wait();                      // the producer of x is done
-  // activations (batched loads, see the int8 GEMM)
-  constexpr int kUh = 8;
-  const int totalh = 128 * kc8;
-  for (int base_idx = 0; base_idx < totalh; base_idx += kUh * kGemmThreads) {
-    uint4 v[kUh];
-#pragma unroll
-    for (int u = 0; u < kUh; ++u) {
-      const int idx = base_idx + u * kGemmThreads + tid;
-      const int r = idx / kc8, c = idx - r * kc8;
-      const int64_t m = m0 + r;
-      const __half* src = p.x + m * p.ldx + c * 8;
-      const bool row = idx < totalh && m < p.M;
-      if (row && c * 8 + 8 <= K && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-        v[u] = *reinterpret_cast<const uint4*>(src);
-      } else {
-        __align__(16) __half t[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) t[e] = (row && c * 8 + e < K) ? src[e] : __float2half(0.0f);
-        v[u] = *reinterpret_cast<const uint4*>(t);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kUh; ++u) {
-      const int idx = base_idx + u * kGemmThreads + tid;
-      if (idx >= totalh) continue;
-      const int r = idx / kc8, c = idx - r * kc8;
-      *reinterpret_cast<uint4*>(As + c * 2048 + r * 16) = v[u];
-    }
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
-    const uint32_t ab = smem_u32(As), bb = smem_u32(Bs);
-    constexpr uint32_t idesc = idesc_f16(128, NT);
-    for (int kk = 0; kk < Kp / 16; ++kk) {
-      const uint64_t ad = smem_desc(ab + kk * 2 * 2048, 2048, 128);
-      const uint64_t bd = smem_desc(bb + kk * 2 * NT * 16, NT * 16, 128);
-      mma_f16(tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
-    }
-    mma_commit(mbar);
-  }
-  const bool ok = mbar_wait_bounded(mbar, 0);
-  if (!ok) *abort_flag = 1;
-  tc_fence_after();
-  __syncthreads();
-  if (!*abort_flag) {
-    const int quarter = warp & 3, half = warp >> 2;
-    const int64_t m = m0 + 32 * quarter + lane;
-    const bool row_ok = m < p.M;
-    static_assert(NT % 32 == 0, "N tile must be a multiple of 32");
-    constexpr int kHalfCols = NT / 2;
-#pragma unroll 1
-    for (int cb = 0; cb < kHalfCols / 16; ++cb) {
-      const int col0 = half * kHalfCols + cb * 16;
-      uint32_t rr[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + col0, rr);
-      tmem_ld_wait();
-      __align__(16) __half h[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        h[j] = __float2half_rn(__uint_as_float(rr[j]) + cbias[col0 + j]);
-        if (p.elu) h[j] = elu16(h[j]);
-      }
-      if (row_ok) {
-        const int nb = n0 + col0;
-        if (p.y) {
-          __half* dst = p.y + m * p.ldy + nb;
-          if (nb + 16 <= N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-            reinterpret_cast<uint4*>(dst)[0] = reinterpret_cast<const uint4*>(h)[0];
-            reinterpret_cast<uint4*>(dst)[1] = reinterpret_cast<const uint4*>(h)[1];
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (nb + j < N) dst[j] = h[j];
-          }
-        }
-        if (p.y32) {
-          float* dst = p.y32 + m * p.ldy32 + nb;
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (nb + j < N) dst[j] = __half2float(h[j]);
-        }
-      }
-    }
-  }
-  if (*abort_flag) mbar_wait_bounded(mbar, 0);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kCols);
-  }
-}
-
-size_t hgemm_smem_bytes(int K, int NT) {
-  const size_t Kp = (size_t)((K + 15) & ~15);
-  return Kp * 2 * 128 + Kp * 2 * NT + NT * sizeof(float) + 64 + 128;
-}
-
-template <int NT>
-cudaError_t launch_hgemm(const HGemmParams& p, cudaStream_t st, bool pdl) {
-  const size_t smem = hgemm_smem_bytes(p.K, NT);
-  static bool done[64] = {false};
-  cudaError_t e = allow_max_smem((const void*)hgemm_kernel<NT>, done);
-  if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((p.M + 127) / 128), (unsigned)((p.N + NT - 1) / NT));
-  return launch_k(hgemm_kernel<NT>, grid, dim3(kGemmThreads), smem, st, pdl, p);
-}
-template cudaError_t launch_hgemm<128>(const HGemmParams&, cudaStream_t, bool);
-template cudaError_t launch_hgemm<64>(const HGemmParams&, cudaStream_t, bool);
-template cudaError_t launch_hgemm<32>(const HGemmParams&, cudaStream_t, bool);
 
 // ---- dynamic absmax of alpha*x + beta over [M, K] ---------------------------------------
 // `round16`: the input is first rounded to fp16 (the .half() cast in front of
