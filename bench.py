@@ -225,7 +225,9 @@ def run_ours(args):
 
     rank, local, world = rank_info()
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     B = args.batch
@@ -421,10 +423,10 @@ def run_ours(args):
         fwd_gbs = BYTES_PER_ENV_FWD * B / (ms_step / 1e3) / 1e9
         tops = MACS_PER_ENV * 2 * B / (ms_step / 1e3) / 1e12
         conv_chain = None
-        if not args.no_conv_chain:
+        if world == 1 and not args.no_conv_chain:
             conv_chain = bench_conv_chain(device, hbm_peak, fused.weights().conv)
         w4 = None
-        if not args.no_w4a16:
+        if world == 1 and not args.no_w4a16:
             w4 = bench_w4a16(device, hbm_peak, fused, infer)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
