@@ -147,6 +147,40 @@ class InferenceRunner:
         return self._call("act", self._act_fn, policy_obs)
 
     @torch.inference_mode()
+    def act_host(self, host_obs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``act`` for observations in host memory: the rows are copied straight into
+        the captured graph's input buffer (pinned memory makes the copy asynchronous)
+        and the means straight back into ``out`` (host [B, num_actions] fp32; pinned
+        if allocated here). Returns ``out``; its copy completes on the current stream,
+        so synchronise before reading it."""
+        if host_obs.is_cuda:
+            raise ValueError("act_host takes host observations; use act for device tensors")
+        dev = self._device()
+        B = host_obs.shape[0]
+        if out is None:
+            out = torch.empty(B, 29, dtype=torch.float32, pin_memory=True)
+        if self.mode == "eager":
+            x = host_obs.to(dev, non_blocking=True)
+            out.copy_(self._act_fn(x), non_blocking=True)
+            return out
+        k = ("act", tuple(host_obs.shape), host_obs.dtype, dev)
+        g = self._graphs.get(k)
+        if g is None:
+            g = _Graph(self._act_fn, host_obs.to(dev))
+            self._graphs[k] = g
+        g.static_in.copy_(host_obs, non_blocking=True)
+        g.graph.replay()
+        out.copy_(g.out, non_blocking=True)
+        return out
+
+    def _device(self):
+        for t in self.model.parameters():
+            return t.device
+        for t in self.model.buffers():
+            return t.device
+        return torch.device("cuda")
+
+    @torch.inference_mode()
     def evaluate(self, critic_obs):
         if not self.with_critic:
             raise RuntimeError("evaluate needs InferenceRunner(with_critic=True)")

@@ -123,6 +123,21 @@ def test_runner_act_matches_reference(gm, golden_fwd, mode):
         assert np.abs(mean - ref).max() <= 1e-2 and cos(mean, ref) >= 0.99999
 
 
+@pytest.mark.parametrize("mode", ["eager", "manual-graph"])
+def test_runner_act_host_equals_act(gm, golden_fwd, mode):
+    """act_host (host obs straight into the graph input, means straight back) gives the
+    means of act on the same observations."""
+    m, _ = gm
+    r = InferenceRunner(m, mode=mode)
+    d = golden_fwd[16]
+    po = torch.from_numpy(d["policy_obs"]).float()
+    out = r.act_host(po.pin_memory())
+    torch.cuda.synchronize()
+    assert torch.equal(out, r.act(po.cuda()).cpu())
+    with pytest.raises(ValueError):
+        r.act_host(po.cuda())
+
+
 def test_patched_encoder_outputs(gm, golden_fwd):
     m, _ = gm
     d = golden_fwd[16]
