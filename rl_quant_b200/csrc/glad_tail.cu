@@ -17,9 +17,12 @@
 
 namespace glad {
 
-constexpr int kTailEnvs = 8;                 // environments per CTA (= warps)
-constexpr int kTailThreads = 32 * kTailEnvs;
-constexpr int kTailRows = 32 * kTailEnvs;    // GEMM rows per CTA
+constexpr int kTailWarps = 8;                // one warp per environment slot
+constexpr int kTailThreads = 32 * kTailWarps;
+constexpr int kTailRows = 32 * kTailWarps;   // GEMM rows per CTA
+// Environments per group: 7 of the 8 warp slots, so that 4096 environments make 586
+// groups = two per resident CTA (2 per SM x 148) with no third wave; slot 7 is idle.
+constexpr int kTailEnvs = 7;
 constexpr int kTailTmemCols = 256;           // tile t: columns [128t, 128t+128): conv2, then K|V
 
 struct __align__(128) TailSmem {
@@ -40,11 +43,11 @@ struct __align__(128) TailSmem {
   float bin[192], bout[64];
   float wsq[64];                  // scorer weight, query half
   float a0_a[232], a0_b[232];
-  float qv[kTailEnvs][64];        // query (fp16 values)
-  float qm[kTailEnvs][64];        // MHA query projection (fp16 values)
-  float om[kTailEnvs][64];        // attention output (fp16 values)
-  uint32_t keys[kTailEnvs][32];
-  int sel[kTailEnvs][32];
+  float qv[kTailWarps][64];        // query (fp16 values)
+  float qm[kTailWarps][64];        // MHA query projection (fp16 values)
+  float om[kTailWarps][64];        // attention output (fp16 values)
+  uint32_t keys[kTailWarps][32];
+  int sel[kTailWarps][32];
   uint64_t mbar;
   uint32_t tmem_base;
   int abort_flag;
@@ -168,7 +171,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   const int64_t ngroups = (p.B + kTailEnvs - 1) / kTailEnvs;
   for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x) {
     const int64_t env = g * kTailEnvs + warp;
-    const bool have = env < p.B;
+    const bool have = warp < kTailEnvs && env < p.B;
     const int r = 32 * warp + lane;              // GEMM row of this thread
     if (have) {
       // ---- 1. query projector: W8A8 over cat(gc, pe) ---------------------------------
@@ -436,7 +439,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     if (tid == 0) {
       float mm = s.qv[0][0];
 #pragma unroll
-      for (int w = 1; w < kTailEnvs; ++w) mm = fmaxf(mm, s.qv[w][0]);
+      for (int w = 1; w < kTailWarps; ++w) mm = fmaxf(mm, s.qv[w][0]);
       if (mm > 0.0f) atomic_max_nonneg(&p.slots[2], mm);
     }
   }
