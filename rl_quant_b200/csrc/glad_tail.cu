@@ -174,6 +174,13 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     const bool have = warp < kTailEnvs && env < p.B;
     const int r = 32 * warp + lane;              // GEMM row of this thread
     if (have) {
+      // this environment's local scores, loaded first (used after the two GEMVs)
+      __half sl[6];
+#pragma unroll
+      for (int j = 0; j < 6; ++j) {
+        const int i = lane + 32 * j;
+        sl[j] = i < kTok ? p.score_local[env * kTok + i] : __float2half(0.0f);
+      }
       // ---- 1. query projector: W8A8 over cat(gc, pe) ---------------------------------
       const __half* gc = p.enc + env * p.ld_enc + 64;
       const __half* pe = p.pe + env * kD;
@@ -224,7 +231,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         const int i = lane + 32 * j;
         key[j] = 0;
         if (i < kTok) {
-          float lg = fp16r(__fadd_rn(__half2float(p.score_local[env * kTok + i]), sq));
+          float lg = fp16r(__fadd_rn(__half2float(sl[j]), sq));
           if (p.gumbel) lg = fp16r(__fadd_rn(lg, gumbel16(p.gumbel_seed, g_offset, env, i)));
           else if (p.noise) lg = fp16r(__fadd_rn(lg, p.noise[env * kTok + i]));
           const __half lh = __float2half_rn(lg);
@@ -375,13 +382,27 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         sc[4 * cb + hh] = fp16r(__fmul_rn(fp16r(d), 0.5f));
       }
     }
+    // softmax over the 32 tokens of every head: the 16 heads' butterflies interleaved
+    float red[kHeads];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) red[h] = sc[h];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) red[h] = fmaxf(red[h], __shfl_xor_sync(0xffffffffu, red[h], o));
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+      sc[h] = expf(sc[h] - red[h]);
+      red[h] = sc[h];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) red[h] += __shfl_xor_sync(0xffffffffu, red[h], o);
     float asum = 0.0f;
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) {
-      const float mx = warp_max(sc[h]);
-      const float ex = expf(sc[h] - mx);
-      const float sm = warp_sum(ex);
-      const float a = fp16r(__fdiv_rn(ex, sm));
+      const float a = fp16r(__fdiv_rn(sc[h], red[h]));
       asum += a;
       sc[h] = a;
     }
