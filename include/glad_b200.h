@@ -178,6 +178,22 @@ int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype
                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Actor and critic of one rollout step (eval mode) from ONE read of the
+ * height scan: the policy group `policy_obs` [B, 96+2079] supplies the scan,
+ * the actor proprio and the actor head; the critic group `critic_obs` (row
+ * stride ld_critic) supplies only its first P_c proprio columns -- its scan
+ * must equal the policy group's, as in the reference's benchmarks
+ * (qrt/bench/_common.py:60). The encoder weights (conv, GPS, scorer, query
+ * projector, MHA) are taken from `wa` for both heads (GLAD shares them);
+ * `wc` supplies the fp16 critic proprio embedding and critic MLP. Results are
+ * those of glad_actor_forward + glad_critic_forward. No counterpart in the
+ * reference, which encodes the shared scan twice.                           */
+size_t glad_actor_critic_workspace_size(int64_t B);
+int glad_actor_critic_forward(const GladActorWeights* wa, const GladCriticWeights* wc, const void* policy_obs,
+                              const void* critic_obs, int obs_dtype, int64_t B, int64_t ld_policy,
+                              int64_t ld_critic, int act_mode, float* mean_out, float* value_out,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Train-mode rollout forward (qrt/encoder_opt.py:87-91 with qrt's default
  * rollout_training=True): as glad_actor_forward, with the Gumbel term drawn
  * inside the kernel instead of read from memory. Token i of environment e

@@ -104,6 +104,10 @@ SIGNATURES = {
     "glad_w4a16_mlp_forward": (c_int, [POINTER(GladW4Linear), c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "glad_actor_forward_w4a16": (c_int, [POINTER(GladActorWeights), POINTER(GladW4Linear), c_void_p, c_int,
                                          c_int64, c_int64, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "glad_actor_critic_workspace_size": (c_size_t, [c_int64]),
+    "glad_actor_critic_forward": (c_int, [POINTER(GladActorWeights), POINTER(GladCriticWeights), c_void_p,
+                                          c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p,
+                                          c_void_p, c_size_t, c_void_p]),
     "glad_critic_workspace_size": (c_size_t, [c_int64]),
     "glad_critic_forward": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                     c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),

@@ -337,7 +337,18 @@ int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int 
 
 size_t glad_actor_workspace_size(int64_t B) { return actor_ws(nullptr, B < 0 ? 0 : B).bytes; }
 
+constexpr int kCriticEnc = 232;   // encoded row stride of the critic (128 + P <= 232)
+
 namespace {
+// Fused actor + critic: the critic head's inputs and outputs (eval mode).
+struct DualArgs {
+  const GladCriticWeights* wc;
+  const void* critic_obs;
+  int64_t ld_c;
+  float* value_out;
+  __half* pe_c;          // [B, 64]
+  __half* enc_c;         // [B, 232]
+};
 struct GumbelArgs {
   uint64_t seed;
   unsigned long long* offset;
@@ -345,7 +356,7 @@ struct GumbelArgs {
 int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
                        int64_t ld_obs, int act_mode, const float* topk_noise, const GumbelArgs* gumbel,
                        float* mean_out, const GladActorAux* aux, void* workspace,
-                       size_t workspace_bytes, void* stream);
+                       size_t workspace_bytes, void* stream, const DualArgs* dual = nullptr);
 }  // namespace
 
 int glad_actor_forward(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
@@ -369,11 +380,50 @@ int glad_actor_forward_train(const GladActorWeights* w, const void* obs, int obs
                             workspace_bytes, stream);
 }
 
+size_t glad_actor_critic_workspace_size(int64_t B) {
+  const int64_t b = B < 0 ? 0 : B;
+  return actor_ws(nullptr, b).bytes + up256((size_t)b * kD * 2) + up256((size_t)b * kCriticEnc * 2);
+}
+
+int glad_actor_critic_forward(const GladActorWeights* wa, const GladCriticWeights* wc, const void* policy_obs,
+                              const void* critic_obs, int obs_dtype, int64_t B, int64_t ld_policy,
+                              int64_t ld_critic, int act_mode, float* mean_out, float* value_out,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!wc) return fail(GLAD_ERR_INVALID_ARG, "critic weights are NULL");
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (B == 0) return GLAD_OK;
+  if (!mean_out || !value_out || !critic_obs) return fail(GLAD_ERR_INVALID_ARG, "mean_out, value_out and critic_obs must be set");
+  const GladLinear16& pe = wc->proprio_emb;
+  if (!pe.weight) return fail(GLAD_ERR_INVALID_ARG, "the critic proprio embedding must be the fp16 Linear");
+  const int Pc = pe.in_features;
+  if (Pc < 1 || Pc > 104 || pe.out_features != kD)
+    return fail(GLAD_ERR_INVALID_ARG, "critic proprio embedding %dx%d; 1..104 inputs, 64 outputs", pe.out_features, Pc);
+  const int hk[4] = {128 + Pc, 512, 256, 128}, hn[4] = {512, 256, 128, 1};
+  for (int i = 0; i < 4; ++i) {
+    const GladLinear16& L = wc->mlp[i];
+    if (!L.weight || L.in_features != hk[i] || L.out_features != hn[i])
+      return fail(GLAD_ERR_INVALID_ARG, "critic MLP layer %d must be fp16 %dx%d", i, hn[i], hk[i]);
+  }
+  if (ld_critic < Pc) return fail(GLAD_ERR_INVALID_ARG, "ld_critic %lld < %d", (long long)ld_critic, Pc);
+  if (!aligned(critic_obs, obs_dtype == GLAD_DTYPE_F32 ? 4 : 2))
+    return fail(GLAD_ERR_INVALID_ARG, "critic_obs is not element-aligned");
+  const size_t need = glad_actor_critic_workspace_size(B);
+  if (!workspace || workspace_bytes < need)
+    return fail(GLAD_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  const size_t abytes = actor_ws(nullptr, B).bytes;
+  uint8_t* extra = reinterpret_cast<uint8_t*>(workspace) + abytes;
+  DualArgs dual{wc, critic_obs, ld_critic, value_out, reinterpret_cast<__half*>(extra),
+                reinterpret_cast<__half*>(extra + up256((size_t)B * kD * 2))};
+  return actor_forward_impl(wa, policy_obs, obs_dtype, B, ld_policy, act_mode, nullptr, nullptr, mean_out,
+                            nullptr, workspace, abytes, stream, &dual);
+}
+
 namespace {
 int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
                        int64_t ld_obs, int act_mode, const float* topk_noise, const GumbelArgs* gumbel,
                        float* mean_out, const GladActorAux* aux, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+                       size_t workspace_bytes, void* stream, const DualArgs* dual) {
   if (!w) return fail(GLAD_ERR_INVALID_ARG, "weights are NULL");
   if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
   if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
@@ -453,6 +503,17 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
   fp.pe_absmax = pe_absmax_in_front ? 1 : 0;
+  if (dual) {
+    fp.dual = 1;
+    fp.in_c = dual->critic_obs;
+    fp.ld_c = dual->ld_c;
+    fp.prop_dim_c = dual->wc->proprio_emb.in_features;
+    fp.pec_w = reinterpret_cast<const __half*>(dual->wc->proprio_emb.weight);
+    fp.pec_b = reinterpret_cast<const __half*>(dual->wc->proprio_emb.bias);
+    fp.ld_enc_c = kCriticEnc;
+    fp.enc_c = dual->enc_c;
+    fp.pe_c_out = dual->pe_c;
+  }
   GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, fgrid, st, front_pdl), "front launch");
   stage_mark(2, st);
 
@@ -469,6 +530,7 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.a0_alpha = w->mlp[0].alpha;
   tp.a0_beta = w->mlp[0].beta;
   tp.a0_absmax = 1;
+  tp.qp_slot = 1;
   tp.act_mode = act_mode;
   tp.ld_enc = kEnc;
   tp.prop_dim = P;
@@ -533,6 +595,26 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
     }
     stage_mark(4 + i, st);
   }
+  if (dual) {
+    // critic head on the shared front: its own query, top-32, attention, fp16 MLP
+    TailParams tc = tp;
+    tc.a0_absmax = 0;
+    tc.qp_slot = kSlotCriticQp;
+    tc.ld_enc = kCriticEnc;
+    tc.prop_dim = dual->wc->proprio_emb.in_features;
+    tc.noise = nullptr;
+    tc.gumbel = 0;
+    tc.pe = dual->pe_c;
+    tc.enc = dual->enc_c;
+    tc.topk_logits_out = nullptr;
+    tc.topk_idx_out = nullptr;
+    tc.attn_w_out = nullptr;
+    GLAD_CHECK_CUDA(launch_tail(tc, tail_grid(B, d.sms), st, true), "critic tail launch");
+    GladLinear16 L[4] = {dual->wc->mlp[0], dual->wc->mlp[1], dual->wc->mlp[2], dual->wc->mlp[3]};
+    GLAD_CHECK_CUDA(launch_f16mlp(L, dual->enc_c, B, kCriticEnc, dual->value_out, 1,
+                                  reinterpret_cast<unsigned int*>(&ws.slots[kSlotStatus]), st, true),
+                    "critic MLP launch");
+  }
   if (ax.act_scales) {
     const float* sz[6] = {w->proprio_emb.s_z, w->query_proj.s_z, w->mlp[0].s_z,
                           w->mlp[1].s_z, w->mlp[2].s_z, w->mlp[3].s_z};
@@ -547,7 +629,6 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
 
 }  // namespace
 
-constexpr int kCriticEnc = 232;   // encoded row stride of the critic (128 + P <= 232)
 
 size_t glad_critic_workspace_size(int64_t B) {
   return actor_ws(nullptr, B < 0 ? 0 : B, kCriticEnc).bytes;
@@ -650,6 +731,7 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   tp.out_w = reinterpret_cast<const __half*>(w->mha_out_w);
   tp.out_b = reinterpret_cast<const __half*>(w->mha_out_b);
   tp.a0_absmax = 0;                 // the critic MLP is fp16: no scale to reduce
+  tp.qp_slot = 1;
   tp.noise = topk_noise;
   tp.act_mode = act_mode;
   tp.ld_enc = kCriticEnc;

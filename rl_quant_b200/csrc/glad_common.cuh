@@ -26,6 +26,7 @@ constexpr int kActions = 29;
 //   4 actor.4, 5 actor.6
 // slots[8]    : device status word (DeviceError bits)
 constexpr int kSlotStatus = 8;
+constexpr int kSlotCriticQp = 7;        // critic query projector absmax (fused actor + critic)
 // slots[16..18] : arrival counters of the fused MLP's grid barriers
 // slots[19]     : arrival counter of the front kernel's proprio-absmax grid barrier
 constexpr int kSlotMlpBarrier = 16;
@@ -275,6 +276,17 @@ struct FrontParams {
   const __half* pe16_b;    // [64]
   int pe_f16;
   int pe_absmax;           // dynamic int8 embedding: reduce slot 0 in-kernel (grid barrier)
+  // actor + critic from one read of the scan (dual != 0): the critic group's proprio
+  // columns come from `in_c`, its fp16 embedding and encoded row are written too
+  int dual;
+  const void* in_c;        // critic obs rows (same dtype as `in`)
+  int64_t ld_c;
+  int prop_dim_c;
+  const __half* pec_w;     // critic proprio embedding fp16 [64, prop_dim_c]
+  const __half* pec_b;     // [64] or null
+  int ld_enc_c;            // row stride of enc_c
+  __half* enc_c;           // [B, ld_enc_c]: writes columns 64..127+prop_dim_c
+  __half* pe_c_out;        // [B, 64]
   GladQLinear qp;          // only alpha/beta are read (absmax of its input)
   int act_mode;
   int ld_enc;              // row stride of `enc` (>= 128 + prop_dim)
@@ -302,6 +314,7 @@ struct TailParams {
   const float* a0_alpha;   // LET of the layer after the encoder (absmax of its input)
   const float* a0_beta;
   int a0_absmax;           // reduce that absmax (an INT8 layer follows the encoder)
+  int qp_slot;             // slot holding the query projector's input absmax
   int act_mode;
   int ld_enc;              // row stride of `enc`
   int prop_dim;            // proprio columns of `enc` (from column 128)

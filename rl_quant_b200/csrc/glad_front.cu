@@ -643,7 +643,7 @@ constexpr int kIssuer = 7 * 32;          // lane 0 of warp 7 issues the conv MMA
 constexpr int kConverters = 7 * 32;      // warps 0-6 stage and convert observation rows
 
 struct __align__(128) FusedSmem {
-  uint8_t planes[2][kPlanesBytes];
+  uint8_t planes[1][kPlanesBytes];     // conv1(e) completes before the conversion of e+1 writes it
   uint8_t w1s[kW1sBytes];
   uint8_t strip[kStripBytes];
   uint8_t w2s[kW2sBytes];
@@ -670,6 +670,12 @@ struct __align__(128) FusedSmem {
   float pe_a[kMaxProp], pe_b[kMaxProp];
   float pe_scale[64], pe_bp[64];
   float qp_a[128], qp_b[128];
+  // fused actor + critic: the critic group's proprio and fp16 embedding
+  alignas(16) uint8_t pec_w[64 * kMaxProp * 2];
+  float pec_bp[64];
+  __half prop16c[2][128];
+  __half pe16c[2][64];
+  alignas(16) uint8_t stage_c[kMaxProp * 4 + 32];
   uint64_t c1_adesc[2][16];            // [planes buffer][tile*8 + K-step]
   uint64_t c1_bdesc[8];
   uint64_t c2_adesc[10];               // [tile*5 + K-step]
@@ -708,6 +714,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const int esz = p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2;
   const int row_elems = P + kMap;
   const bool dyn = p.act_mode == GLAD_ACT_DYNAMIC;
+  const bool dual = FULL && p.dual;
+  const int Pc = dual ? p.prop_dim_c : 0;
   // raw conv weights -> scratch (the local-feature tile is unused until the loop)
   uint8_t* scratch = s.local16;
   for (int i = tid; i < 3 * 64 * 64 / 16; i += NT)
@@ -761,9 +769,17 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       s.qp_b[k] = 0.0f;
     }
   }
-  // the first environment's observation row
+  bool pec_w_async = false;
+  if (dual) {
+    pec_w_async = (kD * Pc) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pec_w) & 15) == 0;
+    if (pec_w_async)
+      for (int i = tid; i < kD * Pc / 8; i += NT)
+        cp_async16(s.pec_w + 16 * i, reinterpret_cast<const uint4*>(p.pec_w) + i);
+  }
+  // the first environment's observation row (and the critic group's proprio columns)
   int64_t env = blockIdx.x;
   if (env < p.B) row_issue(row_stage(p.in, env, p.ld, esz, row_elems, s.stage), tid, NT);
+  if (dual && env < p.B) row_issue(row_stage(p.in_c, env, p.ld_c, esz, Pc, s.stage_c), tid, NT);
   cp_async_commit();
   // dynamic int8 proprio embedding: this CTA's part of the batch absmax of
   // |alpha*fp16(x) + beta| over the proprio columns (qrt/qlinear.py:124-128)
@@ -792,7 +808,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   if (FULL && p.pe_f16 && tid < kD && p.pe16_b) pe16b = __half2float(p.pe16_b[tid]);
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int i = tid; i < 2 * kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
+    for (int i = tid; i < kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
     for (int i = tid; i < kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(s.strip)[i] = z;
     for (int i = tid; i < 16 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.bpool)[i] = z;
     for (int i = tid; i < 8 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.blog)[i] = z;
@@ -833,6 +849,13 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       const int n = tid >> 6, c = (tid & 63) >> 3, e = tid & 7;
       reinterpret_cast<__half*>(s.blog)[(c * 16 + n) * 8 + e] = lgw;
     }
+    if (dual) {
+      if (!pec_w_async) {
+        __half* dw = reinterpret_cast<__half*>(s.pec_w);
+        for (int i = tid; i < kD * Pc; i += NT) dw[i] = p.pec_w[i];
+      }
+      if (tid < kD) s.pec_bp[tid] = p.pec_b ? __half2float(p.pec_b[tid]) : 0.0f;
+    }
     if (!FULL) {
     } else if (p.pe_f16) {
       if (!pe_w_async) {
@@ -851,7 +874,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     if (tid < 32) {
       const int bb = tid >> 4, t = (tid >> 3) & 1, pr = tid & 7;
       const uint32_t c0 = conv1_chunk_off(2 * pr), c1 = conv1_chunk_off(2 * pr + 1);
-      s.c1_adesc[bb][t * 8 + pr] = smem_desc(smem_u32(s.planes[bb]) + c0 + t * 128 * 16, c1 - c0, 128);
+      s.c1_adesc[bb][t * 8 + pr] = smem_desc(smem_u32(s.planes[0]) + c0 + t * 128 * 16, c1 - c0, 128);
     } else if (tid < 40) {
       const int pr = tid - 32;
       s.c1_bdesc[pr] = smem_desc(smem_u32(s.w1s) + pr * 512, 256, 128);
@@ -888,9 +911,15 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
   uint32_t ph1 = 0, ph2 = 0;
   float zmax_qp = 0.0f;
+  float zmax_qpc = 0.0f;                // critic query projector input (dual)
 
   // convert the staged row of `e` into planes[b] / prop16[b]
   auto convert = [&](int64_t e, int b, int nthr) {
+    if (dual) {
+      const RowStage rc = row_stage(p.in_c, e, p.ld_c, esz, Pc, s.stage_c);
+      for (int k = tid; k < Pc; k += nthr)
+        s.prop16c[b][k] = __float2half_rn(esz == 4 ? row_elem<4>(rc, k) : row_elem<2>(rc, k));
+    }
     const RowStage rs = row_stage(p.in, e, p.ld, esz, row_elems, s.stage);
     if (esz == 4 && rs.lo == 0 && rs.hi == (uint32_t)row_elems * 4) {
       // the whole fp32 row is in shared memory
@@ -901,7 +930,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         const int pl = ih & 1, r = ((ih - pl) >> 1) + 1, slot = iw + 2;
         const __half2 h01 = __floats2half2_rn(v0, v1);
         const __half2 h2z = __floats2half2_rn(v2, 0.0f);
-        *reinterpret_cast<uint2*>(s.planes[b] + pl * kPlaneBytes + r * kRowBytes + slot * 8) =
+        *reinterpret_cast<uint2*>(s.planes[0] + pl * kPlaneBytes + r * kRowBytes + slot * 8) =
             make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h2z));
       }
       for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(st[k]);
@@ -925,7 +954,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       uint2 pk;
       pk.x = *reinterpret_cast<uint32_t*>(&h01);
       pk.y = *reinterpret_cast<uint32_t*>(&h2z);
-      *reinterpret_cast<uint2*>(s.planes[b] + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
+      *reinterpret_cast<uint2*>(s.planes[0] + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
     }
     for (int k = tid; k < P; k += nthr)
       s.prop16[b][k] = __float2half_rn(esz == 4 ? row_elem<4>(rs, k) : row_elem<2>(rs, k));
@@ -940,6 +969,19 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         for (int pr = 0; pr < 8; ++pr)
           mma_f16(tmem_c1 + t * 16, s.c1_adesc[b][t * 8 + pr], s.c1_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
       mma_commit(&s.bar1);
+    }
+  };
+  // critic proprio embedding (fp16 nn.Linear) of buffer b on threads 128-255
+  auto critic_emb = [&](int b) {
+    if (tid >= 2 * kD) {
+      const int t = tid - 2 * kD, n = t >> 1, part = t & 1;
+      const __half* wrow = reinterpret_cast<const __half*>(s.pec_w) + n * Pc;
+      const int half_k = (Pc + 1) >> 1;
+      const int k0 = part * half_k, k1 = min(Pc, k0 + half_k);
+      float a = 0.0f;
+      for (int k = k0; k < k1; ++k) a = fmaf(__half2float(s.prop16c[b][k]), __half2float(wrow[k]), a);
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      if (part == 0) s.pe16c[b][n] = __float2half_rn(a + s.pec_bp[n]);
     }
   };
   // proprio embedding of the environment in buffer b (threads 0-127)
@@ -983,6 +1025,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     const int64_t nx = env + gridDim.x;
     if (nx < p.B && tid < kConverters)
       row_issue(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), tid, kConverters);
+    if (dual && nx < p.B && tid < kConverters)
+      row_issue(row_stage(p.in_c, nx, p.ld_c, esz, Pc, s.stage_c), tid, kConverters);
     cp_async_commit();
     issue_conv1(0);
     if (grid_absmax) {
@@ -1008,6 +1052,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       __syncthreads();
     }
     if (FULL) proprio_emb(0);
+    if (dual) critic_emb(0);
   }
 
   int b = 0;
@@ -1071,6 +1116,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       if (warp == 7) {
         named_bar_sync(2, NT);            // planes of e+1 written by warps 0-6
         issue_conv1(b ^ 1);
+        if (dual) critic_emb(b ^ 1);
       } else {
         cp_async_wait_all();
         named_bar_sync(1, kConverters);   // the staged row of e+1 is complete
@@ -1081,8 +1127,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         named_bar_sync(1, kConverters);   // every converter is done with the stage buffer
         const int64_t nn = nxt + gridDim.x;
         if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, kConverters);
+        if (dual && nn < p.B) row_issue(row_stage(p.in_c, nn, p.ld_c, esz, Pc, s.stage_c), tid, kConverters);
         cp_async_commit();
         if (FULL) proprio_emb(b ^ 1);
+        if (dual) critic_emb(b ^ 1);
       }
     }
 
@@ -1264,12 +1312,23 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       s.gc16[tid] = gh;
       p.enc[env * p.ld_enc + 64 + tid] = gh;
       p.pe_out[env * kD + tid] = s.pe16[b][tid];
+      if (dual) {
+        p.enc_c[env * p.ld_enc_c + 64 + tid] = gh;
+        p.pe_c_out[env * kD + tid] = s.pe16c[b][tid];
+      }
     }
     for (int k = tid; k < P; k += NT) p.enc[env * p.ld_enc + 128 + k] = s.prop16[b][k];
+    for (int k = tid; k < Pc; k += NT) p.enc_c[env * p.ld_enc_c + 128 + k] = s.prop16c[b][k];
     __syncthreads();
     if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
       const float x = __half2float(tid < kD ? s.gc16[tid] : s.pe16[b][tid - kD]);
       zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, s.qp_a[tid], s.qp_b[tid]));
+    }
+    if (dual && p.act_mode == GLAD_ACT_DYNAMIC && tid >= 2 * kD) {
+      // the critic's query projector input cat(gc, pe_critic)
+      const int t = tid - 2 * kD;
+      const float x = __half2float(t < kD ? s.gc16[t] : s.pe16c[b][t - kD]);
+      zmax_qpc = fmaxf(zmax_qpc, aq_qp.absz(x, s.qp_a[t], s.qp_b[t]));
     }
   }
 
@@ -1290,6 +1349,18 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
 #pragma unroll
       for (int w = 1; w < 8; ++w) mm = fmaxf(mm, s.wmax[w]);
       if (mm > 0.0f) atomic_max_nonneg(&p.slots[1], mm);
+    }
+    if (dual) {
+      const float mc = warp_max(zmax_qpc);
+      __syncthreads();
+      if (lane == 0) s.wmax[warp] = mc;
+      __syncthreads();
+      if (tid == 0) {
+        float mm = s.wmax[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) mm = fmaxf(mm, s.wmax[w]);
+        if (mm > 0.0f) atomic_max_nonneg(&p.slots[kSlotCriticQp], mm);
+      }
     }
   }
   if (s.abort_flag && tid == 0 && p.slots)

@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   }
   float r_bin = tid < 192 ? __half2float(p.in_b[tid]) : 0.0f;
   grid_dep_wait();                      // outputs of the front kernel are visible from here
-  const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, 1);
+  const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, p.qp_slot);
   cp_async_wait_all();
   __syncthreads();
   conv2_b_relayout(s.w2s, scratch, tid, NT);

@@ -203,3 +203,40 @@ class FusedCritic:
             B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise), value.data_ptr(), None,
             ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
         N.check(rc, "glad_critic_forward")
+
+
+class FusedActorCritic:
+    """Actor and critic of one rollout step from ONE read of the shared height
+    scan (``glad_actor_critic_forward``, eval mode). The critic group must carry
+    the same scan as the policy group (as in the reference's benchmarks); its
+    proprio columns come first. Results equal FusedActor.run + FusedCritic.run."""
+
+    def __init__(self, model: nn.Module):
+        self.actor = FusedActor(model)
+        self.critic = FusedCritic(model)
+        if self.critic.use_actor_emb:
+            raise FusedUnsupported("critic and actor proprio widths agree: the critic reuses the actor "
+                                   "embedding, run the two heads separately")
+        self._ws: dict[tuple, torch.Tensor] = {}
+
+    def run(self, policy_obs: torch.Tensor, critic_obs: torch.Tensor, mean: torch.Tensor,
+            value: torch.Tensor) -> None:
+        N.require_cuda(policy_obs)
+        N.require_cuda(critic_obs)
+        if policy_obs.dtype != critic_obs.dtype or policy_obs.shape[0] != critic_obs.shape[0]:
+            raise ValueError("policy and critic groups must share dtype and batch")
+        if policy_obs.stride(1) != 1 or critic_obs.stride(1) != 1:
+            raise ValueError("observation rows must be contiguous")
+        B = policy_obs.shape[0]
+        key = (B, str(policy_obs.device))
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = torch.empty(N.load().glad_actor_critic_workspace_size(B), dtype=torch.uint8,
+                             device=policy_obs.device)
+            self._ws[key] = ws
+        dt = N.DTYPE_F32 if policy_obs.dtype == torch.float32 else N.DTYPE_F16
+        rc = N.load().glad_actor_critic_forward(
+            self.actor.weights(), self.critic.weights(), policy_obs.data_ptr(), critic_obs.data_ptr(), dt, B,
+            policy_obs.stride(0), critic_obs.stride(0), N.ACT_MODES[self.actor.act_mode], mean.data_ptr(),
+            value.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_handle(policy_obs.device))
+        N.check(rc, "glad_actor_critic_forward")

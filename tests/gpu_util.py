@@ -158,3 +158,28 @@ def actor_forward_train(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, see
     N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
     torch.cuda.synchronize()
     return mean, aux_t
+
+
+def golden_model(w):
+    """fp16 GLAD copy with the golden state dict and the reference's LET plan,
+    swapped/patched through the package API exactly as qrt's integration does."""
+    from oracle import glad_oracle as O
+    from rl_quant_b200 import patch_encoder, swap, swap_cnn
+    from rl_quant_b200.glad_model import build_glad
+    QL = O.GladWeights.QL
+    m = build_glad(seed=0, critic_seed=2).cuda()
+    sd = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in w.items()
+          if not k.startswith(("plan.", "meta.")) and k in m.state_dict()}
+    m.load_state_dict(sd, strict=False)
+    m = m.half().eval()
+    plan = {p: {"s_z": float(w[f"plan.{p}.s_z"]), "alpha": torch.from_numpy(w[f"{p}.alpha"]).cuda(),
+                "beta": torch.from_numpy(w[f"{p}.beta"]).cuda(), "act_mode": "dynamic"} for p in QL}
+    # load the plain weights first (the golden file has the inference copy's params)
+    for p in QL:
+        lin = m.get_submodule(p)
+        lin.weight.data.copy_(torch.from_numpy(w[f"{p}.weight"]))
+        lin.bias.data.copy_(torch.from_numpy(w[f"{p}.bias"]))
+    swapped = swap.apply(m, plan)
+    swap_cnn(m, float(w["meta.s_cnn"]))
+    patch_encoder(m)
+    return m.eval(), swapped

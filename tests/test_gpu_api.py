@@ -14,7 +14,7 @@ from rl_quant_b200.glad_model import build_glad
 from rl_quant_b200.qconv import conv2_int8_acc
 from rl_quant_b200.synthetic import glad_obs
 
-from gpu_util import fp16_ulp_close
+from gpu_util import fp16_ulp_close, golden_model
 
 pytestmark = pytest.mark.gpu
 QL = O.GladWeights.QL
@@ -23,27 +23,6 @@ QL = O.GladWeights.QL
 def cos(a, b):
     a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
     return float((a @ b) / np.sqrt((a @ a) * (b @ b)))
-
-
-def golden_model(w):
-    """fp16 GLAD copy with the golden state dict and the reference's LET plan,
-    swapped/patched through the package API exactly as qrt's integration does."""
-    m = build_glad(seed=0, critic_seed=2).cuda()
-    sd = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in w.items()
-          if not k.startswith(("plan.", "meta.")) and k in m.state_dict()}
-    m.load_state_dict(sd, strict=False)
-    m = m.half().eval()
-    plan = {p: {"s_z": float(w[f"plan.{p}.s_z"]), "alpha": torch.from_numpy(w[f"{p}.alpha"]).cuda(),
-                "beta": torch.from_numpy(w[f"{p}.beta"]).cuda(), "act_mode": "dynamic"} for p in QL}
-    # load the plain weights first (the golden file has the inference copy's params)
-    for p in QL:
-        lin = m.get_submodule(p)
-        lin.weight.data.copy_(torch.from_numpy(w[f"{p}.weight"]))
-        lin.bias.data.copy_(torch.from_numpy(w[f"{p}.bias"]))
-    swapped = swap.apply(m, plan)
-    swap_cnn(m, float(w["meta.s_cnn"]))
-    patch_encoder(m)
-    return m.eval(), swapped
 
 
 @pytest.fixture(scope="module")
