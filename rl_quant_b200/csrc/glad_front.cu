@@ -24,6 +24,8 @@
 // 198 rows); rows outside the 11x17 grid are computed and discarded.
 #include <cuda_runtime.h>
 
+#include <cstddef>
+
 #include "glad_common.cuh"
 
 namespace glad {
@@ -670,12 +672,6 @@ struct __align__(128) FusedSmem {
   float pe_a[kMaxProp], pe_b[kMaxProp];
   float pe_scale[64], pe_bp[64];
   float qp_a[128], qp_b[128];
-  // fused actor + critic: the critic group's proprio and fp16 embedding
-  alignas(16) uint8_t pec_w[64 * kMaxProp * 2];
-  float pec_bp[64];
-  __half prop16c[2][128];
-  __half pe16c[2][64];
-  alignas(16) uint8_t stage_c[kMaxProp * 4 + 32];
   uint64_t c1_adesc[2][16];            // [planes buffer][tile*8 + K-step]
   uint64_t c1_bdesc[8];
   uint64_t c2_adesc[10];               // [tile*5 + K-step]
@@ -687,11 +683,22 @@ struct __align__(128) FusedSmem {
   uint64_t bar1, bar2;                 // conv1 / (conv2, logits, pooling) completion
   uint32_t tmem_base;
   int abort_flag;
+  // fused actor + critic only (launches without it allocate up to `pec_w`): the critic
+  // group's proprio and its fp16 embedding
+  alignas(128) uint8_t pec_w[64 * kMaxProp * 2];
+  float pec_bp[64];
+  __half prop16c[2][128];
+  __half pe16c[2][64];
+  alignas(16) uint8_t stage_c[kMaxProp * 4 + 32];
 };
+// dynamic shared memory of a launch (+128 for the in-kernel alignment)
+constexpr size_t kFusedSmemSingle = offsetof(FusedSmem, pec_w) + 128;
+constexpr size_t kFusedSmemDual = sizeof(FusedSmem) + 128;
 
 // FULL = false: the QuantCNN chain alone (x_nhwc -> z8 -> fp16 local features), the same
 // pipeline without the pooling / embedding stages.
-template <bool FULL>
+// DUAL (with FULL): also the critic head's proprio embedding and encoded row.
+template <bool FULL, bool DUAL>
 __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS)
 front_fused_kernel(const __grid_constant__ FrontParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -714,7 +721,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const int esz = p.in_dtype == GLAD_DTYPE_F32 ? 4 : 2;
   const int row_elems = P + kMap;
   const bool dyn = p.act_mode == GLAD_ACT_DYNAMIC;
-  const bool dual = FULL && p.dual;
+  constexpr bool dual = FULL && DUAL;
   const int Pc = dual ? p.prop_dim_c : 0;
   // raw conv weights -> scratch (the local-feature tile is unused until the loop)
   uint8_t* scratch = s.local16;
@@ -1387,10 +1394,10 @@ int front_fused_blocks_per_sm() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (have[dev]) return cached[dev];
   static bool done[64] = {false};
-  if (allow_max_smem((const void*)front_fused_kernel<true>, done) != cudaSuccess) return 0;
+  if (allow_max_smem((const void*)front_fused_kernel<true, false>, done) != cudaSuccess) return 0;
   cudaFuncAttributes a;
   cudaDeviceProp pr;
-  if (cudaFuncGetAttributes(&a, (const void*)front_fused_kernel<true>) != cudaSuccess ||
+  if (cudaFuncGetAttributes(&a, (const void*)front_fused_kernel<true, false>) != cudaSuccess ||
       cudaGetDeviceProperties(&pr, dev) != cudaSuccess) {
     cudaGetLastError();
     return 0;
@@ -1412,10 +1419,9 @@ int front_fused_blocks_per_sm() {
 // The QuantCNN chain through the pipelined kernel (x_nhwc rows, P = 0).
 cudaError_t launch_chain(const FrontParams& p, int grid, cudaStream_t st) {
   static bool done_c[64] = {false};
-  cudaError_t e = allow_max_smem((const void*)front_fused_kernel<false>, done_c);
+  cudaError_t e = allow_max_smem((const void*)front_fused_kernel<false, false>, done_c);
   if (e != cudaSuccess) return e;
-  return launch_k(front_fused_kernel<false>, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
-                  false, p);
+  return launch_k(front_fused_kernel<false, false>, dim3(grid), dim3(kFrontThreads), kFusedSmemSingle, st, false, p);
 }
 
 template <int MODE>
@@ -1423,9 +1429,16 @@ cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool p
   if constexpr (MODE == kModeFront) {
     // the fused forward's front runs the pipelined kernel
     static bool done_f[64] = {false};
-    cudaError_t e = allow_max_smem((const void*)front_fused_kernel<true>, done_f);
+    static bool done_d[64] = {false};
+    if (p.dual) {
+      cudaError_t e = allow_max_smem((const void*)front_fused_kernel<true, true>, done_d);
+      if (e != cudaSuccess) return e;
+      return launch_k(front_fused_kernel<true, true>, dim3(grid), dim3(kFrontThreads), kFusedSmemDual, st,
+                      pdl, p);
+    }
+    cudaError_t e = allow_max_smem((const void*)front_fused_kernel<true, false>, done_f);
     if (e != cudaSuccess) return e;
-    return launch_k(front_fused_kernel<true>, dim3(grid), dim3(kFrontThreads), sizeof(FusedSmem) + 128, st,
+    return launch_k(front_fused_kernel<true, false>, dim3(grid), dim3(kFrontThreads), kFusedSmemSingle, st,
                     pdl, p);
   } else {
     const size_t smem = front_smem_bytes();
