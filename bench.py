@@ -28,6 +28,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -42,9 +43,9 @@ BYTES_PER_ENV_FWD = 8816          # obs read (fp32) + action mean write, fused i
 MACS_PER_ENV = 2.55e6             # conv1 .. actor MLP (int8 2.02 M + fp16 0.53 M)
 OBS_BYTES_PER_ENV = 2175 * 4      # what the front kernel must read per env
 # DRAM bytes (read + write) per front_fused_kernel launch per environment, from the ncu
-# capture summarised in profiles/front_fused_kernel_glad_b4096.md (35.763 MB read +
-# 0.040 MB written at B=4096); traffic grows with the environments processed.
-FRONT_DRAM_BYTES_PER_ENV = (35.763456e6 + 0.03968e6) / 4096
+# capture summarised in profiles/front_fused_kernel_glad_b4096.md (35.769 MB read +
+# 0.110 MB written at B=4096); traffic grows with the environments processed.
+FRONT_DRAM_BYTES_PER_ENV = (35.768832e6 + 0.109568e6) / 4096
 N_STAGES = ("absmax", "front", "tail", "actor.0", "actor.2", "actor.4", "actor.6")
 
 
@@ -88,21 +89,40 @@ class ClockSampler:
             self.cmd = None
 
     def start(self):
-        if self.cmd:
-            try:
-                self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                             text=True)
-            except OSError:
-                self.proc = None
+        """Start sampling and wait (up to 3 s) for the first sample, so that the
+        sampler's own start-up does not fall inside a short timed region."""
+        if not self.cmd:
+            return
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._reader = threading.Thread(target=self._read, daemon=True)
+        self._reader.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        time.sleep(0.06)                # one more sample period past the timed region
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait(timeout=10)
+        self._reader.join(timeout=10)
         sm, smax, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in out.strip().splitlines():
+        for line in self.lines:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) != len(self.FIELDS):
                 continue
@@ -455,7 +475,8 @@ def run_ours(args):
                        "weights": "seed-0 default init, LET calibrated 200 Adam steps on 512 obs (seed 1)",
                        "l2": f"{args.nbuf} rotating obs buffers ({args.nbuf * B * OBS_BYTES_PER_ENV / 1e6:.0f} MB) > 126 MB L2",
                        "launch": f"CUDA graph per step (memset + {n_kernels} kernels)"},
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * 2175 * 4,
                     "d2h_bytes_per_step": B * 29 * 4},
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": hbm_peak,
