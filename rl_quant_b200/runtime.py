@@ -58,11 +58,51 @@ class _Graph:
         return self.out
 
 
+class _HostPipe:
+    """Captured forwards over ``lanes`` input/output buffer pairs for host
+    observations. Step k uses lane k % lanes: its host-to-device copy runs on a
+    copy stream once the lane's previous forward has read the input, the forward
+    (graph replay) and the device-to-host copy of the means run on the current
+    stream after the copy. With two lanes the copy of step k+1 overlaps the
+    forward of step k; forwards stay in one stream, one after the other."""
+
+    def __init__(self, fn, example_dev, lanes):
+        dev = example_dev.device
+        self.lanes = [_Graph(fn, example_dev.clone()) for _ in range(lanes)]
+        self.copy_stream = torch.cuda.Stream(device=dev)
+        self.in_ready = [torch.cuda.Event() for _ in range(lanes)]
+        self.free = [torch.cuda.Event() for _ in range(lanes)]
+        self.used = [False] * lanes
+        self.i = 0
+
+    def __call__(self, host_obs, out):
+        j = self.i % len(self.lanes)
+        self.i += 1
+        g = self.lanes[j]
+        cur = torch.cuda.current_stream(g.static_in.device)
+        cs = self.copy_stream
+        if self.used[j]:
+            cs.wait_event(self.free[j])
+        with torch.cuda.stream(cs):
+            g.static_in.copy_(host_obs, non_blocking=True)
+        self.in_ready[j].record(cs)
+        cur.wait_event(self.in_ready[j])
+        g.graph.replay()
+        out.copy_(g.out, non_blocking=True)
+        self.free[j].record(cur)
+        self.used[j] = True
+        return out
+
+
 class InferenceRunner:
     def __init__(self, model, mode: str = "max-autotune", with_critic: bool = False,
-                 clone_outputs: bool = False):
+                 clone_outputs: bool = False, host_lanes: int = 2):
         if mode not in _MODES:
             raise ValueError(f"unknown mode: {mode}")
+        if host_lanes < 1:
+            raise ValueError("host_lanes must be >= 1")
+        self.host_lanes = host_lanes
+        self._pipes: dict[tuple, _HostPipe] = {}
         if model.training:
             warnings.warn("[rl_quant_b200] model is in train mode; call model.eval() for rollouts")
         self.model = model
@@ -152,7 +192,9 @@ class InferenceRunner:
         the captured graph's input buffer (pinned memory makes the copy asynchronous)
         and the means straight back into ``out`` (host [B, num_actions] fp32; pinned
         if allocated here). Returns ``out``; its copy completes on the current stream,
-        so synchronise before reading it."""
+        so synchronise before reading it (and before rewriting ``host_obs``).
+        Consecutive calls rotate over ``host_lanes`` captured forwards, so the input
+        copy of one call overlaps the forward of the previous one."""
         if host_obs.is_cuda:
             raise ValueError("act_host takes host observations; use act for device tensors")
         dev = self._device()
@@ -164,14 +206,11 @@ class InferenceRunner:
             out.copy_(self._act_fn(x), non_blocking=True)
             return out
         k = ("act", tuple(host_obs.shape), host_obs.dtype, dev)
-        g = self._graphs.get(k)
-        if g is None:
-            g = _Graph(self._act_fn, host_obs.to(dev))
-            self._graphs[k] = g
-        g.static_in.copy_(host_obs, non_blocking=True)
-        g.graph.replay()
-        out.copy_(g.out, non_blocking=True)
-        return out
+        pipe = self._pipes.get(k)
+        if pipe is None:
+            pipe = _HostPipe(self._act_fn, host_obs.to(dev), self.host_lanes)
+            self._pipes[k] = pipe
+        return pipe(host_obs, out)
 
     def _device(self):
         for t in self.model.parameters():

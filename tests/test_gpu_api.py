@@ -117,6 +117,22 @@ def test_runner_act_host_equals_act(gm, golden_fwd, mode):
         r.act_host(po.cuda())
 
 
+@pytest.mark.parametrize("lanes", [1, 2, 3])
+def test_runner_act_host_pipelined_calls(gm, lanes):
+    """Back-to-back act_host calls without a synchronise in between (the input copy of
+    one call overlapping the forward of the previous one) each return act's means of
+    their own observations."""
+    m, _ = gm
+    r = InferenceRunner(m, mode="manual-graph", host_lanes=lanes)
+    obs = [glad_obs(64, seed=100 + i).float().pin_memory() for i in range(7)]
+    outs = [torch.empty(64, 29, dtype=torch.float32).pin_memory() for _ in obs]
+    for o, out in zip(obs, outs):
+        r.act_host(o, out)
+    torch.cuda.synchronize()
+    for o, out in zip(obs, outs):
+        assert torch.equal(out, r.act(o.cuda()).cpu())
+
+
 def test_patched_encoder_outputs(gm, golden_fwd):
     m, _ = gm
     d = golden_fwd[16]
