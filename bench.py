@@ -355,33 +355,59 @@ def run_ours(args):
             fused.run(a_in[i], means[i])
             fused_critic.run(c_in[i], values[i])
 
-    for i in range(n_ac):
-        ac_step(i)
-    torch.cuda.synchronize()
-    ac_graphs = []
-    with torch.cuda.stream(side):
-        for i in range(n_ac):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=side):
-                ac_step(i)
-            ac_graphs.append(g)
-    torch.cuda.current_stream(device).wait_stream(side)
     k_ac = max(10, min(args.steps, 1000))
-    for k in range(10):
-        ac_graphs[k % n_ac].replay()
-    barrier()
-    e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e4.record()
-    for k in range(k_ac):
-        ac_graphs[k % n_ac].replay()
-    e5.record()
-    barrier()
-    ms_ac = e4.elapsed_time(e5)
-    if world > 1:
-        t = torch.tensor([ms_ac], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_ac = float(t.item())
+
+    def time_graphed(step):
+        """Capture step(i) for each rotating buffer i, then time k_ac replays (max over ranks)."""
+        for i in range(n_ac):
+            step(i)
+        torch.cuda.synchronize()
+        graphs_ = []
+        with torch.cuda.stream(side):
+            for i in range(n_ac):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=side):
+                    step(i)
+                graphs_.append(g)
+        torch.cuda.current_stream(device).wait_stream(side)
+        for k in range(10):
+            graphs_[k % n_ac].replay()
+        barrier()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record()
+        for k in range(k_ac):
+            graphs_[k % n_ac].replay()
+        eb.record()
+        barrier()
+        ms_ = ea.elapsed_time(eb)
+        if world > 1:
+            t = torch.tensor([ms_], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_ = float(t.item())
+        return ms_
+
+    ms_ac = time_graphed(ac_step)
     ac_value = B * world / (ms_ac / k_ac / 1e3)
+
+    # the whole PPO.act transition (rsl_rl/algorithms/ppo.py:129-140): actor + critic,
+    # then the Normal(mean, std) sample and its log-probability (glad_ppo_epilogue)
+    ppo = None
+    if fused_ac is not None:
+        from rl_quant_b200.fused import ppo_epilogue
+        std_t = infer.std.detach().float().contiguous()
+        rng_t = torch.zeros(2, dtype=torch.int64, device=device)
+        acts = [torch.empty(B, 29, dtype=torch.float32, device=device) for _ in range(n_ac)]
+        lps = [torch.empty(B, dtype=torch.float32, device=device) for _ in range(n_ac)]
+        sgs = [torch.empty(B, 29, dtype=torch.float32, device=device) for _ in range(n_ac)]
+
+        def ppo_step(i):
+            fused_ac.run(a_in[i], c_in[i], means[i], values[i])
+            ppo_epilogue(means[i], std_t, 1234 + rank, rng_t, acts[i], lps[i], sgs[i])
+
+        ms_ppo = time_graphed(ppo_step)
+        ppo = {"value": B * world / (ms_ppo / k_ac / 1e3), "unit": UNIT, "ms_per_step": ms_ppo / k_ac,
+               "workload": f"PPO.act transition, B={B} per GPU: fused actor + critic, Normal sample, "
+                           "log-prob, sigma (glad_actor_critic_forward + glad_ppo_epilogue)"}
 
     # end to end through InferenceRunner.act_host with host buffers: every step copies
     # its obs in from pinned host memory and its means back out. Two host lanes: the
@@ -502,6 +528,7 @@ def run_ours(args):
                              "workload": f"actor + critic forward, B={B} per GPU, {world * B} envs" +
                                          (", one read of the shared scan (glad_actor_critic_forward)"
                                           if fused_ac is not None else "")},
+            "ppo_act": ppo,
             "weight_sync": {"ms": sync_ms, "bytes": packed.nbytes,
                             "collective": "nccl broadcast of one packed blob" if world > 1 else "none (1 GPU)",
                             "steps": "cast-copy fp32 master -> fp16 copy + requantise (one CUDA graph) + broadcast",

@@ -209,6 +209,40 @@ int glad_actor_forward_train(const GladActorWeights* w, const void* obs, int obs
                              unsigned long long* gumbel_offset, float* mean_out, const GladActorAux* aux,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Train-mode glad_actor_critic_forward: each head adds its own Gumbel term to
+ * its top-k logits, as the reference's two compiled functions each draw one
+ * (qrt/integration.py:204-216, qrt/encoder_opt.py:87-91). The actor uses
+ * offset *gumbel_offset, the critic *gumbel_offset + 1 (both with the Philox
+ * layout of glad_actor_forward_train); the call adds two to the device word. */
+int glad_actor_critic_forward_train(const GladActorWeights* wa, const GladCriticWeights* wc,
+                                    const void* policy_obs, const void* critic_obs, int obs_dtype,
+                                    int64_t B, int64_t ld_policy, int64_t ld_critic, int act_mode,
+                                    uint64_t gumbel_seed, unsigned long long* gumbel_offset,
+                                    float* mean_out, float* value_out, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/* PPO.act epilogue of a rollout step (rsl_rl/algorithms/ppo.py:129-140): the
+ * action distribution Normal(mean, std) (rsl_rl/modules/actor_critic_encoder.py:
+ * 329-335) sampled once per environment and scored (:366-367):
+ *   actions[e,j]  = mean[e,j] + std[j] * z[e,j]
+ *   log_prob[e]   = sum_j ( -(a-mean)^2 / (2 std^2) - log(std) - log(sqrt(2 pi)) )
+ *   sigma_out[e,j] = std[j]                       (optional, action_sigma)
+ * with every operation in fp32 as torch.distributions.Normal evaluates it; the
+ * sum over the n_actions terms is a fixed butterfly (lane j holds terms j and
+ * j+32; partners 16, 8, 4, 2, 1 apart). z ~ N(0,1) by the Box-Muller transform:
+ * pair q = j/2 of environment e takes words (2(q&1), 2(q&1)+1) of Philox4x32-10
+ * with counter {0x80000000 | q/2, e, e >> 32, offset} and key {seed, seed >> 32}:
+ * u1 = ((w0 >> 8) + 1) / 2^24, u2 = (w1 >> 8) / 2^24, r = sqrt(-2 log u1),
+ * z[2q] = r cos(2 pi u2), z[2q+1] = r sin(2 pi u2). rng_state is a device pair
+ * {offset, scratch counter} (zero-initialise once); each call uses offset
+ * rng_state[0] and adds one to it on the device. The reference samples with
+ * torch.normal: equal in distribution, not bit for bit. n_actions 1..64;
+ * mean/actions f32 with row strides ld_mean/ld_actions, std f32 [n_actions],
+ * log_prob f32 [B].                                                        */
+int glad_ppo_epilogue(const float* mean, int64_t B, int64_t ld_mean, const float* std, int n_actions,
+                      uint64_t seed, unsigned long long* rng_state, float* actions, int64_t ld_actions,
+                      float* log_prob, float* sigma_out, void* stream);
+
 /* The compiled critic function of qrt full mode (qrt/integration.py:133-135):
  * the same encoder over the critic observation group, then the fp16 critic
  * MLP. obs [B, P+2079] (P <= 104), value_out f32 [B,1] (the fp16 output

@@ -247,6 +247,66 @@ def gumbel16(seed, offset, B, n_tok=187):
     return -b
 
 
+def ppo_normal(seed, offset, B, n):
+    """The N(0,1) draws of glad_ppo_epilogue: pair q = j // 2 of env e takes words
+    (2(q&1), 2(q&1)+1) of philox({0x80000000 | q>>1, e, e>>32, offset}, {seed, seed>>32});
+    u1 = ((w0 >> 8) + 1) / 2^24, u2 = (w1 >> 8) / 2^24, r = sqrt(-2 log u1) in fp32,
+    z[2q] = r cos(2 pi u2), z[2q+1] = r sin(2 pi u2) (Box-Muller; the sine and cosine
+    evaluated in float64 and rounded, CUDA's sincospif is within 2 ulp of that)."""
+    j = np.arange(n)
+    q = j // 2
+    env = np.arange(B, dtype=np.uint64)[:, None] * np.ones((1, n), np.uint64)
+    qq = np.broadcast_to(q[None, :], (B, n)).astype(np.uint64)
+    ctr = [(np.uint64(0x80000000) | (qq >> np.uint64(1))).astype(np.uint32),
+           (env & np.uint64(0xFFFFFFFF)).astype(np.uint32), (env >> np.uint64(32)).astype(np.uint32),
+           np.full(env.shape, offset & 0xFFFFFFFF, np.uint32)]
+    words = np.stack(philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)))
+    h = (qq & np.uint64(1)).astype(np.int64)
+    w0 = np.take_along_axis(words, (2 * h)[None], axis=0)[0]
+    w1 = np.take_along_axis(words, (2 * h + 1)[None], axis=0)[0]
+    u1 = ((w0 >> np.uint32(8)) + np.uint32(1)).astype(f32) * f32(2.0 ** -24)
+    u2 = (w1 >> np.uint32(8)).astype(f32) * f32(2.0 ** -24)
+    r = np.sqrt(f32(-2.0) * np.log(u1).astype(f32)).astype(f32)
+    ang = 2.0 * np.pi * u2.astype(np.float64)
+    trig = np.where(j[None, :] % 2 == 1, np.sin(ang), np.cos(ang)).astype(f32)
+    return (r * trig).astype(f32)
+
+
+def ppo_log_prob_terms(mean, std, actions):
+    """Per-action terms of torch.distributions.Normal(mean, std).log_prob(actions) in fp32:
+    (-(a - mean)^2) / (2 std^2) - log(std) - log(sqrt(2 pi))."""
+    d = (actions.astype(f32) - mean.astype(f32)).astype(f32)
+    var = (std.astype(f32) * std.astype(f32)).astype(f32)
+    t = ((-(d * d)).astype(f32) / (f32(2.0) * var)).astype(f32)
+    return ((t - np.log(std.astype(f32)).astype(f32)).astype(f32) - f32(0.9189385332046727)).astype(f32)
+
+
+def butterfly_sum32(terms):
+    """Sum of up to 64 terms per row in glad_ppo_epilogue's order: lane l holds terms l and
+    l + 32, then five xor butterflies (partners 16, 8, 4, 2, 1 apart), all in fp32."""
+    B, n = terms.shape
+    v = np.zeros((B, 64), f32)
+    v[:, :n] = terms
+    lanes = (v[:, :32] + v[:, 32:]).astype(f32)
+    idx = np.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        lanes = (lanes + lanes[:, idx ^ o]).astype(f32)
+    return lanes[:, 0]
+
+
+def ppo_epilogue(mean, std, seed, offset):
+    """PPO.act epilogue (rsl_rl/algorithms/ppo.py:129-140; Normal sample and log_prob,
+    rsl_rl/modules/actor_critic_encoder.py:329-335,366-367): actions = mean + std z,
+    log_prob = the butterfly sum of the per-action log-density terms."""
+    mean = np.asarray(mean, f32)
+    std = np.asarray(std, f32)
+    B, n = mean.shape
+    z = ppo_normal(seed, offset, B, n)
+    a = (mean + (std[None, :] * z).astype(f32)).astype(f32)
+    lp = butterfly_sum32(ppo_log_prob_terms(mean, np.broadcast_to(std[None, :], (B, n)), a))
+    return a, lp
+
+
 def topk_lowest_index(logits, k):
     """Top-k indices ordered by value descending, ties by index ascending."""
     lg = np.asarray(logits).astype(f32)

@@ -108,6 +108,11 @@ SIGNATURES = {
     "glad_actor_critic_forward": (c_int, [POINTER(GladActorWeights), POINTER(GladCriticWeights), c_void_p,
                                           c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p,
                                           c_void_p, c_size_t, c_void_p]),
+    "glad_actor_critic_forward_train": (c_int, [POINTER(GladActorWeights), POINTER(GladCriticWeights), c_void_p,
+                                                c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_uint64,
+                                                c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "glad_ppo_epilogue": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_uint64, c_void_p, c_void_p,
+                                  c_int64, c_void_p, c_void_p, c_void_p]),
     "glad_critic_workspace_size": (c_size_t, [c_int64]),
     "glad_critic_forward": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                     c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),

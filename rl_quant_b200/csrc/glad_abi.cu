@@ -36,6 +36,7 @@ cudaError_t launch_requant_qlinear(const GladQLinearSrc* layers, int n, cudaStre
 cudaError_t launch_requant_qcnn(const GladQCNNSrc& s, cudaStream_t st);
 cudaError_t launch_cast_copy(const GladCastCopy* items, int n, cudaStream_t st);
 int mlp_max_tiles(int act_mode, cudaStream_t st);
+cudaError_t launch_ppo_epilogue(const PpoParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x, int64_t M, int64_t ldx,
                        float* mean, int64_t ldm, float* slots, cudaStream_t st, bool pdl = false);
 }  // namespace glad
@@ -385,11 +386,11 @@ size_t glad_actor_critic_workspace_size(int64_t B) {
   return actor_ws(nullptr, b).bytes + up256((size_t)b * kD * 2) + up256((size_t)b * kCriticEnc * 2);
 }
 
-int glad_actor_critic_forward(const GladActorWeights* wa, const GladCriticWeights* wc, const void* policy_obs,
-                              const void* critic_obs, int obs_dtype, int64_t B, int64_t ld_policy,
-                              int64_t ld_critic, int act_mode, float* mean_out, float* value_out,
-                              void* workspace, size_t workspace_bytes, void* stream) {
-  g_err[0] = 0;
+namespace {
+int actor_critic_impl(const GladActorWeights* wa, const GladCriticWeights* wc, const void* policy_obs,
+                      const void* critic_obs, int obs_dtype, int64_t B, int64_t ld_policy,
+                      int64_t ld_critic, int act_mode, const GumbelArgs* gumbel, float* mean_out,
+                      float* value_out, void* workspace, size_t workspace_bytes, void* stream) {
   if (!wc) return fail(GLAD_ERR_INVALID_ARG, "critic weights are NULL");
   if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
   if (B == 0) return GLAD_OK;
@@ -415,8 +416,32 @@ int glad_actor_critic_forward(const GladActorWeights* wa, const GladCriticWeight
   uint8_t* extra = reinterpret_cast<uint8_t*>(workspace) + abytes;
   DualArgs dual{wc, critic_obs, ld_critic, value_out, reinterpret_cast<__half*>(extra),
                 reinterpret_cast<__half*>(extra + up256((size_t)B * kD * 2))};
-  return actor_forward_impl(wa, policy_obs, obs_dtype, B, ld_policy, act_mode, nullptr, nullptr, mean_out,
+  return actor_forward_impl(wa, policy_obs, obs_dtype, B, ld_policy, act_mode, nullptr, gumbel, mean_out,
                             nullptr, workspace, abytes, stream, &dual);
+}
+}  // namespace
+
+int glad_actor_critic_forward(const GladActorWeights* wa, const GladCriticWeights* wc, const void* policy_obs,
+                              const void* critic_obs, int obs_dtype, int64_t B, int64_t ld_policy,
+                              int64_t ld_critic, int act_mode, float* mean_out, float* value_out,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  return actor_critic_impl(wa, wc, policy_obs, critic_obs, obs_dtype, B, ld_policy, ld_critic, act_mode,
+                           nullptr, mean_out, value_out, workspace, workspace_bytes, stream);
+}
+
+int glad_actor_critic_forward_train(const GladActorWeights* wa, const GladCriticWeights* wc,
+                                    const void* policy_obs, const void* critic_obs, int obs_dtype,
+                                    int64_t B, int64_t ld_policy, int64_t ld_critic, int act_mode,
+                                    uint64_t gumbel_seed, unsigned long long* gumbel_offset,
+                                    float* mean_out, float* value_out, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!gumbel_offset) return fail(GLAD_ERR_INVALID_ARG, "gumbel_offset (device word) must be set");
+  if (!aligned(gumbel_offset, 8)) return fail(GLAD_ERR_INVALID_ARG, "gumbel_offset must be 8-byte aligned");
+  const GumbelArgs g{gumbel_seed, gumbel_offset};
+  return actor_critic_impl(wa, wc, policy_obs, critic_obs, obs_dtype, B, ld_policy, ld_critic, act_mode,
+                           &g, mean_out, value_out, workspace, workspace_bytes, stream);
 }
 
 namespace {
@@ -538,6 +563,7 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.gumbel = gumbel ? 1 : 0;
   tp.gumbel_seed = gumbel ? gumbel->seed : 0;
   tp.gumbel_offset = gumbel ? gumbel->offset : nullptr;
+  tp.done_slot = kSlotTailDone;
   tp.z8 = z8;
   tp.score_local = score_local;
   tp.pe = ws.pe;
@@ -603,7 +629,9 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
     tc.ld_enc = kCriticEnc;
     tc.prop_dim = dual->wc->proprio_emb.in_features;
     tc.noise = nullptr;
-    tc.gumbel = 0;
+    // train mode: the critic draws its own Gumbel term at the offset the actor tail
+    // has advanced (the MLP launched in between waits for the actor tail to finish)
+    tc.done_slot = kSlotCriticTailDone;
     tc.pe = dual->pe_c;
     tc.enc = dual->enc_c;
     tc.topk_logits_out = nullptr;
@@ -907,6 +935,37 @@ int glad_cast_copy(const GladCastCopy* items, int n, void* stream) {
       return fail(GLAD_ERR_INVALID_ARG, "item %d: unknown dtype", i);
   }
   GLAD_CHECK_CUDA(launch_cast_copy(items, n, (cudaStream_t)stream), "cast-copy launch");
+  return GLAD_OK;
+}
+
+int glad_ppo_epilogue(const float* mean, int64_t B, int64_t ld_mean, const float* std, int n_actions,
+                      uint64_t seed, unsigned long long* rng_state, float* actions, int64_t ld_actions,
+                      float* log_prob, float* sigma_out, void* stream) {
+  g_err[0] = 0;
+  if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
+  if (n_actions < 1 || n_actions > 64) return fail(GLAD_ERR_INVALID_ARG, "n_actions %d; 1..64", n_actions);
+  if (B == 0) return GLAD_OK;
+  if (!mean || !std || !rng_state || !actions || !log_prob)
+    return fail(GLAD_ERR_INVALID_ARG, "mean, std, rng_state, actions and log_prob must be set");
+  if (ld_mean < n_actions || ld_actions < n_actions)
+    return fail(GLAD_ERR_INVALID_ARG, "row strides must be >= n_actions");
+  if (!aligned(rng_state, 8)) return fail(GLAD_ERR_INVALID_ARG, "rng_state must be 8-byte aligned");
+  if (!aligned(mean, 4) || !aligned(std, 4) || !aligned(actions, 4) || !aligned(log_prob, 4) ||
+      !aligned(sigma_out, 4))
+    return fail(GLAD_ERR_INVALID_ARG, "f32 buffers must be 4-byte aligned");
+  PpoParams p{};
+  p.mean = mean;
+  p.ld_mean = ld_mean;
+  p.std = std;
+  p.n = n_actions;
+  p.B = B;
+  p.seed = seed;
+  p.rng = rng_state;
+  p.actions = actions;
+  p.ld_act = ld_actions;
+  p.log_prob = log_prob;
+  p.sigma = sigma_out;
+  GLAD_CHECK_CUDA(launch_ppo_epilogue(p, (cudaStream_t)stream, true), "PPO epilogue launch");
   return GLAD_OK;
 }
 

@@ -32,6 +32,7 @@ constexpr int kSlotCriticQp = 7;        // critic query projector absmax (fused 
 constexpr int kSlotMlpBarrier = 16;
 constexpr int kSlotFrontBarrier = 19;
 constexpr int kSlotTailDone = 20;       // CTAs of the tail kernel that finished (Gumbel offset)
+constexpr int kSlotCriticTailDone = 21; // the same for the critic tail of a fused actor + critic call
 constexpr int kSlotsBytes = 256;
 
 __device__ __forceinline__ float fp16r(float x) { return __half2float(__float2half_rn(x)); }
@@ -322,6 +323,7 @@ struct TailParams {
   int gumbel;              // draw the noise in-kernel (Philox4x32-10) instead of reading `noise`
   uint64_t gumbel_seed;
   unsigned long long* gumbel_offset;   // device word: this call's counter offset; advanced by one per call
+  int done_slot;           // slot counting finished CTAs (the last one advances the offset)
   const int8_t* z8;        // [B*187,16]
   const __half* score_local;
   const __half* pe;        // [B,64]
@@ -330,6 +332,20 @@ struct TailParams {
   int64_t* topk_idx_out;   // [B,32] or null
   __half* attn_w_out;      // [B,32] or null
   float* slots;
+};
+
+struct PpoParams {
+  const float* mean;       // [B, ld_mean]
+  int64_t ld_mean;
+  const float* std;        // [n]
+  int n;                   // actions, 1..64
+  int64_t B;
+  uint64_t seed;
+  unsigned long long* rng; // {offset, finished-block counter}
+  float* actions;          // [B, ld_act]
+  int64_t ld_act;
+  float* log_prob;         // [B]
+  float* sigma;            // [B, n] or null
 };
 
 struct GemmParams {

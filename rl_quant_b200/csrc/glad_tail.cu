@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   if (p.gumbel && tid == 0) {
     // the last CTA to finish advances the offset for the next call (every CTA has read it)
     __threadfence();
-    if (atomicAdd(reinterpret_cast<unsigned int*>(&p.slots[kSlotTailDone]), 1u) == gridDim.x - 1)
+    if (atomicAdd(reinterpret_cast<unsigned int*>(&p.slots[p.done_slot]), 1u) == gridDim.x - 1)
       atomicAdd(p.gumbel_offset, 1ull);
   }
   if (s.abort_flag) {

@@ -220,7 +220,10 @@ class FusedActorCritic:
         self._ws: dict[tuple, torch.Tensor] = {}
 
     def run(self, policy_obs: torch.Tensor, critic_obs: torch.Tensor, mean: torch.Tensor,
-            value: torch.Tensor) -> None:
+            value: torch.Tensor, gumbel: tuple | None = None) -> None:
+        """``gumbel=(seed, offset)`` (offset: int64 device tensor of one element) runs the
+        train-mode rollout forward: each head adds its own in-kernel Gumbel term, the actor
+        at offset[0], the critic at offset[0] + 1; the call adds two to offset[0]."""
         N.require_cuda(policy_obs)
         N.require_cuda(critic_obs)
         if policy_obs.dtype != critic_obs.dtype or policy_obs.shape[0] != critic_obs.shape[0]:
@@ -235,8 +238,46 @@ class FusedActorCritic:
                              device=policy_obs.device)
             self._ws[key] = ws
         dt = N.DTYPE_F32 if policy_obs.dtype == torch.float32 else N.DTYPE_F16
-        rc = N.load().glad_actor_critic_forward(
-            self.actor.weights(), self.critic.weights(), policy_obs.data_ptr(), critic_obs.data_ptr(), dt, B,
-            policy_obs.stride(0), critic_obs.stride(0), N.ACT_MODES[self.actor.act_mode], mean.data_ptr(),
-            value.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_handle(policy_obs.device))
-        N.check(rc, "glad_actor_critic_forward")
+        if gumbel is None:
+            rc = N.load().glad_actor_critic_forward(
+                self.actor.weights(), self.critic.weights(), policy_obs.data_ptr(), critic_obs.data_ptr(), dt,
+                B, policy_obs.stride(0), critic_obs.stride(0), N.ACT_MODES[self.actor.act_mode],
+                mean.data_ptr(), value.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_handle(policy_obs.device))
+            N.check(rc, "glad_actor_critic_forward")
+            return
+        seed, offset = gumbel
+        if offset.dtype != torch.int64 or offset.device != policy_obs.device or offset.numel() < 1:
+            raise ValueError("gumbel offset must be an int64 tensor on the observations' device")
+        rc = N.load().glad_actor_critic_forward_train(
+            self.actor.weights(), self.critic.weights(), policy_obs.data_ptr(), critic_obs.data_ptr(), dt,
+            B, policy_obs.stride(0), critic_obs.stride(0), N.ACT_MODES[self.actor.act_mode],
+            int(seed) & (2 ** 64 - 1), offset.data_ptr(), mean.data_ptr(), value.data_ptr(), ws.data_ptr(),
+            ws.numel(), N.stream_handle(policy_obs.device))
+        N.check(rc, "glad_actor_critic_forward_train")
+
+
+def ppo_epilogue(mean: torch.Tensor, std: torch.Tensor, seed: int, rng_state: torch.Tensor,
+                 actions: torch.Tensor, log_prob: torch.Tensor, sigma: torch.Tensor | None = None) -> None:
+    """PPO.act epilogue (``glad_ppo_epilogue``, rsl_rl/algorithms/ppo.py:129-140): actions
+    sampled from Normal(mean, std) and their summed log-probability. ``rng_state`` is an
+    int64 device tensor of two elements {offset, scratch} (zero-initialised once); each
+    call uses offset rng_state[0] and adds one to it on the device."""
+    N.require_cuda(mean)
+    B, n = mean.shape
+    for t, nm in ((mean, "mean"), (std, "std"), (actions, "actions"), (log_prob, "log_prob")):
+        if t.dtype != torch.float32 or t.device != mean.device:
+            raise ValueError(f"{nm} must be float32 on the device of mean")
+    if mean.stride(1) != 1 or actions.stride(1) != 1 or not std.is_contiguous() or std.numel() != n:
+        raise ValueError("mean/actions rows must be contiguous and std must hold one value per action")
+    if actions.shape != mean.shape or log_prob.numel() != B:
+        raise ValueError("actions must match mean and log_prob must hold one value per row")
+    if rng_state.dtype != torch.int64 or rng_state.numel() < 2 or rng_state.device != mean.device:
+        raise ValueError("rng_state must be an int64 device tensor of two elements")
+    if sigma is not None and (sigma.dtype != torch.float32 or not sigma.is_contiguous() or sigma.shape != mean.shape):
+        raise ValueError("sigma must be a contiguous float32 tensor shaped like mean")
+    rc = N.load().glad_ppo_epilogue(mean.data_ptr(), B, mean.stride(0), std.data_ptr(), n,
+                                    int(seed) & (2 ** 64 - 1), rng_state.data_ptr(), actions.data_ptr(),
+                                    actions.stride(0), log_prob.data_ptr(),
+                                    sigma.data_ptr() if sigma is not None else None,
+                                    N.stream_handle(mean.device))
+    N.check(rc, "glad_ppo_epilogue")

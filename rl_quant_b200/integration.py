@@ -62,7 +62,8 @@ class QRTAccelerator:
                  rollout_training: bool = True, update_amp: str | None = "bf16",
                  act_mode: str = "dynamic", cocalib: bool = False, cocalib_source: str = "eager",
                  int8_paths: list[str] | None = None, calib_obs: list | None = None,
-                 let_steps: int = 200, mode: str = "max-autotune", verbose: bool = True):
+                 let_steps: int = 200, mode: str = "max-autotune", fused_ppo_act: bool = False,
+                 verbose: bool = True):
         if cocalib:
             raise NotImplementedError("online co-calibration (training side) is not part of this package")
         if update_amp not in ("bf16", "fp32", None):
@@ -123,6 +124,30 @@ class QRTAccelerator:
         policy.update_distribution = types.MethodType(update_distribution_qrt, policy)
         policy.evaluate = types.MethodType(evaluate_qrt, policy)
 
+        # opt-in: PPO.act (ppo.py:129-140) as one fused forward -- actor + critic from one
+        # read of the height scan, then the Normal sample and its log-probability drawn
+        # in the kernel (Philox) instead of by torch.normal. Needs the policy and critic
+        # groups to carry the same scan (the critic reads it from the policy group).
+        self._orig_act = self.alg.act
+        if fused_ppo_act:
+            alg = self.alg
+
+            def act_fused(obs):
+                if policy.is_recurrent:
+                    return acc._orig_act(obs)
+                ao = policy.actor_obs_normalizer(policy.get_actor_obs(obs))
+                co = policy.critic_obs_normalizer(policy.get_critic_obs(obs))
+                kw = {"log_std": policy.log_std} if getattr(policy, "noise_std_type", "scalar") == "log" \
+                    else {"std": policy.std}
+                a, v, lp, m, sg = run.ppo_act(ao, co, **kw)
+                t = alg.transition
+                t.actions, t.values, t.actions_log_prob = a, v, lp
+                t.action_mean, t.action_sigma = m, sg
+                t.observations = obs
+                return t.actions
+
+            self.alg.act = act_fused
+
         self._orig_update = self.alg.update
 
         def update_qrt():
@@ -172,6 +197,7 @@ class QRTAccelerator:
         self.policy.update_distribution = self._orig_ud
         self.policy.evaluate = self._orig_eval
         self.alg.update = self._orig_update
+        self.alg.act = self._orig_act
 
 
 def accelerate_runner(runner, **kwargs) -> QRTAccelerator:

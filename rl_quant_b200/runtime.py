@@ -23,7 +23,7 @@ import torch
 
 from . import _native as N
 from .encoder_opt import _gumbel_noise
-from .fused import FusedActor, FusedCritic, FusedUnsupported
+from .fused import FusedActor, FusedActorCritic, FusedCritic, FusedUnsupported, ppo_epilogue
 from .qconv import QuantCNN
 from .qlinear import QuantLinear
 
@@ -39,21 +39,28 @@ def _dt(t: torch.Tensor) -> int:
 
 
 class _Graph:
+    """``fn`` captured over static input buffer(s): ``static_in`` is a tensor or a
+    tuple of tensors; a call copies its arguments into them and replays."""
+
     def __init__(self, fn, static_in):
         self.static_in = static_in
-        s = torch.cuda.Stream(device=static_in.device)
-        s.wait_stream(torch.cuda.current_stream(static_in.device))
+        args = static_in if isinstance(static_in, tuple) else (static_in,)
+        dev = args[0].device
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
             for _ in range(2):
-                fn(static_in)
-        torch.cuda.current_stream(static_in.device).wait_stream(s)
+                fn(*args)
+        torch.cuda.current_stream(dev).wait_stream(s)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.out = fn(static_in)
+            self.out = fn(*args)
 
-    def __call__(self, x):
-        if x.data_ptr() != self.static_in.data_ptr():
-            self.static_in.copy_(x)
+    def __call__(self, *xs):
+        args = self.static_in if isinstance(self.static_in, tuple) else (self.static_in,)
+        for a, x in zip(args, xs):
+            if x.data_ptr() != a.data_ptr():
+                a.copy_(x)
         self.graph.replay()
         return self.out
 
@@ -66,9 +73,9 @@ class _HostPipe:
     stream after the copy. With two lanes the copy of step k+1 overlaps the
     forward of step k; forwards stay in one stream, one after the other."""
 
-    def __init__(self, fn, example_dev, lanes):
+    def __init__(self, make_graph, example_dev, lanes):
         dev = example_dev.device
-        self.lanes = [_Graph(fn, example_dev.clone()) for _ in range(lanes)]
+        self.lanes = [make_graph(example_dev.clone()) for _ in range(lanes)]
         self.copy_stream = torch.cuda.Stream(device=dev)
         self.in_ready = [torch.cuda.Event() for _ in range(lanes)]
         self.free = [torch.cuda.Event() for _ in range(lanes)]
@@ -125,6 +132,11 @@ class InferenceRunner:
         # Gumbel stream of train-mode rollouts: seed from torch's default generator
         self._gumbel_seed = int(torch.randint(0, 2 ** 62, (1,)).item())
         self._gumbel_offset = None
+        # PPO.act sampling stream (Philox, its own seed) and the fused actor + critic
+        self._ppo_seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+        self._ppo_rng = None
+        self._fused_ac = None
+        self._fused_ac_err = None
         self._g_refresh = None
         self._g_sync = None
         self._sync_items = None
@@ -136,9 +148,7 @@ class InferenceRunner:
             if self.model.training:
                 # train-mode rollouts keep the Gumbel top-k exploration (qrt/encoder_opt.py:87-91),
                 # drawn inside the kernel; the device offset advances on every (replayed) call
-                if self._gumbel_offset is None or self._gumbel_offset.device != po.device:
-                    self._gumbel_offset = torch.zeros(1, dtype=torch.int64, device=po.device)
-                self._fused.run(po, mean, gumbel=(self._gumbel_seed, self._gumbel_offset))
+                self._fused.run(po, mean, gumbel=self._gumbel_state(po.device))
             else:
                 self._fused.run(po, mean)
             return mean
@@ -157,16 +167,57 @@ class InferenceRunner:
         enc, _, _, _ = (enc_fn or m._encode_terrain)(c)
         return m.critic(enc)
 
-    def _call(self, key, fn, x):
+    def _call(self, key, fn, *xs):
         if self.mode == "eager":
-            return fn(x)
-        k = (key, tuple(x.shape), x.dtype, x.device)
+            return fn(*xs)
+        k = (key,) + tuple((tuple(x.shape), x.dtype, x.device) for x in xs)
         g = self._graphs.get(k)
         if g is None:
-            g = _Graph(fn, x.clone())
+            static = tuple(x.clone() for x in xs)
+            g = self._new_graph(fn, static if len(static) > 1 else static[0])
             self._graphs[k] = g
-        out = g(x)
-        return out.clone() if self.clone_outputs else out
+        out = g(*xs)
+        if not self.clone_outputs:
+            return out
+        return tuple(o.clone() for o in out) if isinstance(out, tuple) else out.clone()
+
+    def _new_graph(self, fn, static):
+        """Capture ``fn``; the warm-up runs of the capture leave the device noise
+        counters (Gumbel offset, PPO sampling offset) as they found them."""
+        saved = [(a, getattr(self, a).clone() if getattr(self, a) is not None else None)
+                 for a in ("_gumbel_offset", "_ppo_rng")]
+        g = _Graph(fn, static)
+        for a, old in saved:
+            t = getattr(self, a)
+            if t is None:
+                continue
+            if old is not None and old.device == t.device:
+                t.copy_(old)
+            else:
+                t.zero_()
+        return g
+
+    # -- PPO.act in one forward -------------------------------------------------------------
+    def _gumbel_state(self, dev):
+        if self._gumbel_offset is None or self._gumbel_offset.device != dev:
+            self._gumbel_offset = torch.zeros(1, dtype=torch.int64, device=dev)
+        return self._gumbel_seed, self._gumbel_offset
+
+    def _ppo_fn(self, po, co, std_fn):
+        B, dev = po.shape[0], po.device
+        mean = torch.empty(B, 29, dtype=torch.float32, device=dev)
+        value = torch.empty(B, 1, dtype=torch.float32, device=dev)
+        actions = torch.empty(B, 29, dtype=torch.float32, device=dev)
+        log_prob = torch.empty(B, dtype=torch.float32, device=dev)
+        sigma = torch.empty(B, 29, dtype=torch.float32, device=dev)
+        if self.model.training:
+            self._fused_ac.run(po, co, mean, value, gumbel=self._gumbel_state(dev))
+        else:
+            self._fused_ac.run(po, co, mean, value)
+        if self._ppo_rng is None or self._ppo_rng.device != dev:
+            self._ppo_rng = torch.zeros(2, dtype=torch.int64, device=dev)
+        ppo_epilogue(mean, std_fn(), self._ppo_seed, self._ppo_rng, actions, log_prob, sigma)
+        return actions, value, log_prob, mean, sigma
 
     # -- public API (qrt/runtime.py:128-191) ------------------------------------------------
     @torch.inference_mode()
@@ -208,7 +259,7 @@ class InferenceRunner:
         k = ("act", tuple(host_obs.shape), host_obs.dtype, dev)
         pipe = self._pipes.get(k)
         if pipe is None:
-            pipe = _HostPipe(self._act_fn, host_obs.to(dev), self.host_lanes)
+            pipe = _HostPipe(lambda st: self._new_graph(self._act_fn, st), host_obs.to(dev), self.host_lanes)
             self._pipes[k] = pipe
         return pipe(host_obs, out)
 
@@ -224,6 +275,40 @@ class InferenceRunner:
         if not self.with_critic:
             raise RuntimeError("evaluate needs InferenceRunner(with_critic=True)")
         return self._call("val", self._val_fn, critic_obs)
+
+    @torch.inference_mode()
+    def ppo_act(self, policy_obs, critic_obs, std: torch.Tensor | None = None,
+                log_std: torch.Tensor | None = None):
+        """One PPO.act transition (rsl_rl/algorithms/ppo.py:129-140) in one forward:
+        the fused actor + critic over one read of the shared scan (train-mode Gumbel
+        terms when the model is in train mode), then the Normal(mean, std) sample and
+        its log-probability (glad_ppo_epilogue). Returns (actions [B,A], values [B,1],
+        actions_log_prob [B], action_mean [B,A], action_sigma [B,A]), all fp32.
+        ``std`` (or ``log_std``, exponentiated per call) defaults to the model's own
+        parameter; captured modes read the given tensor in place on every call, so it
+        must keep its storage (an nn.Parameter updated in place does)."""
+        if not self.with_critic:
+            raise RuntimeError("ppo_act needs InferenceRunner(with_critic=True)")
+        if self._fused_ac is None and self._fused_ac_err is None:
+            try:
+                self._fused_ac = FusedActorCritic(self.model)
+            except FusedUnsupported as e:
+                self._fused_ac_err = str(e)
+        if self._fused_ac is None:
+            raise FusedUnsupported(f"fused actor + critic unavailable: {self._fused_ac_err}")
+        if std is None and log_std is None:
+            if getattr(self.model, "noise_std_type", "scalar") == "log":
+                log_std = self.model.log_std
+            else:
+                std = self.model.std
+        if std is not None:
+            src = std
+            std_fn = lambda: src.float()  # noqa: E731
+        else:
+            src = log_std
+            std_fn = lambda: torch.exp(src.float())  # noqa: E731
+        key = ("ppo", src.data_ptr())
+        return self._call(key, lambda po, co: self._ppo_fn(po, co, std_fn), policy_obs, critic_obs)
 
     @torch.inference_mode()
     def act_sample(self, policy_obs):

@@ -116,3 +116,33 @@ def test_w4_quantize_host_matches_oracle():
     step = s_ref.astype(np.float32)[:, np.arange(224) // 64]
     assert np.all(np.abs(Wd - W) <= step * 0.5 + 1e-3 * step + 1e-8)
     assert np.all(Wd[3, 64:128] == 0.0)
+
+
+def test_ppo_log_prob_terms_match_torch_normal():
+    """The oracle's per-action log-density terms are torch.distributions.Normal.log_prob's
+    fp32 arithmetic (rsl_rl/modules/actor_critic_encoder.py:366-367)."""
+    import torch
+    g = torch.Generator().manual_seed(3)
+    mean = torch.randn(64, 29, generator=g)
+    std = 0.1 + torch.rand(29, generator=g)
+    a = mean + std * torch.randn(64, 29, generator=g)
+    ref = torch.distributions.Normal(mean, std.expand(64, 29)).log_prob(a).numpy()
+    got = O.ppo_log_prob_terms(mean.numpy(), np.broadcast_to(std.numpy()[None], (64, 29)), a.numpy())
+    np.testing.assert_allclose(got, ref, rtol=2e-7, atol=1e-6)
+    s = O.butterfly_sum32(got)
+    np.testing.assert_allclose(s, ref.astype(np.float64).sum(-1), rtol=1e-6, atol=2e-5)
+
+
+def test_ppo_normal_distribution_and_pairs():
+    """Box-Muller draws: N(0,1) marginals, the cosine and sine halves of a pair share
+    their radius, distinct offsets and seeds give distinct draws."""
+    import scipy.stats as st
+    z = O.ppo_normal(7, 0, 2048, 29)
+    assert abs(z.mean()) < 0.01 and abs(z.std() - 1.0) < 0.01
+    assert st.kstest(z.ravel(), "norm").pvalue > 1e-3
+    r2 = z[:, 0] ** 2 + z[:, 1] ** 2
+    assert np.all(r2 > 0)
+    assert not np.array_equal(z, O.ppo_normal(7, 1, 2048, 29))
+    assert not np.array_equal(z, O.ppo_normal(8, 0, 2048, 29))
+    a, lp = O.ppo_epilogue(np.zeros((3, 29), np.float32), np.ones(29, np.float32), 7, 0)
+    assert np.array_equal(a, z[:3])
