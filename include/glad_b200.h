@@ -72,6 +72,20 @@ typedef struct GladQLinear {
   int32_t out_features;
 } GladQLinear;
 
+/* rsl_rl EmpiricalNormalization of one observation group
+ * (rsl_rl/networks/normalization.py:44-47), applied while the rows are loaded:
+ * x' = (x - mean) / (sqrt(var) + eps), every step an fp32 operation, then the
+ * fp16 cast of qrt's `actor_obs.half()` (qrt/integration.py:206). sqrt(var) is
+ * the module's `_std`, which it recomputes from `_var`; `_mean` and `_var` are
+ * updated in place, so captured graphs stay valid. mean = NULL: identity.
+ * n = the group's width; the observations must be f32.                       */
+typedef struct GladObsNorm {
+  const float* mean;             /* [n] f32 (_mean)                          */
+  const float* var;              /* [n] f32 (_var)                           */
+  float eps;                     /* the module's eps as f32                  */
+  int32_t n;
+} GladObsNorm;
+
 /* Every tensor the fused actor forward reads (qrt full mode: QuantCNN,
  * LET W8A8 on actor_proprio_embedding, query_projector, actor.0/2/4/6;
  * fp16 GPS selector, top-k scorer and MHA, qrt/integration.py:42-43).     */
@@ -88,6 +102,7 @@ typedef struct GladActorWeights {
   const void* mha_out_w;         /* mha.out_proj.weight f16 [64,64]          */
   const void* mha_out_b;         /* mha.out_proj.bias   f16 [64]             */
   GladQLinear mlp[4];            /* actor.0 224->512, .2 ->256, .4 ->128, .6 ->29 */
+  GladObsNorm obs_norm;          /* actor_obs_normalizer (mean NULL: identity) */
 } GladActorWeights;
 
 /* Plain fp16 Linear (weight [out,in] f16 row-major, bias [out] f16 or NULL). */
@@ -119,6 +134,7 @@ typedef struct GladCriticWeights {
   const void* mha_out_w;
   const void* mha_out_b;
   GladLinear16 mlp[4];           /* critic.0 (128+P)->512, .2 ->256, .4 ->128, .6 ->1 */
+  GladObsNorm obs_norm;          /* critic_obs_normalizer (mean NULL: identity) */
 } GladCriticWeights;
 
 /* Optional per-call outputs of the fused forward (any field may be NULL). */

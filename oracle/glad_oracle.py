@@ -247,6 +247,15 @@ def gumbel16(seed, offset, B, n_tok=187):
     return -b
 
 
+def obs_normalize(x, mean, var, eps):
+    """rsl_rl EmpiricalNormalization.forward (rsl_rl/networks/normalization.py:44-47) with
+    std = sqrt(var) as the module keeps it (:67-68): (x - mean) / (std + eps), each step an
+    fp32 operation."""
+    x, mean, var = (np.asarray(t, f32) for t in (x, mean, var))
+    std = np.sqrt(var).astype(f32)
+    return ((x - mean).astype(f32) / (std + f32(eps)).astype(f32)).astype(f32)
+
+
 def ppo_normal(seed, offset, B, n):
     """The N(0,1) draws of glad_ppo_epilogue: pair q = j // 2 of env e takes words
     (2(q&1), 2(q&1)+1) of philox({0x80000000 | q>>1, e, e>>32, offset}, {seed, seed>>32});

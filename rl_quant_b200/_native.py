@@ -38,10 +38,14 @@ class GladQLinear(Structure):
         ("in_features", c_int32), ("out_features", c_int32)]
 
 
+class GladObsNorm(Structure):
+    _fields_ = [("mean", c_void_p), ("var", c_void_p), ("eps", c_float), ("n", c_int32)]
+
+
 class GladActorWeights(Structure):
     _fields_ = [("conv", GladConvWeights), ("proprio_emb", GladQLinear), ("query_proj", GladQLinear)] + [
         (n, c_void_p) for n in ("gps_w", "gps_b", "scorer_w", "scorer_b", "mha_in_w", "mha_in_b",
-                                "mha_out_w", "mha_out_b")] + [("mlp", GladQLinear * 4)]
+                                "mha_out_w", "mha_out_b")] + [("mlp", GladQLinear * 4), ("obs_norm", GladObsNorm)]
 
 
 class GladLinear16(Structure):
@@ -52,7 +56,7 @@ class GladCriticWeights(Structure):
     _fields_ = [("conv", GladConvWeights), ("proprio_emb", GladLinear16), ("proprio_emb_q", GladQLinear),
                 ("query_proj", GladQLinear)] + [
         (n, c_void_p) for n in ("gps_w", "gps_b", "scorer_w", "scorer_b", "mha_in_w", "mha_in_b",
-                                "mha_out_w", "mha_out_b")] + [("mlp", GladLinear16 * 4)]
+                                "mha_out_w", "mha_out_b")] + [("mlp", GladLinear16 * 4), ("obs_norm", GladObsNorm)]
 
 
 class GladActorAux(Structure):

@@ -29,7 +29,8 @@ cudaError_t launch_qgemm(const GemmParams& p, cudaStream_t st, bool pdl = false)
 size_t qgemm_smem_bytes(int K, int NT);
 cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
                           const float* alpha, const float* beta, int round16, float* slot,
-                          int num_sms, cudaStream_t st);
+                          int num_sms, cudaStream_t st, const float* norm_mean = nullptr,
+                          const float* norm_var = nullptr, float norm_eps = 0.0f);
 cudaError_t launch_act_scales(const float* slots, int act_mode, const float* const s_z[6],
                               const int let[6], float* out, cudaStream_t st);
 cudaError_t launch_requant_qlinear(const GladQLinearSrc* layers, int n, cudaStream_t st);
@@ -119,6 +120,18 @@ int check_conv(const GladConvWeights* w, bool c1, bool c2) {
 // `gemm`: the layer runs through the tcgen05 GEMM (in_features % 8 == 0,
 // qrt/qlinear.py:52-53); otherwise it is the front kernel's dp4a embedding
 // (in_features % 4 == 0, <= 128).
+// Observation normaliser of a group of `width` columns (mean NULL: none).
+int check_norm(const GladObsNorm& n, int width, int obs_dtype) {
+  if (!n.mean) return GLAD_OK;
+  if (!n.var) return fail(GLAD_ERR_INVALID_ARG, "obs_norm: mean set but var NULL");
+  if (n.n != width) return fail(GLAD_ERR_INVALID_ARG, "obs_norm covers %d columns, the group has %d", n.n, width);
+  if (obs_dtype != GLAD_DTYPE_F32)
+    return fail(GLAD_ERR_INVALID_ARG, "obs_norm needs f32 observations (it runs before the fp16 cast)");
+  if (!(n.eps >= 0.0f) || !aligned(n.mean, 4) || !aligned(n.var, 4))
+    return fail(GLAD_ERR_INVALID_ARG, "obs_norm: eps must be >= 0 and mean/var 4-byte aligned");
+  return GLAD_OK;
+}
+
 int check_ql(const GladQLinear* L, const char* name, int K, int N, bool gemm = true) {
   if (!L->w8 || !L->dq_scale || !L->s_w || !L->b_prime || !L->s_z || !L->inv_sz)
     return fail(GLAD_ERR_INVALID_ARG, "%s: QuantLinear buffers must be set", name);
@@ -198,7 +211,7 @@ extern "C" {
 
 const char* glad_last_error(void) { return g_err; }
 
-int glad_abi_version(void) { return 100; }
+int glad_abi_version(void) { return 101; }
 
 int glad_conv1_fused_q(const void* x_nhwc, int64_t B, const GladConvWeights* w, int8_t* z8_out,
                        void* stream) {
@@ -467,6 +480,11 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
     return fail(GLAD_ERR_INVALID_ARG, "obs is not element-aligned");
   int rc = check_conv(&w->conv, true, true);
   if (rc) return rc;
+  const GladObsNorm& nm = w->obs_norm;
+  if ((rc = check_norm(nm, P + kMap, obs_dtype))) return rc;
+  if (dual && (nm.mean || dual->wc->obs_norm.mean))
+    return fail(GLAD_ERR_INVALID_ARG, "the fused actor + critic call reads one scan for both heads and takes "
+                "no observation normalisers; run the two heads separately");
   if ((rc = check_ql(&w->proprio_emb, "actor_proprio_embedding", 96, 64, false))) return rc;
   if ((rc = check_ql(&w->query_proj, "query_projector", 128, 64))) return rc;
   const int mk[4] = {224, 512, 256, 128}, mn[4] = {512, 256, 128, kActions};
@@ -503,7 +521,7 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   const bool front_pdl = act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front;
   if (act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb.alpha,
-                                  w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st),
+                                  w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st, nm.mean, nm.var, nm.eps),
                     "absmax launch");
   stage_mark(1, st);
   FrontParams fp{};
@@ -528,6 +546,9 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.pe_out = ws.pe;
   fp.slots = ws.slots;
   fp.pe_absmax = pe_absmax_in_front ? 1 : 0;
+  fp.norm_mean = nm.mean;
+  fp.norm_var = nm.var;
+  fp.norm_eps = nm.eps;
   if (dual) {
     fp.dual = 1;
     fp.in_c = dual->critic_obs;
@@ -691,6 +712,7 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   if (!aligned(obs, obs_dtype == GLAD_DTYPE_F32 ? 4 : 2))
     return fail(GLAD_ERR_INVALID_ARG, "obs is not element-aligned");
   if ((rc = check_conv(&w->conv, true, true))) return rc;
+  if ((rc = check_norm(w->obs_norm, P + kMap, obs_dtype))) return rc;
   if ((rc = check_ql(&w->query_proj, "query_projector", 128, 64))) return rc;
   const int hk[4] = {128 + P, 512, 256, 128}, hn[4] = {512, 256, 128, 1};
   for (int i = 0; i < 4; ++i) {
@@ -720,7 +742,8 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   const bool front_pdl = !pe16 && act_mode == GLAD_ACT_DYNAMIC;
   if (front_pdl)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb_q.alpha,
-                                  w->proprio_emb_q.beta, 1, &ws.slots[0], d.sms, st),
+                                  w->proprio_emb_q.beta, 1, &ws.slots[0], d.sms, st, w->obs_norm.mean,
+                                  w->obs_norm.var, w->obs_norm.eps),
                     "absmax launch");
   FrontParams fp{};
   fp.in = obs;
@@ -736,6 +759,9 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   fp.pe = w->proprio_emb_q;
   fp.pe16_w = reinterpret_cast<const __half*>(w->proprio_emb.weight);
   fp.pe16_b = reinterpret_cast<const __half*>(w->proprio_emb.bias);
+  fp.norm_mean = w->obs_norm.mean;
+  fp.norm_var = w->obs_norm.var;
+  fp.norm_eps = w->obs_norm.eps;
   fp.qp = w->query_proj;
   fp.act_mode = act_mode;
   fp.ld_enc = kCriticEnc;

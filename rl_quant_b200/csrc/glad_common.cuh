@@ -258,6 +258,13 @@ __device__ __forceinline__ float gumbel16(uint64_t seed, uint64_t offset, int64_
   return -b;
 }
 
+// rsl_rl EmpiricalNormalization of column k (rsl_rl/networks/normalization.py:44-47):
+// (x - mean) / (std + eps) with std = sqrt(var) as the module computes it, every step
+// an fp32 operation.
+__device__ __forceinline__ float obs_norm(float x, const float* mean, const float* var, float eps, int k) {
+  return __fdiv_rn(__fsub_rn(x, __ldg(mean + k)), __fadd_rn(__fsqrt_rn(__ldg(var + k)), eps));
+}
+
 // ---- kernel parameter blocks -------------------------------------------------------
 enum FrontMode : int { kModeConv1 = 0, kModeConv2 = 1, kModeChain = 2, kModeFront = 3 };
 
@@ -291,6 +298,10 @@ struct FrontParams {
   GladQLinear qp;          // only alpha/beta are read (absmax of its input)
   int act_mode;
   int ld_enc;              // row stride of `enc` (>= 128 + prop_dim)
+  // observation normaliser of the `in` rows (norm_mean NULL: identity; f32 rows only)
+  const float* norm_mean;
+  const float* norm_var;
+  float norm_eps;
   // outputs
   int8_t* z8_out;          // [B*187,16]
   __half* feat_out;        // [B*187,64]

@@ -698,7 +698,8 @@ constexpr size_t kFusedSmemDual = sizeof(FusedSmem) + 128;
 // FULL = false: the QuantCNN chain alone (x_nhwc -> z8 -> fp16 local features), the same
 // pipeline without the pooling / embedding stages.
 // DUAL (with FULL): also the critic head's proprio embedding and encoded row.
-template <bool FULL, bool DUAL>
+// NORM (with FULL, not DUAL): the observation normaliser runs in the row loads.
+template <bool FULL, bool DUAL, bool NORM = false>
 __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS)
 front_fused_kernel(const __grid_constant__ FrontParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -798,8 +799,9 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
          row += (int64_t)8 * gridDim.x) {
 #pragma unroll 4
       for (int k = lane; k < P; k += 32) {
-        const float x = esz == 4 ? reinterpret_cast<const float*>(p.in)[row * p.ld + k]
-                                 : __half2float(reinterpret_cast<const __half*>(p.in)[row * p.ld + k]);
+        float x = esz == 4 ? reinterpret_cast<const float*>(p.in)[row * p.ld + k]
+                           : __half2float(reinterpret_cast<const __half*>(p.in)[row * p.ld + k]);
+        if constexpr (NORM) x = obs_norm(x, p.norm_mean, p.norm_var, p.norm_eps, k);
         const float xr = fp16r(x);
         m = fmaxf(m, p.pe.alpha ? fabsf(__fadd_rn(__fmul_rn(xr, p.pe.alpha[k]), p.pe.beta[k])) : fabsf(xr));
       }
@@ -920,6 +922,11 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   float zmax_qp = 0.0f;
   float zmax_qpc = 0.0f;                // critic query projector input (dual)
 
+  // observation normaliser of column k (identity without one)
+  auto nz = [&](float x, int k) {
+    if constexpr (NORM) return obs_norm(x, p.norm_mean, p.norm_var, p.norm_eps, k);
+    return x;
+  };
   // convert the staged row of `e` into planes[b] / prop16[b]
   auto convert = [&](int64_t e, int b, int nthr) {
     if (dual) {
@@ -931,25 +938,35 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     if (esz == 4 && rs.lo == 0 && rs.hi == (uint32_t)row_elems * 4) {
       // the whole fp32 row is in shared memory
       const float* st = reinterpret_cast<const float*>(s.stage + (rs.stage - s.stage));
-      for (int px = tid; px < kH1 * kW1; px += nthr) {
+      auto put = [&](int px, float v0, float v1, float v2) {
         const int ih = px / kW1, iw = px - ih * kW1;
-        const float v0 = st[P + px * 3], v1 = st[P + px * 3 + 1], v2 = st[P + px * 3 + 2];
         const int pl = ih & 1, r = ((ih - pl) >> 1) + 1, slot = iw + 2;
         const __half2 h01 = __floats2half2_rn(v0, v1);
         const __half2 h2z = __floats2half2_rn(v2, 0.0f);
         *reinterpret_cast<uint2*>(s.planes[0] + pl * kPlaneBytes + r * kRowBytes + slot * 8) =
             make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h2z));
+      };
+      if constexpr (NORM) {
+        for (int px = tid; px < kH1 * kW1; px += nthr) {
+          const int c0 = P + px * 3;
+          put(px, nz(st[c0], c0), nz(st[c0 + 1], c0 + 1), nz(st[c0 + 2], c0 + 2));
+        }
+        for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(nz(st[k], k));
+      } else {
+        for (int px = tid; px < kH1 * kW1; px += nthr)
+          put(px, st[P + px * 3], st[P + px * 3 + 1], st[P + px * 3 + 2]);
+        for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(st[k]);
       }
-      for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(st[k]);
       return;
     }
     for (int px = tid; px < kH1 * kW1; px += nthr) {
       const int ih = px / kW1, iw = px - ih * kW1;
       float v0, v1, v2;
       if (esz == 4) {
-        v0 = row_elem<4>(rs, P + px * 3);
-        v1 = row_elem<4>(rs, P + px * 3 + 1);
-        v2 = row_elem<4>(rs, P + px * 3 + 2);
+        const int c0 = P + px * 3;
+        v0 = nz(row_elem<4>(rs, c0), c0);
+        v1 = nz(row_elem<4>(rs, c0 + 1), c0 + 1);
+        v2 = nz(row_elem<4>(rs, c0 + 2), c0 + 2);
       } else {
         v0 = row_elem<2>(rs, P + px * 3);
         v1 = row_elem<2>(rs, P + px * 3 + 1);
@@ -964,7 +981,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       *reinterpret_cast<uint2*>(s.planes[0] + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
     }
     for (int k = tid; k < P; k += nthr)
-      s.prop16[b][k] = __float2half_rn(esz == 4 ? row_elem<4>(rs, k) : row_elem<2>(rs, k));
+      s.prop16[b][k] = __float2half_rn(esz == 4 ? nz(row_elem<4>(rs, k), k) : row_elem<2>(rs, k));
   };
   auto issue_conv1 = [&](int b) {      // by lane 0 of warp 7
     if (tid == kIssuer) {
@@ -1435,6 +1452,13 @@ cudaError_t launch_front(const FrontParams& p, int grid, cudaStream_t st, bool p
       if (e != cudaSuccess) return e;
       return launch_k(front_fused_kernel<true, true>, dim3(grid), dim3(kFrontThreads), kFusedSmemDual, st,
                       pdl, p);
+    }
+    if (p.norm_mean) {
+      static bool done_n[64] = {false};
+      cudaError_t e = allow_max_smem((const void*)front_fused_kernel<true, false, true>, done_n);
+      if (e != cudaSuccess) return e;
+      return launch_k(front_fused_kernel<true, false, true>, dim3(grid), dim3(kFrontThreads), kFusedSmemSingle,
+                      st, pdl, p);
     }
     cudaError_t e = allow_max_smem((const void*)front_fused_kernel<true, false>, done_f);
     if (e != cudaSuccess) return e;

@@ -232,7 +232,7 @@ template cudaError_t launch_qgemm<32>(const GemmParams&, cudaStream_t, bool);
 // the compiled actor, qrt/integration.py:206).
 __global__ void absmax_kernel(const void* x, int dtype, int64_t M, int64_t ld, int K,
                               const float* alpha, const float* beta, int round16,
-                              float* slot) {
+                              float* slot, const float* norm_mean, const float* norm_var, float norm_eps) {
   grid_dep_launch();
   ActQuant q{};
   q.let = alpha != nullptr;
@@ -255,6 +255,7 @@ __global__ void absmax_kernel(const void* x, int dtype, int64_t M, int64_t ld, i
     for (int u = 0; u < 4; ++u) {
       const int k = lane + 32 * u;
       if (k < K) {
+        if (norm_mean) v[u] = obs_norm(v[u], norm_mean, norm_var, norm_eps, k);
         const float xv = round16 ? fp16r(v[u]) : v[u];
         m = fmaxf(m, q.absz(xv, q.let ? alpha[k] : 0.0f, q.let ? beta[k] : 0.0f));
       }
@@ -262,6 +263,7 @@ __global__ void absmax_kernel(const void* x, int dtype, int64_t M, int64_t ld, i
     for (int k = lane + 128; k < K; k += 32) {     // rows wider than 128
       float xv = dtype == GLAD_DTYPE_F32 ? reinterpret_cast<const float*>(x)[r * ld + k]
                                          : __half2float(reinterpret_cast<const __half*>(x)[r * ld + k]);
+      if (norm_mean) xv = obs_norm(xv, norm_mean, norm_var, norm_eps, k);
       if (round16) xv = fp16r(xv);
       m = fmaxf(m, q.absz(xv, q.let ? alpha[k] : 0.0f, q.let ? beta[k] : 0.0f));
     }
@@ -272,11 +274,13 @@ __global__ void absmax_kernel(const void* x, int dtype, int64_t M, int64_t ld, i
 
 cudaError_t launch_absmax(const void* x, int dtype, int64_t M, int64_t ld, int K,
                           const float* alpha, const float* beta, int round16, float* slot,
-                          int num_sms, cudaStream_t st) {
+                          int num_sms, cudaStream_t st, const float* norm_mean, const float* norm_var,
+                          float norm_eps) {
   int64_t blocks = (M + 7) / 8;
   if (blocks > 4LL * num_sms) blocks = 4LL * num_sms;
   if (blocks < 1) blocks = 1;
-  absmax_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, dtype, M, ld, K, alpha, beta, round16, slot);
+  absmax_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, dtype, M, ld, K, alpha, beta, round16, slot,
+                                                  norm_mean, norm_var, norm_eps);
   return cudaGetLastError();
 }
 

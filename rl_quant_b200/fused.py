@@ -27,6 +27,21 @@ def _fp16(t: torch.Tensor, name: str) -> torch.Tensor:
     return t
 
 
+def obs_norm_struct(norm, width: int) -> N.GladObsNorm:
+    """GladObsNorm of an rsl_rl EmpiricalNormalization (rsl_rl/networks/normalization.py:
+    44-47): its fp32 ``_mean`` / ``_var`` buffers, read in place on every call, and its
+    eps. None or nn.Identity: no normaliser."""
+    if norm is None or isinstance(norm, nn.Identity):
+        return N.GladObsNorm()
+    mean, var = getattr(norm, "_mean", None), getattr(norm, "_var", None)
+    if mean is None or var is None or not hasattr(norm, "eps"):
+        raise FusedUnsupported(f"{type(norm).__name__} is not an EmpiricalNormalization (_mean, _var, eps)")
+    for t, nm in ((mean, "_mean"), (var, "_var")):
+        if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous() or t.numel() != width:
+            raise ValueError(f"normaliser {nm} must be a contiguous fp32 CUDA tensor of {width} values")
+    return N.GladObsNorm(mean.data_ptr(), var.data_ptr(), float(norm.eps), width)
+
+
 def model_act_mode(model: nn.Module) -> str:
     modes = {m.act_mode for m in model.modules() if isinstance(m, QuantLinear)}
     if len(modes) != 1 or not modes <= {"static", "dynamic"}:
@@ -55,9 +70,10 @@ class FusedActor:
         if getattr(model, "num_heads", 16) != 16 or getattr(model, "mha_dim", 64) != 64:
             raise FusedUnsupported("the fused encoder is built for D=64, 16 heads")
 
-    def weights(self) -> N.GladActorWeights:
+    def weights(self, obs_norm=None) -> N.GladActorWeights:
         m = self.model
         w = N.GladActorWeights()
+        w.obs_norm = obs_norm_struct(obs_norm, 96 + 2079)
         w.conv = m.map_cnn.conv_struct()
         w.proprio_emb = N.qlinear_struct(m.actor_proprio_embedding)
         w.query_proj = N.qlinear_struct(m.query_projector)
@@ -84,12 +100,14 @@ class FusedActor:
         return ws
 
     def run(self, obs: torch.Tensor, mean: torch.Tensor | None, aux: N.GladActorAux | None = None,
-            noise: torch.Tensor | None = None, gumbel: tuple | None = None) -> None:
+            noise: torch.Tensor | None = None, gumbel: tuple | None = None, obs_norm=None) -> None:
         """Launch the fused forward on the current stream (no host sync).
 
         ``noise``: f32 [B,187] added to the top-k logits. ``gumbel = (seed, offset)``
         instead draws the train-mode Gumbel term inside the kernel; ``offset`` is an
-        int64 device tensor of one element that every call advances by one."""
+        int64 device tensor of one element that every call advances by one.
+        ``obs_norm``: an EmpiricalNormalization applied to the f32 rows as they load
+        (the observations are then the raw group)."""
         N.require_cuda(obs)
         if obs.dim() != 2 or obs.stride(1) != 1:
             raise ValueError("obs must be a row-major [B, 96+2079] tensor")
@@ -106,13 +124,13 @@ class FusedActor:
             if offset.dtype != torch.int64 or offset.numel() != 1:
                 raise ValueError("gumbel offset must be a one-element int64 CUDA tensor")
             rc = N.load().glad_actor_forward_train(
-                self.weights(), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode],
+                self.weights(obs_norm), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode],
                 int(seed) & 0xFFFFFFFFFFFFFFFF, offset.data_ptr(), N.ptr(mean), aux, ws.data_ptr(), ws.numel(),
                 N.stream_handle(obs.device))
             N.check(rc, "glad_actor_forward_train")
             return
         rc = N.load().glad_actor_forward(
-            self.weights(), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise),
+            self.weights(obs_norm), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise),
             N.ptr(mean), aux, ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
         N.check(rc, "glad_actor_forward")
 
@@ -162,9 +180,10 @@ class FusedCritic:
         self.act_mode = model_act_mode(model)
         self._ws: dict[tuple, torch.Tensor] = {}
 
-    def weights(self) -> N.GladCriticWeights:
+    def weights(self, obs_norm=None) -> N.GladCriticWeights:
         m = self.model
         w = N.GladCriticWeights()
+        w.obs_norm = obs_norm_struct(obs_norm, self.P + 2079)
         w.conv = m.map_cnn.conv_struct()
         if self.use_actor_emb:
             w.proprio_emb_q = N.qlinear_struct(m.actor_proprio_embedding)
@@ -188,7 +207,9 @@ class FusedCritic:
                                       L.in_features, L.out_features)
         return w
 
-    def run(self, obs: torch.Tensor, value: torch.Tensor, noise: torch.Tensor | None = None) -> None:
+    def run(self, obs: torch.Tensor, value: torch.Tensor, noise: torch.Tensor | None = None,
+            obs_norm=None) -> None:
+        """``obs_norm``: an EmpiricalNormalization applied to the f32 rows as they load."""
         N.require_cuda(obs)
         if obs.dim() != 2 or obs.stride(1) != 1:
             raise ValueError("obs must be a row-major [B, P+2079] tensor")
@@ -199,7 +220,7 @@ class FusedCritic:
             ws = torch.empty(N.load().glad_critic_workspace_size(B), dtype=torch.uint8, device=obs.device)
             self._ws[key] = ws
         rc = N.load().glad_critic_forward(
-            self.weights(), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
+            self.weights(obs_norm), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
             B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise), value.data_ptr(), None,
             ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
         N.check(rc, "glad_critic_forward")

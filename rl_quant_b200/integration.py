@@ -94,7 +94,9 @@ class QRTAccelerator:
         if graph_rewrite:
             patch_encoder(infer)
         self.set_infer_training(rollout_training)
-        self._runner = InferenceRunner(infer, mode=mode, with_critic=True)
+        # observations reach the runner normalised by the fp32 master's normalisers
+        # (policy.act / evaluate_qrt), as qrt compiles its heads without them
+        self._runner = InferenceRunner(infer, mode=mode, with_critic=True, normalize=False)
         self._sync_runner = self._runner
 
         policy = self.policy
@@ -124,10 +126,10 @@ class QRTAccelerator:
         policy.update_distribution = types.MethodType(update_distribution_qrt, policy)
         policy.evaluate = types.MethodType(evaluate_qrt, policy)
 
-        # opt-in: PPO.act (ppo.py:129-140) as one fused forward -- actor + critic from one
-        # read of the height scan, then the Normal sample and its log-probability drawn
-        # in the kernel (Philox) instead of by torch.normal. Needs the policy and critic
-        # groups to carry the same scan (the critic reads it from the policy group).
+        # opt-in: PPO.act (ppo.py:129-140) as one fused forward -- actor + critic (from one
+        # read of the height scan when no normaliser is active: the policy and critic
+        # groups must then carry the same scan), then the Normal sample and its
+        # log-probability drawn in the kernel (Philox) instead of by torch.normal.
         self._orig_act = self.alg.act
         if fused_ppo_act:
             alg = self.alg
@@ -135,11 +137,13 @@ class QRTAccelerator:
             def act_fused(obs):
                 if policy.is_recurrent:
                     return acc._orig_act(obs)
-                ao = policy.actor_obs_normalizer(policy.get_actor_obs(obs))
-                co = policy.critic_obs_normalizer(policy.get_critic_obs(obs))
+                # raw groups; the master's normalisers run inside the kernels' row loads
+                ao = policy.get_actor_obs(obs)
+                co = policy.get_critic_obs(obs)
                 kw = {"log_std": policy.log_std} if getattr(policy, "noise_std_type", "scalar") == "log" \
                     else {"std": policy.std}
-                a, v, lp, m, sg = run.ppo_act(ao, co, **kw)
+                a, v, lp, m, sg = run.ppo_act(
+                    ao, co, obs_norm=(policy.actor_obs_normalizer, policy.critic_obs_normalizer), **kw)
                 t = alg.transition
                 t.actions, t.values, t.actions_log_prob = a, v, lp
                 t.action_mean, t.action_sigma = m, sg

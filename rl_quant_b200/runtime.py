@@ -20,6 +20,7 @@ from __future__ import annotations
 import warnings
 
 import torch
+import torch.nn as nn
 
 from . import _native as N
 from .encoder_opt import _gumbel_noise
@@ -103,12 +104,17 @@ class _HostPipe:
 
 class InferenceRunner:
     def __init__(self, model, mode: str = "max-autotune", with_critic: bool = False,
-                 clone_outputs: bool = False, host_lanes: int = 2):
+                 clone_outputs: bool = False, host_lanes: int = 2, normalize: bool = True):
+        """``normalize``: act/evaluate apply the model's own observation normalisers
+        first, as qrt's InferenceRunner does (act_inference and f_val, qrt/runtime.py:
+        98-106); False for observations that arrive normalised, as in qrt's integration
+        (qrt/integration.py:128-136, which compiles the heads without them)."""
         if mode not in _MODES:
             raise ValueError(f"unknown mode: {mode}")
         if host_lanes < 1:
             raise ValueError("host_lanes must be >= 1")
         self.host_lanes = host_lanes
+        self.normalize = normalize
         self._pipes: dict[tuple, _HostPipe] = {}
         if model.training:
             warnings.warn("[rl_quant_b200] model is in train mode; call model.eval() for rollouts")
@@ -142,8 +148,14 @@ class InferenceRunner:
         self._sync_items = None
 
     # -- forward functions ----------------------------------------------------------------
+    @staticmethod
+    def _apply_norm(norm, x):
+        return x if norm is None or isinstance(norm, nn.Identity) else norm(x)
+
     def _act_fn(self, po):
         if self._fused is not None:
+            if self.normalize:
+                po = self._apply_norm(getattr(self.model, "actor_obs_normalizer", None), po)
             mean = torch.empty(po.shape[0], 29, dtype=torch.float32, device=po.device)
             if self.model.training:
                 # train-mode rollouts keep the Gumbel top-k exploration (qrt/encoder_opt.py:87-91),
@@ -152,16 +164,19 @@ class InferenceRunner:
             else:
                 self._fused.run(po, mean)
             return mean
+        if not self.normalize:
+            enc, _, _, _ = self.model._encode_terrain(po)
+            return self.model.actor(enc)
         return self.model.act_inference({"policy_obs": po})[0]
 
     def _val_fn(self, co):
         m = self.model
+        c = self._apply_norm(getattr(m, "critic_obs_normalizer", None), co) if self.normalize else co
         if self._fused_critic is not None and co.shape[1] == self._fused_critic.P + 2079:
             value = torch.empty(co.shape[0], 1, dtype=torch.float32, device=co.device)
             noise = _gumbel_noise((co.shape[0], 187), co.device) if m.training else None
-            self._fused_critic.run(m.critic_obs_normalizer(co), value, noise)
+            self._fused_critic.run(c, value, noise)
             return value
-        c = m.critic_obs_normalizer(co)
         enc_fn = getattr(m, "_encode_terrain_orig", None) if co.shape[1] - 2079 != getattr(
             m, "actor_proprio_dim", -1) else None
         enc, _, _, _ = (enc_fn or m._encode_terrain)(c)
@@ -203,17 +218,26 @@ class InferenceRunner:
             self._gumbel_offset = torch.zeros(1, dtype=torch.int64, device=dev)
         return self._gumbel_seed, self._gumbel_offset
 
-    def _ppo_fn(self, po, co, std_fn):
+    def _ppo_fn(self, po, co, std_fn, norms):
         B, dev = po.shape[0], po.device
         mean = torch.empty(B, 29, dtype=torch.float32, device=dev)
         value = torch.empty(B, 1, dtype=torch.float32, device=dev)
         actions = torch.empty(B, 29, dtype=torch.float32, device=dev)
         log_prob = torch.empty(B, dtype=torch.float32, device=dev)
         sigma = torch.empty(B, 29, dtype=torch.float32, device=dev)
-        if self.model.training:
-            self._fused_ac.run(po, co, mean, value, gumbel=self._gumbel_state(dev))
+        train = self.model.training
+        an, cn = norms
+        if an is None and cn is None:
+            # one read of the shared scan for both heads
+            if train:
+                self._fused_ac.run(po, co, mean, value, gumbel=self._gumbel_state(dev))
+            else:
+                self._fused_ac.run(po, co, mean, value)
         else:
-            self._fused_ac.run(po, co, mean, value)
+            # normalised groups differ in their scans: each head loads (and normalises) its own
+            self._fused.run(po, mean, gumbel=self._gumbel_state(dev) if train else None, obs_norm=an)
+            noise = _gumbel_noise((B, 187), dev) if train else None
+            self._fused_critic.run(co, value, noise, obs_norm=cn)
         if self._ppo_rng is None or self._ppo_rng.device != dev:
             self._ppo_rng = torch.zeros(2, dtype=torch.int64, device=dev)
         ppo_epilogue(mean, std_fn(), self._ppo_seed, self._ppo_rng, actions, log_prob, sigma)
@@ -278,7 +302,7 @@ class InferenceRunner:
 
     @torch.inference_mode()
     def ppo_act(self, policy_obs, critic_obs, std: torch.Tensor | None = None,
-                log_std: torch.Tensor | None = None):
+                log_std: torch.Tensor | None = None, obs_norm: tuple | None = None):
         """One PPO.act transition (rsl_rl/algorithms/ppo.py:129-140) in one forward:
         the fused actor + critic over one read of the shared scan (train-mode Gumbel
         terms when the model is in train mode), then the Normal(mean, std) sample and
@@ -286,16 +310,34 @@ class InferenceRunner:
         actions_log_prob [B], action_mean [B,A], action_sigma [B,A]), all fp32.
         ``std`` (or ``log_std``, exponentiated per call) defaults to the model's own
         parameter; captured modes read the given tensor in place on every call, so it
-        must keep its storage (an nn.Parameter updated in place does)."""
+        must keep its storage (an nn.Parameter updated in place does).
+
+        ``obs_norm=(actor_norm, critic_norm)``: rsl_rl EmpiricalNormalization modules of
+        the two groups, applied in the kernels while the raw f32 rows load (their
+        ``_mean``/``_var`` are read in place on every call). Without it the runner's
+        ``normalize`` setting applies the model's own normalisers first."""
         if not self.with_critic:
             raise RuntimeError("ppo_act needs InferenceRunner(with_critic=True)")
-        if self._fused_ac is None and self._fused_ac_err is None:
-            try:
-                self._fused_ac = FusedActorCritic(self.model)
-            except FusedUnsupported as e:
-                self._fused_ac_err = str(e)
-        if self._fused_ac is None:
-            raise FusedUnsupported(f"fused actor + critic unavailable: {self._fused_ac_err}")
+        an, cn = obs_norm if obs_norm is not None else (None, None)
+        an = None if isinstance(an, nn.Identity) else an
+        cn = None if isinstance(cn, nn.Identity) else cn
+        if obs_norm is None and self.normalize:
+            m = self.model
+            policy_obs = self._apply_norm(getattr(m, "actor_obs_normalizer", None), policy_obs)
+            critic_obs = self._apply_norm(getattr(m, "critic_obs_normalizer", None), critic_obs)
+        if an is not None or cn is not None:
+            if self._fused is None or self._fused_critic is None:
+                raise FusedUnsupported("ppo_act with observation normalisers needs the fused actor and critic")
+            key = ("ppo", id(an), id(cn))
+        else:
+            key = ("ppo",)
+            if self._fused_ac is None and self._fused_ac_err is None:
+                try:
+                    self._fused_ac = FusedActorCritic(self.model)
+                except FusedUnsupported as e:
+                    self._fused_ac_err = str(e)
+            if self._fused_ac is None:
+                raise FusedUnsupported(f"fused actor + critic unavailable: {self._fused_ac_err}")
         if std is None and log_std is None:
             if getattr(self.model, "noise_std_type", "scalar") == "log":
                 log_std = self.model.log_std
@@ -307,8 +349,8 @@ class InferenceRunner:
         else:
             src = log_std
             std_fn = lambda: torch.exp(src.float())  # noqa: E731
-        key = ("ppo", src.data_ptr())
-        return self._call(key, lambda po, co: self._ppo_fn(po, co, std_fn), policy_obs, critic_obs)
+        key = key + (src.data_ptr(),)
+        return self._call(key, lambda po, co: self._ppo_fn(po, co, std_fn, (an, cn)), policy_obs, critic_obs)
 
     @torch.inference_mode()
     def act_sample(self, policy_obs):

@@ -183,3 +183,32 @@ def golden_model(w):
     swap_cnn(m, float(w["meta.s_cnn"]))
     patch_encoder(m)
     return m.eval(), swapped
+
+
+class EmpiricalNorm(torch.nn.Module):
+    """rsl_rl's EmpiricalNormalization restated for the tests (rsl_rl/networks/
+    normalization.py:14-80): running mean/var buffers updated in place, _std
+    recomputed as sqrt(_var), forward (x - mean) / (std + eps)."""
+
+    def __init__(self, n, eps=1e-2):
+        super().__init__()
+        self.eps = eps
+        self.register_buffer("_mean", torch.zeros(n).unsqueeze(0))
+        self.register_buffer("_var", torch.ones(n).unsqueeze(0))
+        self.register_buffer("_std", torch.ones(n).unsqueeze(0))
+        self.register_buffer("count", torch.tensor(0, dtype=torch.long))
+
+    def forward(self, x):
+        return (x - self._mean) / (self._std + self.eps)
+
+    @torch.no_grad()
+    def update(self, x):
+        count_x = x.shape[0]
+        self.count += count_x
+        rate = count_x / self.count
+        var_x = torch.var(x, dim=0, unbiased=False, keepdim=True)
+        mean_x = torch.mean(x, dim=0, keepdim=True)
+        delta_mean = mean_x - self._mean
+        self._mean += rate * delta_mean
+        self._var += rate * (var_x - self._var + delta_mean * (mean_x - self._mean))
+        self._std = torch.sqrt(self._var)

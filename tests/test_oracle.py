@@ -146,3 +146,21 @@ def test_ppo_normal_distribution_and_pairs():
     assert not np.array_equal(z, O.ppo_normal(8, 0, 2048, 29))
     a, lp = O.ppo_epilogue(np.zeros((3, 29), np.float32), np.ones(29, np.float32), 7, 0)
     assert np.array_equal(a, z[:3])
+
+
+def test_obs_normalize_matches_empirical_normalization():
+    """The oracle's normaliser is the module's forward bit for bit once _std = sqrt(_var)
+    (rsl_rl/networks/normalization.py:44-47,67-68)."""
+    import torch
+    from gpu_util import EmpiricalNorm
+    g = torch.Generator().manual_seed(4)
+    norm = EmpiricalNorm(2175)
+    for _ in range(3):
+        norm.update(3.0 * torch.randn(256, 2175, generator=g) + 1.5)
+    # on the GPU, where rsl_rl keeps the module, torch.sqrt is IEEE-rounded; torch's CPU
+    # sqrt is not always, so take _std as the rounded square root here
+    norm._std = torch.from_numpy(np.sqrt(norm._var.numpy()))
+    x = 2.0 * torch.randn(64, 2175, generator=g)
+    ref = norm(x).numpy()
+    got = O.obs_normalize(x.numpy(), norm._mean.numpy(), norm._var.numpy(), norm.eps)
+    assert np.array_equal(got, ref)
