@@ -641,8 +641,10 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
 // [128,160), conv2's in [0,128). All MMA descriptors are built once.
 // ============================================================================================
 constexpr int kFusedTmemCols = 256;
-constexpr int kIssuer = 7 * 32;          // lane 0 of warp 7 issues the conv MMAs
-constexpr int kConverters = 7 * 32;      // warps 0-6 stage and convert observation rows
+// Warps 6 and 7 issue the conv MMAs (tile t by warp 6 + t, each from one elected lane):
+// a warp's MMA issue takes ~140 cycles, so two issuers halve the chain.
+constexpr int kIssuerWarp0 = 6;
+constexpr int kConverters = 6 * 32;      // warps 0-5 stage and convert observation rows
 
 struct __align__(128) FusedSmem {
   uint8_t planes[1][kPlanesBytes];     // conv1(e) completes before the conversion of e+1 writes it
@@ -680,7 +682,7 @@ struct __align__(128) FusedSmem {
   uint64_t lg_bdesc[4];
   uint64_t pl_adesc[8];                // pooling GEMM [K-step]
   uint64_t pl_bdesc[8];
-  uint64_t bar1, bar2;                 // conv1 / (conv2, logits, pooling) completion
+  uint64_t bar1, bar2, bar3;           // conv1 (2 issuers) / conv2 (2 issuers) / logits, pooling, embedding
   uint32_t tmem_base;
   int abort_flag;
   // fused actor + critic only (launches without it allocate up to `pec_w`): the critic
@@ -713,8 +715,9 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   // ---- one-time set-up: every global read is issued before the first wait -----------------
   if (warp == 0) tmem_alloc(&s.tmem_base, kFusedTmemCols);
   if (tid == 0) {
-    mbar_init(&s.bar1, 1);
-    mbar_init(&s.bar2, 1);
+    mbar_init(&s.bar1, 2);
+    mbar_init(&s.bar2, 2);
+    mbar_init(&s.bar3, 1);
     fence_mbar_init();
     s.abort_flag = 0;
   }
@@ -723,6 +726,9 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const int row_elems = P + kMap;
   const bool dyn = p.act_mode == GLAD_ACT_DYNAMIC;
   constexpr bool dual = FULL && DUAL;
+  // int8 proprio embedding: one batched GEMM over all of this CTA's environments
+  // before the loop (fp16 embeddings keep the per-environment path)
+  const bool pe_batch = FULL && !p.pe_f16;
   const int Pc = dual ? p.prop_dim_c : 0;
   // raw conv weights -> scratch (the local-feature tile is unused until the loop)
   uint8_t* scratch = s.local16;
@@ -750,10 +756,16 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       for (int i = tid; i < kD * P / 8; i += NT)
         cp_async16(s.pe_w + 16 * i, reinterpret_cast<const uint4*>(p.pe16_w) + i);
   } else {
-    pe_w_async = (kD * P) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.pe.w8) & 15) == 0;
-    if (pe_w_async)
-      for (int i = tid; i < kD * P / 16; i += NT)
-        cp_async16(s.pe_w + 16 * i, reinterpret_cast<const uint4*>(p.pe.w8) + i);
+    // int8 embedding weights as the B operand of the batched GEMM: [16-byte K chunk]
+    // [64 n][16 B], K zero-padded to a multiple of 32 (P % 4 == 0, w8 16-byte aligned)
+    const int KC = ((P + 31) >> 5) * 2;
+    for (int idx = tid; idx < KC * kD * 4; idx += NT) {
+      const int c = idx / (kD * 4), n = (idx >> 2) % kD, t4 = idx & 3;
+      const int k = c * 16 + 4 * t4;
+      uint8_t* dst = s.pe_w + c * 1024 + n * 16 + 4 * t4;
+      if (k < P) cp_async4(dst, p.pe.w8 + (size_t)n * P + k);
+      else *reinterpret_cast<uint32_t*>(dst) = 0u;
+    }
     for (int k = tid; k < P; k += NT) {
       if (p.pe.alpha) {
         cp_async4(&s.pe_a[k], p.pe.alpha + k);
@@ -873,9 +885,6 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       }
       if (tid < kD) s.pe_bp[tid] = pe16b;
     } else {
-      if (!pe_w_async)
-        for (int i = tid; i < kD * P / 4; i += NT)
-          reinterpret_cast<int*>(s.pe_w)[i] = reinterpret_cast<const int*>(p.pe.w8)[i];
       if (dyn && !grid_absmax && tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
     }
     // every MMA descriptor of the loop, one per thread
@@ -918,7 +927,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const uint32_t tmem = s.tmem_base;
   const uint32_t tmem_c1 = tmem + 128;
   const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
-  uint32_t ph1 = 0, ph2 = 0;
+  uint32_t ph1 = 0, ph2 = 0, ph3 = 0;
   float zmax_qp = 0.0f;
   float zmax_qpc = 0.0f;                // critic query projector input (dual)
 
@@ -951,11 +960,13 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
           const int c0 = P + px * 3;
           put(px, nz(st[c0], c0), nz(st[c0 + 1], c0 + 1), nz(st[c0 + 2], c0 + 2));
         }
-        for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(nz(st[k], k));
+        if (!pe_batch)
+          for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(nz(st[k], k));
       } else {
         for (int px = tid; px < kH1 * kW1; px += nthr)
           put(px, st[P + px * 3], st[P + px * 3 + 1], st[P + px * 3 + 2]);
-        for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(st[k]);
+        if (!pe_batch)
+          for (int k = tid; k < P; k += nthr) s.prop16[b][k] = __float2half_rn(st[k]);
       }
       return;
     }
@@ -980,19 +991,19 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       pk.y = *reinterpret_cast<uint32_t*>(&h2z);
       *reinterpret_cast<uint2*>(s.planes[0] + pl * kPlaneBytes + r * kRowBytes + slot * 8) = pk;
     }
-    for (int k = tid; k < P; k += nthr)
-      s.prop16[b][k] = __float2half_rn(esz == 4 ? nz(row_elem<4>(rs, k), k) : row_elem<2>(rs, k));
+    if (!pe_batch)
+      for (int k = tid; k < P; k += nthr)
+        s.prop16[b][k] = __float2half_rn(esz == 4 ? nz(row_elem<4>(rs, k), k) : row_elem<2>(rs, k));
   };
-  auto issue_conv1 = [&](int b) {      // by lane 0 of warp 7
-    if (tid == kIssuer) {
+  auto issue_conv1 = [&](int b) {      // tile t by warp 6 + t (one elected lane each)
+    if (warp >= kIssuerWarp0) {
+      const int t = warp - kIssuerWarp0;
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(128, 16);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int pr = 0; pr < 8; ++pr)
-          mma_f16(tmem_c1 + t * 16, s.c1_adesc[b][t * 8 + pr], s.c1_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
-      mma_commit(&s.bar1);
+      for (int pr = 0; pr < 8; ++pr)
+        mma_f16_warp(tmem_c1 + t * 16, s.c1_adesc[b][t * 8 + pr], s.c1_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
+      mma_commit_warp(&s.bar1);
     }
   };
   // critic proprio embedding (fp16 nn.Linear) of buffer b on threads 128-255
@@ -1008,39 +1019,135 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       if (part == 0) s.pe16c[b][n] = __float2half_rn(a + s.pec_bp[n]);
     }
   };
-  // proprio embedding of the environment in buffer b (threads 0-127)
+  // fp16 proprio embedding (nn.Linear) of the environment in buffer b (threads 0-127)
   auto proprio_emb = [&](int b) {
-    if (p.pe_f16) {
-      if (tid < 2 * kD) {
-        const int n = tid >> 1, part = tid & 1;
-        const __half* wrow = reinterpret_cast<const __half*>(s.pe_w) + n * P;
-        const int half_k = (P + 1) >> 1;
-        const int k0 = part * half_k, k1 = min(P, k0 + half_k);
-        float a = 0.0f;
-        for (int k = k0; k < k1; ++k) a = fmaf(__half2float(s.prop16[b][k]), __half2float(wrow[k]), a);
-        a += __shfl_xor_sync(0xffffffffu, a, 1);
-        if (part == 0) s.pe16[b][n] = __float2half_rn(a + s.pe_bp[n]);
+    if (tid < 2 * kD) {
+      const int n = tid >> 1, part = tid & 1;
+      const __half* wrow = reinterpret_cast<const __half*>(s.pe_w) + n * P;
+      const int half_k = (P + 1) >> 1;
+      const int k0 = part * half_k, k1 = min(P, k0 + half_k);
+      float a = 0.0f;
+      for (int k = k0; k < k1; ++k) a = fmaf(__half2float(s.prop16[b][k]), __half2float(wrow[k]), a);
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      if (part == 0) s.pe16[b][n] = __float2half_rn(a + s.pe_bp[n]);
+    }
+  };
+  // int8 proprio embedding of ALL of this CTA's environments (qrt/qlinear.py:111-138),
+  // in batches of 128: the quantised rows [env][k] form the A operand (K-major, the
+  // local-feature tile is free until the loop), w8 the B operand, the int32 products
+  // land in TMEM columns [160, 224) and the row's thread dequantises them into pe_out.
+  // The same pass writes each row's fp16 proprio into `enc` and folds the embedding
+  // into the query projector's absmax.
+  // the 4 proprio values of item `item` (row item / (4 KC), columns 4 * (item % (4 KC))
+  // + 0..3) of the batch starting at local row j0
+  const int pe_kc = ((P + 31) >> 5) * 2;
+  const int pe_q = pe_kc * 4;
+  const int64_t pe_nloc = blockIdx.x < p.B ? (p.B - 1 - (int64_t)blockIdx.x) / gridDim.x + 1 : 0;
+  auto pe_load = [&](int item, int64_t j0) -> float4 {
+    const int r = item / pe_q, k0 = 4 * (item - r * pe_q);
+    const int64_t e = (int64_t)blockIdx.x + (j0 + r) * gridDim.x;
+    auto ld = [&](int k) {
+      if (k >= P) return 0.0f;
+      return esz == 4 ? reinterpret_cast<const float*>(p.in)[e * p.ld + k]
+                      : __half2float(reinterpret_cast<const __half*>(p.in)[e * p.ld + k]);
+    };
+    return make_float4(ld(k0), ld(k0 + 1), ld(k0 + 2), ld(k0 + 3));
+  };
+  // int8 proprio embedding of ALL of this CTA's environments (qrt/qlinear.py:111-138),
+  // in batches of 128: the quantised rows [env][k] form the A operand (K-major, the
+  // local-feature tile is free until the loop), w8 the B operand, the int32 products
+  // land in TMEM columns [160, 224); the rows' threads dequantise them into pe_out and
+  // an fp16 copy from which every thread folds the embedding into the query
+  // projector's absmax. The same pass writes each row's fp16 proprio into `enc`.
+  // `pre` holds item `tid` of the first batch, loaded before the absmax barrier.
+  auto pe_batched = [&](float4 pre) {
+    uint8_t* A = s.local16;                                   // [chunk][128 rows][16 B]
+    __half* pes = reinterpret_cast<__half*>(s.local16 + 16384);   // [row][64] fp16
+    for (int64_t j0 = 0; j0 < pe_nloc; j0 += 128) {
+      const int nb = (int)(pe_nloc - j0 < 128 ? pe_nloc - j0 : 128);
+      // rows past nb keep whatever bytes the tile holds (their products are never read)
+      for (int item = tid; item < nb * pe_q; item += NT) {
+        const int r = item / pe_q, k0 = 4 * (item - r * pe_q);
+        const int64_t e = (int64_t)blockIdx.x + (j0 + r) * gridDim.x;
+        const float4 x = (j0 == 0 && item == tid) ? pre : pe_load(item, j0);
+        auto cv = [&](float v, int k) { return __float2half_rn(esz == 4 ? nz(v, k) : v); };
+        const __half h0 = cv(x.x, k0), h1 = cv(x.y, k0 + 1), h2 = cv(x.z, k0 + 2), h3 = cv(x.w, k0 + 3);
+        auto qz = [&](__half h, int k) {
+          return k < P ? ((uint32_t)aq_pe.quant(__half2float(h), s.pe_a[k], s.pe_b[k]) & 0xFFu) : 0u;
+        };
+        const uint32_t w = qz(h0, k0) | (qz(h1, k0 + 1) << 8) | (qz(h2, k0 + 2) << 16) | (qz(h3, k0 + 3) << 24);
+        *reinterpret_cast<uint32_t*>(A + (k0 >> 4) * 2048 + r * 16 + (k0 & 15)) = w;
+        __half* er = p.enc + e * p.ld_enc + 128 + k0;
+        if (k0 + 4 <= P && (reinterpret_cast<uintptr_t>(er) & 7) == 0) {
+          const __half2 a01 = __halves2half2(h0, h1), a23 = __halves2half2(h2, h3);
+          *reinterpret_cast<uint2*>(er) = make_uint2(*reinterpret_cast<const uint32_t*>(&a01),
+                                                     *reinterpret_cast<const uint32_t*>(&a23));
+        } else {
+          if (k0 < P) er[0] = h0;
+          if (k0 + 1 < P) er[1] = h1;
+          if (k0 + 2 < P) er[2] = h2;
+          if (k0 + 3 < P) er[3] = h3;
+        }
       }
-    } else if (tid < 2 * kD) {
-      // warps 0-3 only (named barrier 3), so warp 7 can issue MMAs meanwhile
-      for (int k = tid; k < P; k += 2 * kD)
-        s.q8[k] = (int8_t)aq_pe.quant(__half2float(s.prop16[b][k]), s.pe_a[k], s.pe_b[k]);
-      named_bar_sync(3, 2 * kD);
-      {
-        const int n = tid >> 1, part = tid & 1;
-        const int* wrow = reinterpret_cast<const int*>(s.pe_w + n * P) + part * (P / 8);
-        const int* qw = reinterpret_cast<const int*>(s.q8) + part * (P / 8);
-        int acc = 0;
-        for (int k4 = 0; k4 < P / 8; ++k4) acc = __dp4a(qw[k4], wrow[k4], acc);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        if (part == 0) s.pe16[b][n] = qlinear_out(acc, s.pe_scale[n], s.pe_bp[n]);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (warp == 7) {
+        tc_fence_after();
+        constexpr uint32_t idesc = idesc_i8(128, 64);
+        for (int kk = 0; kk < pe_kc / 2; ++kk)
+          mma_i8_warp(tmem + 160, smem_desc(smem_u32(A) + kk * 4096, 2048, 128),
+                      smem_desc(smem_u32(s.pe_w) + kk * 2048, 1024, 128), idesc, kk > 0 ? 1u : 0u);
+        mma_commit_warp(&s.bar3);
       }
+      if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
+      ph3 ^= 1;
+      tc_fence_after();
+      __syncthreads();
+      if (s.abort_flag) return;
+      if (32 * quarter < nb) {
+        // warps w and w + 4 share TMEM lanes 32*(w & 3)..: each takes two of the four
+        // 16-column chunks of its rows
+        const int r = 32 * quarter + lane;
+        const int64_t e = (int64_t)blockIdx.x + (j0 + r) * gridDim.x;
+#pragma unroll 1
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+          uint32_t acc[16];
+          tmem_ld16(tmem + lane_base + 160 + 16 * c, acc);
+          tmem_ld_wait();
+          if (r < nb) {
+            uint32_t hw[8];
+#pragma unroll
+            for (int t = 0; t < 16; t += 2) {
+              const int n = 16 * c + t;
+              const __half2 h2 = __halves2half2(qlinear_out((int32_t)acc[t], s.pe_scale[n], s.pe_bp[n]),
+                                                qlinear_out((int32_t)acc[t + 1], s.pe_scale[n + 1], s.pe_bp[n + 1]));
+              hw[t >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            const uint4 v0 = make_uint4(hw[0], hw[1], hw[2], hw[3]), v1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            uint4* dst = reinterpret_cast<uint4*>(p.pe_out + e * kD + 16 * c);
+            dst[0] = v0;
+            dst[1] = v1;
+            uint4* sp = reinterpret_cast<uint4*>(pes + r * kD + 16 * c);
+            sp[0] = v0;
+            sp[1] = v1;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncthreads();
+      if (dyn)
+        for (int idx = tid; idx < nb * kD; idx += NT) {
+          const int n = idx & (kD - 1);
+          zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(pes[idx]), s.qp_a[kD + n], s.qp_b[kD + n]));
+        }
+      __syncthreads();                  // A, pes and the TMEM columns are reused by the next batch
     }
   };
 
   // ---- prologue: first environment through conv1 issue ---------------------------------
-  // In the loop, warps 0-6 stage and convert observation rows (named barrier 1) while
-  // lane 0 of warp 7 issues the conv MMAs; only warps 0-6 own cp.async groups there.
+  // In the loop, warps 0-5 stage and convert observation rows (named barrier 1) while
+  // warps 6 and 7 issue the conv MMAs; only warps 0-5 own cp.async groups there.
   if (env < p.B) {
     convert(env, 0, NT);                // its row was staged with the set-up copies
     fence_async_smem();
@@ -1053,6 +1160,9 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       row_issue(row_stage(p.in_c, nx, p.ld_c, esz, Pc, s.stage_c), tid, kConverters);
     cp_async_commit();
     issue_conv1(0);
+    // the first embedding batch's proprio values, in flight while the barrier is awaited
+    float4 pe_pre = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (pe_batch && tid < (pe_nloc < 128 ? (int)pe_nloc : 128) * pe_q) pe_pre = pe_load(tid, 0);
     if (grid_absmax) {
       // every CTA has added its part of the proprio absmax (bounded spin, 2 s)
       if (tid == 0) {
@@ -1075,7 +1185,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       if (tid < kD) s.pe_scale[tid] = __fmul_rn(s.pe_scale[tid], aq_pe.s);   // s_w * s_z
       __syncthreads();
     }
-    if (FULL) proprio_emb(0);
+    if (pe_batch) pe_batched(pe_pre);
+    else if (FULL) proprio_emb(0);
     if (dual) critic_emb(0);
   }
 
@@ -1123,22 +1234,21 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     tc_fence_before();
     fence_async_smem();
     __syncthreads();
-    if (tid == kIssuer) {
+    if (warp >= kIssuerWarp0) {
+      const int t = warp - kIssuerWarp0;
       tc_fence_after();
       constexpr uint32_t idesc = idesc_i8(128, 64);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int pr = 0; pr < 5; ++pr)
-          mma_i8(tmem + t * 64, s.c2_adesc[t * 5 + pr], s.c2_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
-      mma_commit(&s.bar2);
+      for (int pr = 0; pr < 5; ++pr)
+        mma_i8_warp(tmem + t * 64, s.c2_adesc[t * 5 + pr], s.c2_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
+      mma_commit_warp(&s.bar2);
     }
 
-    // ---- next environment: warps 0-6 convert and prefetch while warp 7 issues; then
-    //      warp 7 issues its conv1 and warps 0-3 compute its proprio embedding ---------------
+    // ---- next environment: warps 0-5 convert and prefetch while warps 6-7 issue; then
+    //      warps 6-7 issue its conv1 (warps 0-3 compute an fp16 proprio embedding) ---------
     if (nxt < p.B) {
-      if (warp == 7) {
-        named_bar_sync(2, NT);            // planes of e+1 written by warps 0-6
+      if (warp >= kIssuerWarp0) {
+        named_bar_sync(2, NT);            // planes of e+1 written by warps 0-5
         issue_conv1(b ^ 1);
         if (dual) critic_emb(b ^ 1);
       } else {
@@ -1153,7 +1263,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, kConverters);
         if (dual && nn < p.B) row_issue(row_stage(p.in_c, nn, p.ld_c, esz, Pc, s.stage_c), tid, kConverters);
         cp_async_commit();
-        if (FULL) proprio_emb(b ^ 1);
+        if (FULL && !pe_batch) proprio_emb(b ^ 1);
         if (dual) critic_emb(b ^ 1);
       }
     }
@@ -1248,18 +1358,18 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     fence_async_smem();
     __syncthreads();
     // logits of both heads for every row: [gps, scorer-local] = local @ [w_g; w_s]^T (fp32 in TMEM)
-    if (tid == 0) {
+    if (warp == 0) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(128, 16);
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16(tmem + 160 + 16 * t, s.lg_adesc[t][kk], s.lg_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
-      mma_commit(&s.bar2);
+          mma_f16_warp(tmem + 160 + 16 * t, s.lg_adesc[t][kk], s.lg_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+      mma_commit_warp(&s.bar3);
     }
-    if (!mbar_wait_bounded(&s.bar2, ph2)) s.abort_flag = 1;
-    ph2 ^= 1;
+    if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
+    ph3 ^= 1;
     tc_fence_after();
     __syncthreads();
     if (s.abort_flag) break;
@@ -1309,15 +1419,16 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     __syncthreads();
     // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77): row
     // tile*64 + c of the pooling GEMM, column `tile`
-    if (tid == 0) {
+    if (warp == 0) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16_amajor_m(128, 16);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_f16(tmem + 192, s.pl_adesc[kk], s.pl_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
-      mma_commit(&s.bar2);
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_warp(tmem + 192, s.pl_adesc[kk], s.pl_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+      mma_commit_warp(&s.bar3);
     }
-    if (!mbar_wait_bounded(&s.bar2, ph2)) s.abort_flag = 1;
-    ph2 ^= 1;
+    if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
+    ph3 ^= 1;
     tc_fence_after();
     __syncthreads();
     if (s.abort_flag) break;
@@ -1335,16 +1446,17 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       const __half gh = __float2half_rn(g);
       s.gc16[tid] = gh;
       p.enc[env * p.ld_enc + 64 + tid] = gh;
-      p.pe_out[env * kD + tid] = s.pe16[b][tid];
+      if (!pe_batch) p.pe_out[env * kD + tid] = s.pe16[b][tid];
       if (dual) {
         p.enc_c[env * p.ld_enc_c + 64 + tid] = gh;
         p.pe_c_out[env * kD + tid] = s.pe16c[b][tid];
       }
     }
-    for (int k = tid; k < P; k += NT) p.enc[env * p.ld_enc + 128 + k] = s.prop16[b][k];
+    if (!pe_batch)
+      for (int k = tid; k < P; k += NT) p.enc[env * p.ld_enc + 128 + k] = s.prop16[b][k];
     for (int k = tid; k < Pc; k += NT) p.enc_c[env * p.ld_enc_c + 128 + k] = s.prop16c[b][k];
     __syncthreads();
-    if (p.act_mode == GLAD_ACT_DYNAMIC && tid < 2 * kD) {
+    if (p.act_mode == GLAD_ACT_DYNAMIC && tid < (pe_batch ? kD : 2 * kD)) {
       const float x = __half2float(tid < kD ? s.gc16[tid] : s.pe16[b][tid - kD]);
       zmax_qp = fmaxf(zmax_qp, aq_qp.absz(x, s.qp_a[tid], s.qp_b[tid]));
     }
@@ -1361,6 +1473,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   if (s.abort_flag) {
     mbar_wait_bounded(&s.bar1, ph1);
     mbar_wait_bounded(&s.bar2, ph2);
+    mbar_wait_bounded(&s.bar3, ph3);
   }
   if (FULL && p.act_mode == GLAD_ACT_DYNAMIC) {
     // one atomic per CTA on the query projector's absmax slot
