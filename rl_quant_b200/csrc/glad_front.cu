@@ -133,6 +133,21 @@ __device__ __forceinline__ void row_issue(const RowStage& r, int tid, int nthr) 
   else if (tid < nh + nt) cp_async4(r.stage + r.body_hi + 4 * (tid - nh), r.src + r.body_hi + 4 * (tid - nh));
 }
 
+// The same with the 16-byte body as ONE bulk copy by thread 0, whose completion
+// (a phase of `bar`) the consumers wait for; the ragged head and tail words still go
+// by 4-byte cp.async (consumers also wait for their cp.async groups).
+__device__ __forceinline__ void row_issue_bulk(const RowStage& r, uint64_t* bar, int tid) {
+  const uint32_t n = r.body_hi - r.body_lo;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, n);
+    if (n) bulk_copy_g2s(r.stage + r.body_lo, r.src + r.body_lo, n, bar);
+  }
+  const int nh = (int)(r.body_lo - r.lo) >> 2, nt = (int)(r.hi - r.body_hi) >> 2;   // <= 3 each
+  if (tid >= 1 && tid <= nh) cp_async4(r.stage + r.lo + 4 * (tid - 1), r.src + r.lo + 4 * (tid - 1));
+  else if (tid > nh && tid <= nh + nt)
+    cp_async4(r.stage + r.body_hi + 4 * (tid - 1 - nh), r.src + r.body_hi + 4 * (tid - 1 - nh));
+}
+
 template <int ESZ>
 __device__ __forceinline__ float row_elem(const RowStage& r, int i) {
   const uint32_t b = (uint32_t)i * ESZ;
@@ -683,6 +698,7 @@ struct __align__(128) FusedSmem {
   uint64_t pl_adesc[8];                // pooling GEMM [K-step]
   uint64_t pl_bdesc[8];
   uint64_t bar1, bar2, bar3;           // conv1 (2 issuers) / conv2 (2 issuers) / logits, pooling, embedding
+  uint64_t bar_row;                    // bulk copy of the next observation row
   uint32_t tmem_base;
   int abort_flag;
   // fused actor + critic only (launches without it allocate up to `pec_w`): the critic
@@ -718,6 +734,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     mbar_init(&s.bar1, 2);
     mbar_init(&s.bar2, 2);
     mbar_init(&s.bar3, 1);
+    mbar_init(&s.bar_row, 1);
     fence_mbar_init();
     s.abort_flag = 0;
   }
@@ -928,6 +945,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const uint32_t tmem_c1 = tmem + 128;
   const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
   uint32_t ph1 = 0, ph2 = 0, ph3 = 0;
+  uint32_t ph_row = 0;                  // next phase of bar_row the converters consume
+  bool row_pending = false;             // a bulk row copy is in flight (converters)
   float zmax_qp = 0.0f;
   float zmax_qpc = 0.0f;                // critic query projector input (dual)
 
@@ -1154,8 +1173,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     tc_fence_before();
     __syncthreads();
     const int64_t nx = env + gridDim.x;
-    if (nx < p.B && tid < kConverters)
-      row_issue(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), tid, kConverters);
+    if (nx < p.B && tid < kConverters) {
+      row_issue_bulk(row_stage(p.in, nx, p.ld, esz, row_elems, s.stage), &s.bar_row, tid);
+      row_pending = true;
+    }
     if (dual && nx < p.B && tid < kConverters)
       row_issue(row_stage(p.in_c, nx, p.ld_c, esz, Pc, s.stage_c), tid, kConverters);
     cp_async_commit();
@@ -1253,6 +1274,12 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         if (dual) critic_emb(b ^ 1);
       } else {
         cp_async_wait_all();
+        if (mbar_wait_bounded(&s.bar_row, ph_row)) {   // the bulk body of row e+1
+          ph_row ^= 1;
+          row_pending = false;
+        } else {
+          s.abort_flag = 1;                 // the teardown waits for it once more
+        }
         named_bar_sync(1, kConverters);   // the staged row of e+1 is complete
         convert(nxt, b ^ 1, kConverters);
         fence_async_smem();
@@ -1260,7 +1287,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         named_bar_arrive(2, NT);          // planes ready for the issuer
         named_bar_sync(1, kConverters);   // every converter is done with the stage buffer
         const int64_t nn = nxt + gridDim.x;
-        if (nn < p.B) row_issue(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), tid, kConverters);
+        if (nn < p.B) {
+          row_issue_bulk(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), &s.bar_row, tid);
+          row_pending = true;
+        }
         if (dual && nn < p.B) row_issue(row_stage(p.in_c, nn, p.ld_c, esz, Pc, s.stage_c), tid, kConverters);
         cp_async_commit();
         if (FULL && !pe_batch) proprio_emb(b ^ 1);
@@ -1470,6 +1500,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
 
   // ---- teardown ----------------------------------------------------------------------------
   cp_async_wait_all();
+  if (row_pending) mbar_wait_bounded(&s.bar_row, ph_row);   // an aborted loop's row copy in flight
   if (s.abort_flag) {
     mbar_wait_bounded(&s.bar1, ph1);
     mbar_wait_bounded(&s.bar2, ph2);
