@@ -697,7 +697,8 @@ struct __align__(128) FusedSmem {
   uint64_t lg_bdesc[4];
   uint64_t pl_adesc[8];                // pooling GEMM [K-step]
   uint64_t pl_bdesc[8];
-  uint64_t bar1, bar2, bar3;           // conv1 (2 issuers) / conv2 (2 issuers) / logits, pooling, embedding
+  uint64_t bar1, bar2, bar3;           // conv1 / conv2 / logits and pooling (two issuing warps each)
+  uint64_t bar_pe;                     // batched proprio embedding
   uint64_t bar_row;                    // bulk copy of the next observation row
   uint32_t tmem_base;
   int abort_flag;
@@ -733,7 +734,8 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   if (tid == 0) {
     mbar_init(&s.bar1, 2);
     mbar_init(&s.bar2, 2);
-    mbar_init(&s.bar3, 1);
+    mbar_init(&s.bar3, 2);
+    mbar_init(&s.bar_pe, 1);
     mbar_init(&s.bar_row, 1);
     fence_mbar_init();
     s.abort_flag = 0;
@@ -944,7 +946,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const uint32_t tmem = s.tmem_base;
   const uint32_t tmem_c1 = tmem + 128;
   const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
-  uint32_t ph1 = 0, ph2 = 0, ph3 = 0;
+  uint32_t ph1 = 0, ph2 = 0, ph3 = 0, ph_pe = 0;
   uint32_t ph_row = 0;                  // next phase of bar_row the converters consume
   bool row_pending = false;             // a bulk row copy is in flight (converters)
   float zmax_qp = 0.0f;
@@ -1117,10 +1119,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         for (int kk = 0; kk < pe_kc / 2; ++kk)
           mma_i8_warp(tmem + 160, smem_desc(smem_u32(A) + kk * 4096, 2048, 128),
                       smem_desc(smem_u32(s.pe_w) + kk * 2048, 1024, 128), idesc, kk > 0 ? 1u : 0u);
-        mma_commit_warp(&s.bar3);
+        mma_commit_warp(&s.bar_pe);
       }
-      if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
-      ph3 ^= 1;
+      if (!mbar_wait_bounded(&s.bar_pe, ph_pe)) s.abort_flag = 1;
+      ph_pe ^= 1;
       tc_fence_after();
       __syncthreads();
       if (s.abort_flag) return;
@@ -1387,15 +1389,15 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     tc_fence_before();
     fence_async_smem();
     __syncthreads();
-    // logits of both heads for every row: [gps, scorer-local] = local @ [w_g; w_s]^T (fp32 in TMEM)
-    if (warp == 0) {
+    // logits of both heads for every row: [gps, scorer-local] = local @ [w_g; w_s]^T (fp32 in
+    // TMEM), tile t issued by warp t
+    if (warp < 2) {
+      const int t = warp;
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16(128, 16);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f16_warp(tmem + 160 + 16 * t, s.lg_adesc[t][kk], s.lg_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_warp(tmem + 160 + 16 * t, s.lg_adesc[t][kk], s.lg_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
       mma_commit_warp(&s.bar3);
     }
     if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
@@ -1448,13 +1450,16 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     fence_async_smem();
     __syncthreads();
     // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77): row
-    // tile*64 + c of the pooling GEMM, column `tile`
-    if (warp == 0) {
+    // tile*64 + c of the pooling GEMM, column `tile`; warp h sums the rows 64h..64h+63 of
+    // each tile into its own accumulator (TMEM columns 192 + 16h)
+    if (warp < 2) {
+      const int h = warp;
       tc_fence_after();
       constexpr uint32_t idesc = idesc_f16_amajor_m(128, 16);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_warp(tmem + 192, s.pl_adesc[kk], s.pl_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_warp(tmem + 192 + 16 * h, s.pl_adesc[4 * h + kk], s.pl_bdesc[4 * h + kk], idesc,
+                     kk > 0 ? 1u : 0u);
       mma_commit_warp(&s.bar3);
     }
     if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
@@ -1463,11 +1468,12 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     __syncthreads();
     if (s.abort_flag) break;
     if (warp < 4) {
-      uint32_t d0, d1;
+      uint32_t d0, d1, e0, e1;
       tmem_ld2(tmem + lane_base + 192, d0, d1);
+      tmem_ld2(tmem + lane_base + 208, e0, e1);
       tmem_ld_wait();
       const int mrow = 32 * warp + lane;
-      s.poolv[mrow] = __uint_as_float(mrow < 64 ? d0 : d1);
+      s.poolv[mrow] = __fadd_rn(__uint_as_float(mrow < 64 ? d0 : d1), __uint_as_float(mrow < 64 ? e0 : e1));
     }
     tc_fence_before();
     __syncthreads();
@@ -1505,6 +1511,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     mbar_wait_bounded(&s.bar1, ph1);
     mbar_wait_bounded(&s.bar2, ph2);
     mbar_wait_bounded(&s.bar3, ph3);
+    mbar_wait_bounded(&s.bar_pe, ph_pe);
   }
   if (FULL && p.act_mode == GLAD_ACT_DYNAMIC) {
     // one atomic per CTA on the query projector's absmax slot
