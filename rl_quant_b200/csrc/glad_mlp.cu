@@ -46,7 +46,12 @@ constexpr int kFCount = 1664;
 constexpr int kOffBar = kOffF + kFCount * 4;        // mbarrier, TMEM slot, abort flag
 constexpr int kOffRed = kOffBar + 64;                // per-warp maxima [16]
 constexpr int kMlpSmem = kOffRed + 64;
-constexpr uint32_t kMlpTmemCols = 128;
+// Each layer's K is split over kMlpChains partial accumulators issued by warps 0-3 in
+// parallel (an MMA issue costs ~140 cycles per warp); the int32 partial sums are added
+// exactly in the epilogue. Chain c occupies TMEM columns [c*N, (c+1)*N); every layer
+// has at least four 32-wide K steps, so every chain is written.
+constexpr int kMlpChains = 4;
+constexpr uint32_t kMlpTmemCols = 512;
 static_assert(kMlpSmem + 128 <= 227 * 1024, "shared memory");
 
 // per-layer shape: K, own output columns, column base into the per-column tables
@@ -101,15 +106,17 @@ __device__ __forceinline__ uint4 mlp_quant16(const uint4 v0, const uint4 v1, con
 __device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mbar, uint32_t& phase,
                                         int* abort_flag, bool& mma_timeout, int abuf, int wbuf, int K,
                                         uint32_t idesc, int nj) {
-  if (threadIdx.x == 0) {
+  const int w = threadIdx.x >> 5;
+  if (w < kMlpChains) {
+    // chain w: K steps w, w + 4, ... into columns [w*nj, (w+1)*nj), from one elected lane
     tc_fence_after();
     const uint32_t ab = smem_u32(sm + abuf), bb = smem_u32(sm + wbuf);
-    for (int kc = 0; kc < K / 32; ++kc) {
+    for (int kc = w; kc < K / 32; kc += kMlpChains) {
       const uint64_t ad = smem_desc(ab + kc * 2 * 2048, 2048, 128);
       const uint64_t bd = smem_desc(bb + kc * 2 * nj * 16, nj * 16, 128);
-      mma_i8(tmem, ad, bd, idesc, kc > 0 ? 1u : 0u);
+      mma_i8_warp(tmem + (uint32_t)(w * nj), ad, bd, idesc, kc >= kMlpChains ? 1u : 0u);
     }
-    mma_commit(mbar);
+    mma_commit_warp(mbar);
   }
   if (!mbar_wait_bounded(mbar, phase)) {
     *abort_flag = 1;
@@ -118,6 +125,21 @@ __device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mb
   phase ^= 1;
   tc_fence_after();
   __syncthreads();
+}
+
+// 16 accumulator columns at `taddr`: the sum of the kMlpChains partial chains (int32,
+// exact), chain c at column offset c * nj.
+__device__ __forceinline__ void mlp_ld_acc(uint32_t taddr, int nj, uint32_t (&r)[16]) {
+  tmem_ld16(taddr, r);
+#pragma unroll 1
+  for (int c = 1; c < kMlpChains; ++c) {
+    uint32_t t[16];
+    tmem_ld16(taddr + (uint32_t)(c * nj), t);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = (uint32_t)((int32_t)r[j] + (int32_t)t[j]);
+  }
+  tmem_ld_wait();
 }
 
 // Grid-wide barrier on counter `ctr` (one arrival per CTA), folded with the batch
@@ -168,7 +190,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
 
   if (warp == 0) tmem_alloc(tmem_slot, kMlpTmemCols);
   if (tid == 0) {
-    mbar_init(mbar, 1);
+    mbar_init(mbar, kMlpChains);
     fence_mbar_init();
     *abort_flag = 0;
   }
@@ -264,8 +286,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
 #pragma unroll 1
       for (int ch = part; ch < nch; ch += 4) {
         uint32_t r[16];
-        tmem_ld16(tmem + lane_base + ch * 16, r);
-        tmem_ld_wait();
+        mlp_ld_acc(tmem + lane_base + ch * 16, NJ, r);
         uint32_t h[8];
 #pragma unroll
         for (int j = 0; j < 16; j += 4) {
@@ -338,8 +359,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     if (!*abort_flag && part < 2) {
       const int col0 = part * 16;
       uint32_t r[16];
-      tmem_ld16(tmem + lane_base + col0, r);
-      tmem_ld_wait();
+      mlp_ld_acc(tmem + lane_base + col0, 32, r);
       if (row_ok) {
         float* dst = p.mean + m * p.ldm;
 #pragma unroll
