@@ -751,15 +751,19 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   const int Pc = dual ? p.prop_dim_c : 0;
   // raw conv weights -> scratch (the local-feature tile is unused until the loop)
   uint8_t* scratch = s.local16;
+  #pragma unroll 1
   for (int i = tid; i < 3 * 64 * 64 / 16; i += NT)
     cp_async16(scratch + 16 * i, reinterpret_cast<const uint4*>(p.conv.w8) + i);
+  #pragma unroll 1
   for (int i = tid; i < 128 * 16 * 2 / 16; i += NT)
     cp_async16(scratch + 12288 + 16 * i, reinterpret_cast<const uint4*>(p.conv.w1p) + i);
+  #pragma unroll 1
   for (int i = tid; i < 16; i += NT) {
     cp_async4(&s.b1[i], p.conv.b1f + i);
     cp_async4(&s.qa[i], p.conv.qa + i);
     cp_async4(&s.qc[i], p.conv.qc + i);
   }
+  #pragma unroll 1
   for (int i = tid; i < 64; i += NT) {
     cp_async4(&s.dq[i], p.conv.dq + i);
     cp_async4(&s.b2[i], p.conv.b2f + i);
@@ -772,12 +776,14 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   } else if (p.pe_f16) {
     pe_w_async = (kD * P) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pe16_w) & 15) == 0;
     if (pe_w_async)
+      #pragma unroll 1
       for (int i = tid; i < kD * P / 8; i += NT)
         cp_async16(s.pe_w + 16 * i, reinterpret_cast<const uint4*>(p.pe16_w) + i);
   } else {
     // int8 embedding weights as the B operand of the batched GEMM: [16-byte K chunk]
     // [64 n][16 B], K zero-padded to a multiple of 32 (P % 4 == 0, w8 16-byte aligned)
     const int KC = ((P + 31) >> 5) * 2;
+    #pragma unroll 1
     for (int idx = tid; idx < KC * kD * 4; idx += NT) {
       const int c = idx / (kD * 4), n = (idx >> 2) % kD, t4 = idx & 3;
       const int k = c * 16 + 4 * t4;
@@ -785,6 +791,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       if (k < P) cp_async4(dst, p.pe.w8 + (size_t)n * P + k);
       else *reinterpret_cast<uint32_t*>(dst) = 0u;
     }
+    #pragma unroll 1
     for (int k = tid; k < P; k += NT) {
       if (p.pe.alpha) {
         cp_async4(&s.pe_a[k], p.pe.alpha + k);
@@ -794,11 +801,13 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         s.pe_b[k] = 0.0f;
       }
     }
+    #pragma unroll 1
     for (int i = tid; i < kD; i += NT) {
       cp_async4(&s.pe_scale[i], (dyn ? p.pe.s_w : p.pe.dq_scale) + i);   // raw; scaled below
       cp_async4(&s.pe_bp[i], p.pe.b_prime + i);
     }
   }
+  #pragma unroll 1
   for (int k = tid; k < 128; k += NT) {
     if (FULL && p.qp.alpha) {
       cp_async4(&s.qp_a[k], p.qp.alpha + k);
@@ -812,6 +821,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   if (dual) {
     pec_w_async = (kD * Pc) % 8 == 0 && (reinterpret_cast<uintptr_t>(p.pec_w) & 15) == 0;
     if (pec_w_async)
+      #pragma unroll 1
       for (int i = tid; i < kD * Pc / 8; i += NT)
         cp_async16(s.pec_w + 16 * i, reinterpret_cast<const uint4*>(p.pec_w) + i);
   }
@@ -848,9 +858,13 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   if (FULL && p.pe_f16 && tid < kD && p.pe16_b) pe16b = __half2float(p.pe16_b[tid]);
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
+    #pragma unroll 1
     for (int i = tid; i < kPlanesBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.planes[0][0])[i] = z;
+    #pragma unroll 1
     for (int i = tid; i < kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(s.strip)[i] = z;
+    #pragma unroll 1
     for (int i = tid; i < 16 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.bpool)[i] = z;
+    #pragma unroll 1
     for (int i = tid; i < 8 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(s.blog)[i] = z;
   }
   grid_dep_wait();                      // slots written by the preceding kernel are visible from here
@@ -873,6 +887,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   {
     const __half* w1p = reinterpret_cast<const __half*>(scratch + 12288);
     __half* dst = reinterpret_cast<__half*>(s.w1s);
+    #pragma unroll 1
     for (int idx = tid; idx < kW1sBytes / 2; idx += NT) {
       const int pr = idx >> 8, c = (idx >> 7) & 1, n = (idx >> 3) & 15, e = idx & 7;
       const int q = 2 * pr + c;
@@ -892,6 +907,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     if (dual) {
       if (!pec_w_async) {
         __half* dw = reinterpret_cast<__half*>(s.pec_w);
+        #pragma unroll 1
         for (int i = tid; i < kD * Pc; i += NT) dw[i] = p.pec_w[i];
       }
       if (tid < kD) s.pec_bp[tid] = p.pec_b ? __half2float(p.pec_b[tid]) : 0.0f;
@@ -900,6 +916,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     } else if (p.pe_f16) {
       if (!pe_w_async) {
         __half* dw = reinterpret_cast<__half*>(s.pe_w);
+        #pragma unroll 1
         for (int i = tid; i < kD * P; i += NT) dw[i] = p.pe16_w[i];
       }
       if (tid < kD) s.pe_bp[tid] = pe16b;
