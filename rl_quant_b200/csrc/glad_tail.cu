@@ -239,15 +239,38 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
           key[j] = (ord16(lh) << 16) | (uint32_t)(0xFFFF - i);
         }
       }
-      uint32_t thr = 0;
+      // threshold = the 32nd largest key: first the 32nd largest fp16 value t (radix over
+      // the 16 value bits, two bits per step, the three counts of a step packed into one
+      // warp reduction: 10 bits each, at most 187), then among the keys of value t the
+      // (32 - #greater)-th lowest token index
+      uint32_t thr;
+      {
+        uint32_t t = 0;
 #pragma unroll 1
-      for (int bit = 31; bit >= 0; --bit) {
-        const uint32_t cand = thr | (1u << bit);
-        int cnt = 0;
+        for (int bb = 30; bb >= 16; bb -= 2) {
+          const uint32_t c1 = t | (1u << bb), c2 = t | (2u << bb), c3 = t | (3u << bb);
+          uint32_t pk = 0;
 #pragma unroll
-        for (int j = 0; j < 6; ++j) cnt += key[j] >= cand ? 1 : 0;
-        cnt = __reduce_add_sync(0xffffffffu, cnt);
-        if (cnt >= kTopK) thr = cand;
+          for (int j = 0; j < 6; ++j)
+            pk += (key[j] >= c1 ? 1u : 0u) + (key[j] >= c2 ? (1u << 10) : 0u) + (key[j] >= c3 ? (1u << 20) : 0u);
+          pk = __reduce_add_sync(0xffffffffu, pk);
+          const uint32_t n1 = pk & 1023u, n2 = (pk >> 10) & 1023u, n3 = pk >> 20;
+          t = n3 >= kTopK ? c3 : n2 >= kTopK ? c2 : n1 >= kTopK ? c1 : t;
+        }
+        uint32_t gt = 0;
+#pragma unroll
+        for (int j = 0; j < 6; ++j) gt += key[j] > (t | 0xFFFFu) ? 1u : 0u;   // value above t
+        const int need = kTopK - (int)__reduce_add_sync(0xffffffffu, gt);   // >= 1
+        int acc = 0;
+        thr = t;
+#pragma unroll
+        for (int j = 0; j < 6; ++j) {
+          const uint32_t ball = __ballot_sync(0xffffffffu, key[j] != 0 && (key[j] & 0xFFFF0000u) == t);
+          const int c = __popc(ball);
+          if (acc < need && acc + c >= need)
+            thr = t | (0xFFFFu - (uint32_t)(32 * j + (int)__fns(ball, 0, need - acc)));
+          acc += c;
+        }
       }
       int base = 0;
       const uint32_t lt = (1u << lane) - 1u;
