@@ -556,7 +556,11 @@ def run_reference(args):
     from oracle.cpu_fp32 import time_fp32_forward
 
     per_step_budget = 60.0 / max(args.steps + args.warmup, 1)
-    r0 = time_fp32_forward(batch=256, budget_s=0.0, min_reps=2, max_reps=2)
+    r0 = time_fp32_forward(batch=256, budget_s=0.0, min_reps=3, max_reps=3)      # first warm-up steps
+    # the rest of the W warm-up steps, at most ~10 s of them (at least 3 in all)
+    warm = max(3, min(args.warmup, 3 + int(10.0 / max(r0["sec_per_step"], 1e-6))))
+    if warm > 3:
+        time_fp32_forward(batch=256, budget_s=0.0, min_reps=warm - 3, max_reps=warm - 3)
     steps = args.steps
     if r0["sec_per_step"] > per_step_budget:
         steps = max(3, int(60.0 / r0["sec_per_step"]))
@@ -564,7 +568,7 @@ def run_reference(args):
     v = r["obs_per_s"]
     line = {
         "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": r["reps"],
-        "warmup": 2, "ms_per_step": r["sec_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": warm, "ms_per_step": r["sec_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
         "config": {"workload": f"GLAD actor forward (FP32 eager, reference CPU path), B=256 sample per "
                                f"step of the B={args.batch} workload", "batch_per_step": 256},
