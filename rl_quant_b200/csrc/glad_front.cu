@@ -697,7 +697,7 @@ struct __align__(128) FusedSmem {
   uint64_t lg_bdesc[4];
   uint64_t pl_adesc[8];                // pooling GEMM [K-step]
   uint64_t pl_bdesc[8];
-  uint64_t bar1, bar2, bar3;           // conv1 / conv2 / logits and pooling (two issuing warps each)
+  uint64_t bar1, bar2, bar3;           // conv1 (2 issuers) / conv2 (warp 7) / logits and pooling (2 issuers)
   uint64_t bar_pe;                     // batched proprio embedding
   uint64_t bar_row;                    // bulk copy of the next observation row
   uint32_t tmem_base;
@@ -733,7 +733,7 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
   if (warp == 0) tmem_alloc(&s.tmem_base, kFusedTmemCols);
   if (tid == 0) {
     mbar_init(&s.bar1, 2);
-    mbar_init(&s.bar2, 2);
+    mbar_init(&s.bar2, 1);
     mbar_init(&s.bar3, 2);
     mbar_init(&s.bar_pe, 1);
     mbar_init(&s.bar_row, 1);
@@ -1183,6 +1183,71 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     }
   };
 
+  // conv1(e) accumulators -> z8 -> conv2's strip (and z8_out); warps 0-6 own rows
+  auto conv1_epi = [&](int64_t e) {
+    {
+      const int t = half;
+      const int m = t * 128 + 32 * quarter + lane;
+      if (t * 128 + 32 * quarter < 11 * 19) {
+        uint32_t r[16];
+        tmem_ld16(tmem_c1 + lane_base + t * 16, r);
+        tmem_ld_wait();
+        const int oh = m / 19, ow = m - oh * 19;
+        if (oh < kH2 && ow < kW2) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(&s.b1[4 * w4]);
+            const float4 qa4 = *reinterpret_cast<const float4*>(&s.qa[4 * w4]);
+            const float4 qc4 = *reinterpret_cast<const float4*>(&s.qc[4 * w4]);
+            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+            const float aa[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
+            const float cc[4] = {qc4.x, qc4.y, qc4.z, qc4.w};
+            uint32_t word = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int q = conv1_quant(__uint_as_float(r[4 * w4 + k]), bb[k], aa[k], cc[k]);
+              word |= ((uint32_t)(q & 0xFF)) << (8 * k);
+            }
+            pk[w4] = word;
+          }
+          const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
+          if (p.z8_out) reinterpret_cast<uint4*>(p.z8_out)[e * kTok + oh * kW2 + ow] = v;   // optional for the chain
+        }
+      }
+    }
+  };
+  // conv2 of the strip's environment: warp 7 (one elected lane) issues both tiles
+  auto issue_conv2 = [&]() {
+    if (warp == 7) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_i8(128, 64);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int pr = 0; pr < 5; ++pr)
+          mma_i8_warp(tmem + t * 64, s.c2_adesc[t * 5 + pr], s.c2_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
+      mma_commit_warp(&s.bar2);
+    }
+  };
+  // conv1(e) done -> strip (warps 0-6) -> conv2(e) issued by warp 7 once the strip is
+  // complete (named barrier 3: 224 arrivals + warp 7); warp 7 has no conv1 rows
+  auto stage_conv2 = [&](int64_t e) {
+    if (warp < 7) {
+      if (!mbar_wait_bounded(&s.bar1, ph1)) s.abort_flag = 1;
+      tc_fence_after();
+      conv1_epi(e);
+      tc_fence_before();
+      fence_async_smem();
+      named_bar_arrive(3, NT);
+    } else {
+      named_bar_sync(3, NT);
+      issue_conv2();
+    }
+    ph1 ^= 1;
+  };
+
   // ---- prologue: first environment through conv1 issue ---------------------------------
   // In the loop, warps 0-5 stage and convert observation rows (named barrier 1) while
   // warps 6 and 7 issue the conv MMAs; only warps 0-5 own cp.async groups there.
@@ -1228,64 +1293,14 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     if (pe_batch) pe_batched(pe_pre);
     else if (FULL) proprio_emb(0);
     if (dual) critic_emb(0);
+    stage_conv2(env);                   // conv2 of the first environment, ahead of the loop
   }
 
   int b = 0;
   for (; env < p.B; env += gridDim.x, b ^= 1) {
     const int64_t nxt = env + gridDim.x;
-    // ---- conv1(e) done -> z8 -> strip, issue conv2(e) ---------------------------------------
-    if (!mbar_wait_bounded(&s.bar1, ph1)) s.abort_flag = 1;
-    ph1 ^= 1;
-    tc_fence_after();
-    __syncthreads();
-    if (s.abort_flag) break;
-    {
-      const int t = half;
-      const int m = t * 128 + 32 * quarter + lane;
-      if (t * 128 + 32 * quarter < 11 * 19) {
-        uint32_t r[16];
-        tmem_ld16(tmem_c1 + lane_base + t * 16, r);
-        tmem_ld_wait();
-        const int oh = m / 19, ow = m - oh * 19;
-        if (oh < kH2 && ow < kW2) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int w4 = 0; w4 < 4; ++w4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(&s.b1[4 * w4]);
-            const float4 qa4 = *reinterpret_cast<const float4*>(&s.qa[4 * w4]);
-            const float4 qc4 = *reinterpret_cast<const float4*>(&s.qc[4 * w4]);
-            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
-            const float aa[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
-            const float cc[4] = {qc4.x, qc4.y, qc4.z, qc4.w};
-            uint32_t word = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int q = conv1_quant(__uint_as_float(r[4 * w4 + k]), bb[k], aa[k], cc[k]);
-              word |= ((uint32_t)(q & 0xFF)) << (8 * k);
-            }
-            pk[w4] = word;
-          }
-          const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
-          if (p.z8_out) reinterpret_cast<uint4*>(p.z8_out)[env * kTok + oh * kW2 + ow] = v;   // optional for the chain
-        }
-      }
-    }
-    tc_fence_before();
-    fence_async_smem();
-    __syncthreads();
-    if (warp >= kIssuerWarp0) {
-      const int t = warp - kIssuerWarp0;
-      tc_fence_after();
-      constexpr uint32_t idesc = idesc_i8(128, 64);
-#pragma unroll
-      for (int pr = 0; pr < 5; ++pr)
-        mma_i8_warp(tmem + t * 64, s.c2_adesc[t * 5 + pr], s.c2_bdesc[pr], idesc, pr > 0 ? 1u : 0u);
-      mma_commit_warp(&s.bar2);
-    }
-
-    // ---- next environment: warps 0-5 convert and prefetch while warps 6-7 issue; then
-    //      warps 6-7 issue its conv1 (warps 0-3 compute an fp16 proprio embedding) ---------
+    // ---- next environment: warps 0-5 convert and prefetch it, then warps 6-7 issue its conv1
+    //      (warps 0-3 compute an fp16 proprio embedding); conv2(e) is in flight ----------------
     if (nxt < p.B) {
       if (warp >= kIssuerWarp0) {
         named_bar_sync(2, NT);            // planes of e+1 written by warps 0-5
@@ -1398,9 +1413,10 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
       }
     }
     if constexpr (!FULL) {
-      // chain only: the next iteration's barriers order these TMEM reads before the next MMA
+      // chain only: conv1(e+1) -> strip -> conv2(e+1) while the next row is converted
       tc_fence_before();
       __syncthreads();
+      if (nxt < p.B) stage_conv2(nxt);
       continue;
     }
     tc_fence_before();
@@ -1417,83 +1433,87 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         mma_f16_warp(tmem + 160 + 16 * t, s.lg_adesc[t][kk], s.lg_bdesc[kk], idesc, kk > 0 ? 1u : 0u);
       mma_commit_warp(&s.bar3);
     }
-    if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
-    ph3 ^= 1;
-    tc_fence_after();
-    __syncthreads();
-    if (s.abort_flag) break;
-    // logits (qrt/encoder_opt.py:69-73) and the softmax over the 187 tokens (:75)
-    float my_logit;
-    int my_tok = -1;
-    {
-      const int t = half, i = 32 * quarter + lane;
-      const int m = t * 128 + i;
-      const int oh = m / kStripCols, ow = m - oh * kStripCols;
-      uint32_t l0 = 0, l1 = 0;
-      if (t * 128 + 32 * quarter < 11 * kStripCols) {
-        tmem_ld2(tmem + lane_base + 160 + 16 * t, l0, l1);
-        tmem_ld_wait();
-      }
-      float g = -INFINITY;
-      if (oh < kH2 && ow < kW2) {
-        my_tok = oh * kW2 + ow;
-        g = fp16r(__fadd_rn(fp16r(__uint_as_float(l0)), gb));
-        p.score_local[env * kTok + my_tok] = __float2half_rn(__uint_as_float(l1));
-      }
-      my_logit = g;
-    }
-    tc_fence_before();
-    float mx = warp_max(my_logit);
-    if (lane == 0) s.wmax[warp] = mx;
-    __syncthreads();
-    mx = s.wmax[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s.wmax[w]);
-    const float ex = my_tok < 0 ? 0.0f : expf(my_logit - mx);
-    float sm = warp_sum(ex);
-    if (lane == 0) s.wsum[warp] = sm;
-    __syncthreads();
-    sm = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) sm += s.wsum[w];
-    {
-      const __half wh = __float2half_rn(__fdiv_rn(ex, sm));
-      const int i = 32 * quarter + lane;
-      // pooling B: column n = tile, K = row within the tile
-      reinterpret_cast<__half*>(s.bpool + (i >> 3) * 256 + half * 16)[i & 7] =
-          my_tok < 0 ? __float2half(0.0f) : wh;
-      if (my_tok >= 0 && p.gc_w_out) p.gc_w_out[env * kTok + my_tok] = wh;
-    }
-    fence_async_smem();
-    __syncthreads();
-    // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77): row
-    // tile*64 + c of the pooling GEMM, column `tile`; warp h sums the rows 64h..64h+63 of
-    // each tile into its own accumulator (TMEM columns 192 + 16h)
-    if (warp < 2) {
-      const int h = warp;
+    // while the logits GEMM runs: conv1(e+1) -> strip, and warp 7 issues conv2(e+1); warp 7
+    // owns no valid token rows, so the softmax and pooling below run on warps 0-6 (named
+    // barrier 4) while it issues, and it rejoins at the CTA barrier before the outputs
+    if (nxt < p.B) stage_conv2(nxt);
+    if (warp < 7) {
+      if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
       tc_fence_after();
-      constexpr uint32_t idesc = idesc_f16_amajor_m(128, 16);
+      named_bar_sync(4, 7 * 32);
+      // logits (qrt/encoder_opt.py:69-73) and the softmax over the 187 tokens (:75)
+      float my_logit;
+      int my_tok = -1;
+      {
+        const int t = half, i = 32 * quarter + lane;
+        const int m = t * 128 + i;
+        const int oh = m / kStripCols, ow = m - oh * kStripCols;
+        uint32_t l0 = 0, l1 = 0;
+        if (t * 128 + 32 * quarter < 11 * kStripCols) {
+          tmem_ld2(tmem + lane_base + 160 + 16 * t, l0, l1);
+          tmem_ld_wait();
+        }
+        float g = -INFINITY;
+        if (oh < kH2 && ow < kW2) {
+          my_tok = oh * kW2 + ow;
+          g = fp16r(__fadd_rn(fp16r(__uint_as_float(l0)), gb));
+          p.score_local[env * kTok + my_tok] = __float2half_rn(__uint_as_float(l1));
+        }
+        my_logit = g;
+      }
+      tc_fence_before();
+      float mx = warp_max(my_logit);
+      if (lane == 0) s.wmax[warp] = mx;
+      named_bar_sync(4, 7 * 32);
+      mx = s.wmax[0];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_warp(tmem + 192 + 16 * h, s.pl_adesc[4 * h + kk], s.pl_bdesc[4 * h + kk], idesc,
-                     kk > 0 ? 1u : 0u);
-      mma_commit_warp(&s.bar3);
-    }
-    if (!mbar_wait_bounded(&s.bar3, ph3)) s.abort_flag = 1;
-    ph3 ^= 1;
-    tc_fence_after();
-    __syncthreads();
+      for (int w = 1; w < 7; ++w) mx = fmaxf(mx, s.wmax[w]);
+      const float ex = my_tok < 0 ? 0.0f : expf(my_logit - mx);
+      float sm = warp_sum(ex);
+      if (lane == 0) s.wsum[warp] = sm;
+      named_bar_sync(4, 7 * 32);
+      sm = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 7; ++w) sm += s.wsum[w];
+      {
+        const __half wh = __float2half_rn(__fdiv_rn(ex, sm));
+        const int i = 32 * quarter + lane;
+        // pooling B: column n = tile, K = row within the tile
+        reinterpret_cast<__half*>(s.bpool + (i >> 3) * 256 + half * 16)[i & 7] =
+            my_tok < 0 ? __float2half(0.0f) : wh;
+        if (my_tok >= 0 && p.gc_w_out) p.gc_w_out[env * kTok + my_tok] = wh;
+      }
+      fence_async_smem();
+      named_bar_sync(4, 7 * 32);
+      // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77): row
+      // tile*64 + c of the pooling GEMM, column `tile`; warp h sums the rows 64h..64h+63 of
+      // each tile into its own accumulator (TMEM columns 192 + 16h)
+      if (warp < 2) {
+        const int h = warp;
+        tc_fence_after();
+        constexpr uint32_t idesc = idesc_f16_amajor_m(128, 16);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_warp(tmem + 192 + 16 * h, s.pl_adesc[4 * h + kk], s.pl_bdesc[4 * h + kk], idesc,
+                       kk > 0 ? 1u : 0u);
+        mma_commit_warp(&s.bar3);
+      }
+      if (!mbar_wait_bounded(&s.bar3, ph3 ^ 1)) s.abort_flag = 1;
+      tc_fence_after();
+      named_bar_sync(4, 7 * 32);
+      if (warp < 4) {
+        uint32_t d0, d1, e0, e1;
+        tmem_ld2(tmem + lane_base + 192, d0, d1);
+        tmem_ld2(tmem + lane_base + 208, e0, e1);
+        tmem_ld_wait();
+        const int mrow = 32 * warp + lane;
+        s.poolv[mrow] = __fadd_rn(__uint_as_float(mrow < 64 ? d0 : d1), __uint_as_float(mrow < 64 ? e0 : e1));
+      }
+      tc_fence_before();
+    }                                   // softmax group
+    // bar3 completed two phases (logits, pooling) this iteration: ph3 is unchanged
+    __syncthreads();                    // warp 7 rejoins
     if (s.abort_flag) break;
-    if (warp < 4) {
-      uint32_t d0, d1, e0, e1;
-      tmem_ld2(tmem + lane_base + 192, d0, d1);
-      tmem_ld2(tmem + lane_base + 208, e0, e1);
-      tmem_ld_wait();
-      const int mrow = 32 * warp + lane;
-      s.poolv[mrow] = __fadd_rn(__uint_as_float(mrow < 64 ? d0 : d1), __uint_as_float(mrow < 64 ? e0 : e1));
-    }
-    tc_fence_before();
-    __syncthreads();
     if (tid < kD) {
       const float g = s.poolv[tid] + s.poolv[64 + tid];
       const __half gh = __float2half_rn(g);
