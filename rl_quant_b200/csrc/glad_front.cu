@@ -659,7 +659,7 @@ constexpr int kFusedTmemCols = 256;
 // Warps 6 and 7 issue the conv MMAs (tile t by warp 6 + t, each from one elected lane):
 // a warp's MMA issue takes ~140 cycles, so two issuers halve the chain.
 constexpr int kIssuerWarp0 = 6;
-constexpr int kConverters = 6 * 32;      // warps 0-5 stage and convert observation rows
+constexpr int kConverters = 6 * 32;      // warps 0-5 stage observation rows (all warps convert them)
 
 struct __align__(128) FusedSmem {
   uint8_t planes[1][kPlanesBytes];     // conv1(e) completes before the conversion of e+1 writes it
@@ -1302,11 +1302,9 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
     // ---- next environment: warps 0-5 convert and prefetch it, then warps 6-7 issue its conv1
     //      (warps 0-3 compute an fp16 proprio embedding); conv2(e) is in flight ----------------
     if (nxt < p.B) {
-      if (warp >= kIssuerWarp0) {
-        named_bar_sync(2, NT);            // planes of e+1 written by warps 0-5
-        issue_conv1(b ^ 1);
-        if (dual) critic_emb(b ^ 1);
-      } else {
+      // all eight warps convert the staged row of e+1; then warps 6-7 issue its conv1 while
+      // warps 0-5 start the copy of row e+2
+      if (warp < kIssuerWarp0) {
         cp_async_wait_all();
         if (mbar_wait_bounded(&s.bar_row, ph_row)) {   // the bulk body of row e+1
           ph_row ^= 1;
@@ -1314,12 +1312,16 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
         } else {
           s.abort_flag = 1;                 // the teardown waits for it once more
         }
-        named_bar_sync(1, kConverters);   // the staged row of e+1 is complete
-        convert(nxt, b ^ 1, kConverters);
-        fence_async_smem();
-        tc_fence_before();
-        named_bar_arrive(2, NT);          // planes ready for the issuer
-        named_bar_sync(1, kConverters);   // every converter is done with the stage buffer
+      }
+      __syncthreads();                    // the staged row of e+1 is complete
+      convert(nxt, b ^ 1, NT);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();                    // planes ready; the stage buffer is free
+      if (warp >= kIssuerWarp0) {
+        issue_conv1(b ^ 1);
+        if (dual) critic_emb(b ^ 1);
+      } else {
         const int64_t nn = nxt + gridDim.x;
         if (nn < p.B) {
           row_issue_bulk(row_stage(p.in, nn, p.ld, esz, row_elems, s.stage), &s.bar_row, tid);
