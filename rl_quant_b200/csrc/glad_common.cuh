@@ -69,6 +69,32 @@ struct ActQuant {
     r = fminf(fmaxf(r, -128.0f), 127.0f);
     return (int)r;
   }
+  // quant() as the low byte of an fp32 bit pattern: the clamped value plus 1.5*2^23
+  // rounds to the nearest even integer in the mantissa (equal to rintf for |t| < 2^22,
+  // and clamping before rounding equals clamping after, the bounds being integers), so
+  // no float->int conversion is needed. The dynamic LET path tests the fast quotient on
+  // the clamped value with the wider bound |t - rint(t)| >= 0.4999, which contains every
+  // case quant() re-evaluates (|t| <= 128 there, 128*4.8e-7 < 1e-4); a clamped value has
+  // no fraction, and both give the clamp bound whenever the fast quotient is outside
+  // [-128, 127].
+  __device__ __forceinline__ uint32_t qbits(float x, float alpha, float beta) const {
+    constexpr float kMagic = 12582912.0f;
+    float t;
+    if (let) {
+      const float z = __fadd_rn(__fmul_rn(x, alpha), beta);
+      if (dyn) {
+        t = fminf(fmaxf(__fmul_rn(z, rcp), -128.0f), 127.0f);
+        const float u = __fadd_rn(t, kMagic);
+        if (fabsf(__fsub_rn(t, __fsub_rn(u, kMagic))) < 0.4999f) return __float_as_uint(u);
+        t = fminf(fmaxf(rintf(__fdiv_rn(z, s)), -128.0f), 127.0f);
+      } else {
+        t = fminf(fmaxf(__fmul_rn(z, inv), -128.0f), 127.0f);
+      }
+    } else {
+      t = fminf(fmaxf(fp16r(dyn ? __fdiv_rn(x, s) : __fmul_rn(x, inv)), -128.0f), 127.0f);
+    }
+    return __float_as_uint(__fadd_rn(t, kMagic));
+  }
   // |z| of one input element (what the dynamic absmax reduces).
   __device__ __forceinline__ float absz(float x, float alpha, float beta) const {
     return let ? fabsf(__fadd_rn(__fmul_rn(x, alpha), beta)) : fabsf(x);

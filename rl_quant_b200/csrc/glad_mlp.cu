@@ -74,13 +74,15 @@ struct MlpParams {
   float* slots;            // absmax slots 2..5, status, barrier counters
 };
 
-// Rows [n0, n0+rows) of a row-major int8 [*, K] weight -> [K/16][rows][16 B].
-__device__ __forceinline__ void mlp_load_w(uint8_t* dst, const int8_t* w8, int K, int n0, int rows,
-                                           int tid) {
-  const int n16 = rows * (K / 16);
+// Rows [n0, n0+ROWS) of a row-major int8 [*, K] weight -> [K/16][ROWS][16 B] (compile-time
+// shapes: the index split is a shift).
+template <int K, int ROWS>
+__device__ __forceinline__ void mlp_load_w(uint8_t* dst, const int8_t* w8, int n0, int tid) {
+  constexpr int n16 = ROWS * (K / 16);
+#pragma unroll 1
   for (int idx = tid; idx < n16; idx += kMlpThreads) {
-    const int c = idx / rows, n = idx - c * rows;
-    cp_async16(dst + c * rows * 16 + n * 16, w8 + (int64_t)(n0 + n) * K + c * 16);
+    const int c = idx / ROWS, n = idx % ROWS;
+    cp_async16(dst + idx * 16, w8 + (int64_t)(n0 + n) * K + c * 16);
   }
 }
 
@@ -95,10 +97,10 @@ __device__ __forceinline__ uint4 mlp_quant16(const uint4 v0, const uint4 v1, con
     const float4 b4 = *reinterpret_cast<const float4*>(b + j);
     const float2 x01 = __half22float2(*reinterpret_cast<const __half2*>(&h[j >> 1]));
     const float2 x23 = __half22float2(*reinterpret_cast<const __half2*>(&h[(j >> 1) + 1]));
-    const int q0 = aq.quant(x01.x, a4.x, b4.x), q1 = aq.quant(x01.y, a4.y, b4.y);
-    const int q2 = aq.quant(x23.x, a4.z, b4.z), q3 = aq.quant(x23.y, a4.w, b4.w);
-    w[j >> 2] = (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
-                ((uint32_t)(q3 & 0xFF) << 24);
+    const uint32_t q0 = aq.qbits(x01.x, a4.x, b4.x), q1 = aq.qbits(x01.y, a4.y, b4.y);
+    const uint32_t q2 = aq.qbits(x23.x, a4.z, b4.z), q3 = aq.qbits(x23.y, a4.w, b4.w);
+    // low bytes of q0..q3 -> one word (byte permutes instead of masks and shifts)
+    w[j >> 2] = __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
@@ -130,16 +132,40 @@ __device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mb
 // 16 accumulator columns at `taddr`: the sum of the kMlpChains partial chains (int32,
 // exact), chain c at column offset c * nj.
 __device__ __forceinline__ void mlp_ld_acc(uint32_t taddr, int nj, uint32_t (&r)[16]) {
+  static_assert(kMlpChains == 4, "two loads per wait");
+  uint32_t t[16], u[16];
   tmem_ld16(taddr, r);
-#pragma unroll 1
-  for (int c = 1; c < kMlpChains; ++c) {
-    uint32_t t[16];
-    tmem_ld16(taddr + (uint32_t)(c * nj), t);
-    tmem_ld_wait();
-#pragma unroll
-    for (int j = 0; j < 16; ++j) r[j] = (uint32_t)((int32_t)r[j] + (int32_t)t[j]);
-  }
+  tmem_ld16(taddr + (uint32_t)nj, t);
   tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) r[j] += t[j];
+  tmem_ld16(taddr + (uint32_t)(2 * nj), t);
+  tmem_ld16(taddr + (uint32_t)(3 * nj), u);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) r[j] += t[j] + u[j];
+}
+
+// 16 int32 accumulators -> fp32, exactly: through the mantissa of 1.5*2^23 (two ALU
+// operations) when every |acc| < 2^22, which the OR of the offset values shows, else
+// by the conversion instruction.
+__device__ __forceinline__ void mlp_acc_f32(const uint32_t (&r)[16], float (&a)[16]) {
+  uint32_t span = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) span |= r[j] + (1u << 22);
+  if (span < (1u << 23)) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] = i2f_small((int32_t)r[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] = (float)(int32_t)r[j];
+  }
+}
+
+// ELU of two fp16 values (each computed in fp32 and rounded to fp16, as elu16).
+__device__ __forceinline__ __half2 elu16x2(__half2 h) {
+  const float2 x = __half22float2(h);
+  return __floats2half2_rn(x.x > 0.0f ? x.x : expm1f(x.x), x.y > 0.0f ? x.y : expm1f(x.y));
 }
 
 // Grid-wide barrier on counter `ctr` (one arrival per CTA), folded with the batch
@@ -231,12 +257,23 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   }
   cp_async_commit();
   // weight slices of all four layers, in flight while the input is quantised
-  mlp_load_w(sm + kOffW0, p.L[0].w8, 224, (int)rank * 128, 128, tid);
-  mlp_load_w(sm + kOffW1, p.L[1].w8, 512, (int)rank * 64, 64, tid);
-  mlp_load_w(sm + kOffW2, p.L[2].w8, 256, (int)rank * 32, 32, tid);
-  if (rank == 0) mlp_load_w(sm + kOffW3, p.L[3].w8, 128, 0, 32, tid);
+  mlp_load_w<224, 128>(sm + kOffW0, p.L[0].w8, (int)rank * 128, tid);
+  mlp_load_w<512, 64>(sm + kOffW1, p.L[1].w8, (int)rank * 64, tid);
+  mlp_load_w<256, 32>(sm + kOffW2, p.L[2].w8, (int)rank * 32, tid);
+  if (rank == 0) mlp_load_w<128, 32>(sm + kOffW3, p.L[3].w8, 0, tid);
   cp_async_commit();
   grid_dep_wait();                      // encoded rows and slot 2 of the preceding kernel
+  // this thread's item of the layer-0 input (rank j quantises tile rows [32j, 32j+32), 14
+  // chunks of 16 columns each), loaded before the waits below so that its latency overlaps them
+  static_assert(32 * 14 <= kMlpThreads, "one input item per thread");
+  const int in_rr = 32 * (int)rank + tid / 14, in_kc = tid % 14;
+  const bool in_ok = tid < 32 * 14 && m0 + in_rr < p.M;
+  uint4 in0 = make_uint4(0, 0, 0, 0), in1 = in0;
+  if (in_ok) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (m0 + in_rr) * p.ldx + in_kc * 16);
+    in0 = src[0];
+    in1 = src[1];
+  }
   ActQuant aq = make_act_quant(p.L[0], p.act_mode, p.slots, 2);   // input of the running layer
   cp_async_wait_group<1>();             // constants landed; the weights may still be in flight
   __syncthreads();
@@ -247,20 +284,12 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
 
   // ---- layer 0 input: rank j quantises tile rows [32j, 32j+32) for the whole cluster ------
-  {
-    const uint32_t abase = smem_u32(sm + kOffA0);
-    for (int it = tid; it < 32 * 14; it += kMlpThreads) {
-      const int rr = 32 * (int)rank + it / 14, kc = it % 14;
-      const int64_t mm = m0 + rr;
-      uint4 q = make_uint4(0, 0, 0, 0);
-      if (mm < p.M) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.x + mm * p.ldx + kc * 16);
-        q = mlp_quant16(src[0], src[1], aq, &F[kFInA + kc * 16], &F[kFInB + kc * 16]);
-      }
-      const uint32_t off = abase + kc * 2048 + rr * 16;
+  if (tid < 32 * 14) {
+    uint4 q = make_uint4(0, 0, 0, 0);
+    if (in_ok) q = mlp_quant16(in0, in1, aq, &F[kFInA + in_kc * 16], &F[kFInB + in_kc * 16]);
+    const uint32_t off = smem_u32(sm + kOffA0) + in_kc * 2048 + in_rr * 16;
 #pragma unroll
-      for (int r = 0; r < kMlpCluster; ++r) st_cluster_v4(mapa_shared(off, r), q);
-    }
+    for (int r = 0; r < kMlpCluster; ++r) st_cluster_v4(mapa_shared(off, r), q);
   }
   cp_async_wait_all();
   fence_async_smem();
@@ -287,17 +316,19 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
       for (int ch = part; ch < nch; ch += 4) {
         uint32_t r[16];
         mlp_ld_acc(tmem + lane_base + ch * 16, NJ, r);
+        float a[16];
+        mlp_acc_f32(r, a);
         uint32_t h[8];
 #pragma unroll
         for (int j = 0; j < 16; j += 4) {
           const int c = CB + ch * 16 + j;
           const float4 sc = *reinterpret_cast<const float4*>(&F[kFSc + c]);
           const float4 bp = *reinterpret_cast<const float4*>(&F[kFBp + c]);
-          const __half y0 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j], sc.x, bp.x)));
-          const __half y1 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + 1], sc.y, bp.y)));
-          const __half y2 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + 2], sc.z, bp.z)));
-          const __half y3 = elu16(__float2half_rn(qlinear_out32((int32_t)r[j + 3], sc.w, bp.w)));
-          const __half2 p01 = __halves2half2(y0, y1), p23 = __halves2half2(y2, y3);
+          // y = fp16(acc*scale + b') (qlinear_out32), then ELU in fp32 rounded to fp16
+          const __half2 p01 = elu16x2(__floats2half2_rn(__fadd_rn(__fmul_rn(a[j], sc.x), bp.x),
+                                                        __fadd_rn(__fmul_rn(a[j + 1], sc.y), bp.y)));
+          const __half2 p23 = elu16x2(__floats2half2_rn(__fadd_rn(__fmul_rn(a[j + 2], sc.z), bp.z),
+                                                        __fadd_rn(__fmul_rn(a[j + 3], sc.w), bp.w)));
           h[j >> 1] = *reinterpret_cast<const uint32_t*>(&p01);
           h[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&p23);
           if (want_max) {
@@ -356,18 +387,30 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     if (tid < 32) F[kFSc + CB + tid] = dyn ? __fmul_rn(F[kFSw + CB + tid], aq.s) : F[kFSw + CB + tid];
     mlp_mma(sm, tmem, mbar, phase, abort_flag, mma_timeout, mlp_abuf(3), mlp_wbuf(3), 128,
             idesc_i8(128, 32), 32);
-    if (!*abort_flag && part < 2) {
+    // staged in layer 2's A operand (dead: its MMA completed, no remote stores follow)
+    // and written row-contiguous by all threads
+    float* stage = reinterpret_cast<float*>(sm + kOffA0);   // [128 rows][33]
+    const bool ok = !*abort_flag;                            // uniform after mlp_mma's barrier
+    if (ok && part < 2) {
       const int col0 = part * 16;
       uint32_t r[16];
       mlp_ld_acc(tmem + lane_base + col0, 32, r);
-      if (row_ok) {
-        float* dst = p.mean + m * p.ldm;
+      float a[16];
+      mlp_acc_f32(r, a);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = col0 + j;
-          if (n < kActions)
-            dst[n] = __half2float(qlinear_out((int32_t)r[j], F[kFSc + CB + n], F[kFBp + CB + n]));
-        }
+      for (int j = 0; j < 16; ++j) {
+        const int n = col0 + j;
+        if (n < kActions)
+          stage[row * 33 + n] =
+              __half2float(__float2half_rn(__fadd_rn(__fmul_rn(a[j], F[kFSc + CB + n]), F[kFBp + CB + n])));
+      }
+    }
+    __syncthreads();
+    if (ok) {
+      const int rows = (int)(p.M - m0 < 128 ? p.M - m0 : 128);
+      for (int i = tid; i < rows * kActions; i += kMlpThreads) {
+        const int rr = i / kActions, c = i - rr * kActions;
+        p.mean[(m0 + rr) * p.ldm + c] = stage[rr * 33 + c];
       }
     }
   }
