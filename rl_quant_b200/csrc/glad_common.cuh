@@ -140,12 +140,15 @@ __device__ __forceinline__ __half elu16(__half h) {
   return __float2half_rn(x > 0.0f ? x : expm1f(x));
 }
 
-// conv2 epilogue (qrt/qconv.py:159-161): ((acc*dq + b) relu) * a2 + c2 -> fp16.
-__device__ __forceinline__ __half conv2_out(int32_t acc, float dq, float b, float a2, float c2) {
-  float y = __fadd_rn(__fmul_rn(i2f_small(acc), dq), b);
-  y = fmaxf(y, 0.0f);
-  return __float2half_rn(__fadd_rn(__fmul_rn(y, a2), c2));
+// conv2 epilogue (qrt/qconv.py:159-161): ((acc*dq + b) relu) * a2 + c2 with fused
+// multiply-adds, as the compiled Triton kernel contracts them; the fp16 rounding is the
+// caller's (paired conversions).
+__device__ __forceinline__ float conv2_val(int32_t acc, float dq, float b, float a2, float c2) {
+  return fmaf(fmaxf(fmaf(i2f_small(acc), dq, b), 0.0f), a2, c2);
 }
+
+// fp16 rounding of two fp32 values, back in fp32 (one paired conversion).
+__device__ __forceinline__ float2 fp16r2(float x, float y) { return __half22float2(__floats2half2_rn(x, y)); }
 
 // conv1 epilogue (qrt/qconv.py:96-101): relu(acc+b)*qa + qc, round half away
 // from zero, clamp to int8.

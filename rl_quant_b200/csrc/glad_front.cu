@@ -156,11 +156,6 @@ __device__ __forceinline__ float row_elem(const RowStage& r, int i) {
   return __half2float(*reinterpret_cast<const __half*>(p));
 }
 
-// conv2 epilogue with fused multiply-adds: ((acc*dq + b) relu) * a2 + c2.
-__device__ __forceinline__ float conv2_val(int32_t acc, float dq, float b, float a2, float c2) {
-  return fmaf(fmaxf(fmaf(i2f_small(acc), dq, b), 0.0f), a2, c2);
-}
-
 // 32 values -> one warp sum per lane: lane L ends with the sum of channel L.
 __device__ __forceinline__ float warp_reduce32(float (&v)[32], int lane) {
 #pragma unroll

@@ -199,31 +199,16 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         acc0 = __dp4a(qw, wv.x, acc0);
         acc1 = __dp4a(qw, wv.y, acc1);
       }
-      const float q0 = __half2float(qlinear_out(acc0, s.qp_scale[2 * lane], s.qp_bp[2 * lane]));
-      const float q1 = __half2float(qlinear_out(acc1, s.qp_scale[2 * lane + 1], s.qp_bp[2 * lane + 1]));
+      // y = fp16(acc*scale + b') (qlinear_out); |acc| <= 128*128*128 < 2^22
+      const float2 q01 = fp16r2(__fadd_rn(__fmul_rn(i2f_small(acc0), s.qp_scale[2 * lane]), s.qp_bp[2 * lane]),
+                                __fadd_rn(__fmul_rn(i2f_small(acc1), s.qp_scale[2 * lane + 1]), s.qp_bp[2 * lane + 1]));
+      const float q0 = q01.x, q1 = q01.y;
       s.qv[warp][2 * lane] = q0;
       s.qv[warp][2 * lane + 1] = q1;
       // ---- 2. score_query = q @ w_s[:, 64:]^T + b_s (fp16 matmul then add) ----------------
       const float sqp = warp_sum(fmaf(q1, s.wsq[2 * lane + 1], q0 * s.wsq[2 * lane]));
       const float sq = fp16r(__fadd_rn(fp16r(sqp), sb));
       __syncwarp();
-      // MHA query projection: q_mha = fp16(fp16(query @ Wq^T) + b_q); lane -> n = 2*lane, 2*lane+1
-      {
-        float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-        for (int c2 = 0; c2 < 32; ++c2) {
-          const uint2 wv = s.wqT[c2 * 32 + lane];
-          const float x0 = s.qv[warp][2 * c2], x1 = s.qv[warp][2 * c2 + 1];
-          const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-          const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
-          a0 = fmaf(x0, w0.x, a0);
-          a0 = fmaf(x1, w0.y, a0);
-          a1 = fmaf(x0, w1.x, a1);
-          a1 = fmaf(x1, w1.y, a1);
-        }
-        s.qm[warp][2 * lane] = fp16r(__fadd_rn(fp16r(a0), s.bin[2 * lane]));
-        s.qm[warp][2 * lane + 1] = fp16r(__fadd_rn(fp16r(a1), s.bin[2 * lane + 1]));
-      }
       // ---- 3. top-32 over 187 logits, value desc / index asc ------------------------------
       uint32_t key[6];
 #pragma unroll
@@ -301,6 +286,26 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         else
           *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
       }
+      // MHA query projection: q_mha = fp16(fp16(query @ Wq^T) + b_q); lane -> n = 2*lane, 2*lane+1
+      // (after the gather is issued: the GEMV runs while the z8 rows arrive)
+      {
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+        for (int c2 = 0; c2 < 32; ++c2) {
+          const uint2 wv = s.wqT[c2 * 32 + lane];
+          const float x0 = s.qv[warp][2 * c2], x1 = s.qv[warp][2 * c2 + 1];
+          const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+          const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+          a0 = fmaf(x0, w0.x, a0);
+          a0 = fmaf(x1, w0.y, a0);
+          a1 = fmaf(x0, w1.x, a1);
+          a1 = fmaf(x1, w1.y, a1);
+        }
+        const float2 a01 = fp16r2(a0, a1);
+        const float2 qm = fp16r2(__fadd_rn(a01.x, s.bin[2 * lane]), __fadd_rn(a01.y, s.bin[2 * lane + 1]));
+        s.qm[warp][2 * lane] = qm.x;
+        s.qm[warp][2 * lane + 1] = qm.y;
+      }
     } else {
 #pragma unroll
       for (int q = 0; q < 9; ++q)
@@ -348,10 +353,10 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
         const float4 a24 = *reinterpret_cast<const float4*>(&s.a2c[c]);
         const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
-        const __half2 h01 = __halves2half2(conv2_out((int32_t)rr[j], dq4.x, b24.x, a24.x, c24.x),
-                                           conv2_out((int32_t)rr[j + 1], dq4.y, b24.y, a24.y, c24.y));
-        const __half2 h23 = __halves2half2(conv2_out((int32_t)rr[j + 2], dq4.z, b24.z, a24.z, c24.z),
-                                           conv2_out((int32_t)rr[j + 3], dq4.w, b24.w, a24.w, c24.w));
+        const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)rr[j], dq4.x, b24.x, a24.x, c24.x),
+                                              conv2_val((int32_t)rr[j + 1], dq4.y, b24.y, a24.y, c24.y));
+        const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)rr[j + 2], dq4.z, b24.z, a24.z, c24.z),
+                                              conv2_val((int32_t)rr[j + 3], dq4.w, b24.w, a24.w, c24.w));
         hw[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
         hw[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
       }
@@ -393,16 +398,26 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       uint32_t rr[16];
       tmem_ld16(tcol + cb * 16, rr);
       tmem_ld_wait();
+      float dd[4];
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {
         float d = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < 4; e += 2) {
           const int c = 16 * cb + 4 * hh + e;
-          const float kv = fp16r(__fadd_rn(fp16r(__uint_as_float(rr[4 * hh + e])), s.bin[64 + c]));
-          d = fmaf(s.qm[warp][c], kv, d);
+          const float2 k0 = fp16r2(__uint_as_float(rr[4 * hh + e]), __uint_as_float(rr[4 * hh + e + 1]));
+          const float2 kv = fp16r2(__fadd_rn(k0.x, s.bin[64 + c]), __fadd_rn(k0.y, s.bin[64 + c + 1]));
+          d = fmaf(s.qm[warp][c], kv.x, d);
+          d = fmaf(s.qm[warp][c + 1], kv.y, d);
         }
-        sc[4 * cb + hh] = fp16r(__fmul_rn(fp16r(d), 0.5f));
+        dd[hh] = d;
+      }
+#pragma unroll
+      for (int hh = 0; hh < 4; hh += 2) {
+        const float2 d01 = fp16r2(dd[hh], dd[hh + 1]);
+        const float2 s01 = fp16r2(__fmul_rn(d01.x, 0.5f), __fmul_rn(d01.y, 0.5f));
+        sc[4 * cb + hh] = s01.x;
+        sc[4 * cb + hh + 1] = s01.y;
       }
     }
     // softmax over the 32 tokens of every head: the 16 heads' butterflies interleaved
@@ -424,10 +439,12 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       for (int h = 0; h < kHeads; ++h) red[h] += __shfl_xor_sync(0xffffffffu, red[h], o);
     float asum = 0.0f;
 #pragma unroll
-    for (int h = 0; h < kHeads; ++h) {
-      const float a = fp16r(__fdiv_rn(sc[h], red[h]));
-      asum += a;
-      sc[h] = a;
+    for (int h = 0; h < kHeads; h += 2) {
+      const float2 a = fp16r2(__fdiv_rn(sc[h], red[h]), __fdiv_rn(sc[h + 1], red[h + 1]));
+      asum += a.x;
+      asum += a.y;
+      sc[h] = a.x;
+      sc[h + 1] = a.y;
     }
     if (have && p.attn_w_out) p.attn_w_out[env * kTopK + lane] = __float2half_rn(asum / 16.0f);
 #pragma unroll
@@ -437,9 +454,12 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       tmem_ld_wait();
       float v[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 16; j += 2) {
         const int c = 16 * cb + j;
-        v[j] = sc[4 * cb + (j >> 2)] * fp16r(__fadd_rn(fp16r(__uint_as_float(rr[j])), s.bin[128 + c]));
+        const float2 v0 = fp16r2(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]));
+        const float2 vb = fp16r2(__fadd_rn(v0.x, s.bin[128 + c]), __fadd_rn(v0.y, s.bin[128 + c + 1]));
+        v[j] = sc[4 * cb + (j >> 2)] * vb.x;
+        v[j + 1] = sc[4 * cb + (j >> 2)] * vb.y;
       }
       const float o = warp_reduce16(v, lane);    // lanes L, L^16: channel 16*cb + (L & 15)
       if (lane < 16) s.om[warp][16 * cb + lane] = fp16r(o);
@@ -460,8 +480,9 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         a1 = fmaf(x0, w1.x, a1);
         a1 = fmaf(x1, w1.y, a1);
       }
-      const float f0 = fp16r(__fadd_rn(fp16r(a0), s.bout[2 * lane]));
-      const float f1 = fp16r(__fadd_rn(fp16r(a1), s.bout[2 * lane + 1]));
+      const float2 a01 = fp16r2(a0, a1);
+      const float2 f01 = fp16r2(__fadd_rn(a01.x, s.bout[2 * lane]), __fadd_rn(a01.y, s.bout[2 * lane + 1]));
+      const float f0 = f01.x, f1 = f01.y;
       reinterpret_cast<__half2*>(p.enc + env * p.ld_enc)[lane] = __floats2half2_rn(f0, f1);
       if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
         // |alpha*encoded + beta| for actor.0's dynamic s_z
