@@ -86,22 +86,48 @@ __device__ __forceinline__ void mlp_load_w(uint8_t* dst, const int8_t* w8, int n
   }
 }
 
-// 16 fp16 values -> 16 int8 (one uint4) with per-column LET constants.
+// 16 fp16 values -> 16 int8 (one uint4) with per-column LET constants. For the dynamic
+// LET scale (the common case) the fast quotient of all 16 values is rounded first and
+// the exact path of ActQuant::qbits runs only when one of them lies near a rounding
+// boundary (one test per 16 values instead of one branch per value).
 __device__ __forceinline__ uint4 mlp_quant16(const uint4 v0, const uint4 v1, const ActQuant& aq,
                                              const float* a, const float* b) {
   const uint32_t h[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-  uint32_t w[4] = {0, 0, 0, 0};
+  float x[16], al[16], be[16];
 #pragma unroll
   for (int j = 0; j < 16; j += 4) {
     const float4 a4 = *reinterpret_cast<const float4*>(a + j);
     const float4 b4 = *reinterpret_cast<const float4*>(b + j);
     const float2 x01 = __half22float2(*reinterpret_cast<const __half2*>(&h[j >> 1]));
     const float2 x23 = __half22float2(*reinterpret_cast<const __half2*>(&h[(j >> 1) + 1]));
-    const uint32_t q0 = aq.qbits(x01.x, a4.x, b4.x), q1 = aq.qbits(x01.y, a4.y, b4.y);
-    const uint32_t q2 = aq.qbits(x23.x, a4.z, b4.z), q3 = aq.qbits(x23.y, a4.w, b4.w);
-    // low bytes of q0..q3 -> one word (byte permutes instead of masks and shifts)
-    w[j >> 2] = __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+    x[j] = x01.x, x[j + 1] = x01.y, x[j + 2] = x23.x, x[j + 3] = x23.y;
+    al[j] = a4.x, al[j + 1] = a4.y, al[j + 2] = a4.z, al[j + 3] = a4.w;
+    be[j] = b4.x, be[j + 1] = b4.y, be[j + 2] = b4.z, be[j + 3] = b4.w;
   }
+  uint32_t q[16];
+  bool near = true;
+  if (aq.let && aq.dyn) {
+    constexpr float kMagic = 12582912.0f;
+    near = false;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float z = __fadd_rn(__fmul_rn(x[j], al[j]), be[j]);
+      const float t = fminf(fmaxf(__fmul_rn(z, aq.rcp), -128.0f), 127.0f);
+      const float u = __fadd_rn(t, kMagic);
+      near |= fabsf(__fsub_rn(t, __fsub_rn(u, kMagic))) >= 0.4999f;
+      q[j] = __float_as_uint(u);
+    }
+  }
+  if (near) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) q[j] = aq.qbits(x[j], al[j], be[j]);
+  }
+  // low bytes of q -> four words (byte permutes instead of masks and shifts)
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    w[j] = __byte_perm(__byte_perm(q[4 * j], q[4 * j + 1], 0x0040), __byte_perm(q[4 * j + 2], q[4 * j + 3], 0x0040),
+                       0x5410);
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -264,9 +290,11 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   cp_async_commit();
   grid_dep_wait();                      // encoded rows and slot 2 of the preceding kernel
   // this thread's item of the layer-0 input (rank j quantises tile rows [32j, 32j+32), 14
-  // chunks of 16 columns each), loaded before the waits below so that its latency overlaps them
+  // chunks of 16 columns each; warp k takes chunk k of the 32 rows, so that its constants are
+  // one broadcast and its stores fill consecutive rows), loaded before the waits below so
+  // that its latency overlaps them
   static_assert(32 * 14 <= kMlpThreads, "one input item per thread");
-  const int in_rr = 32 * (int)rank + tid / 14, in_kc = tid % 14;
+  const int in_rr = 32 * (int)rank + lane, in_kc = warp;
   const bool in_ok = tid < 32 * 14 && m0 + in_rr < p.M;
   uint4 in0 = make_uint4(0, 0, 0, 0), in1 = in0;
   if (in_ok) {
