@@ -159,6 +159,17 @@ __device__ __forceinline__ int conv1_quant(float acc, float b, float qa, float q
   q = fminf(fmaxf(q, -128.0f), 127.0f);
   return (int)q;
 }
+// conv1_quant() as the low byte of the returned word, without the conversion unit:
+// clamping first changes nothing (integer bounds), floor(|z| + 0.5) is the mantissa of
+// (|z| + 0.5) + 2^23 added with rounding toward zero, and the sign is applied to the
+// integer (two's complement in the low byte).
+__device__ __forceinline__ uint32_t conv1_qbits(float acc, float b, float qa, float qc) {
+  float z = fmaxf(__fadd_rn(acc, b), 0.0f);
+  z = fminf(fmaxf(__fadd_rn(__fmul_rn(z, qa), qc), -128.0f), 127.0f);
+  const uint32_t t = __float_as_uint(__fadd_rz(__fadd_rn(fabsf(z), 0.5f), 8388608.0f));
+  const uint32_t sgn = (uint32_t)(__float_as_int(z) >> 31);
+  return (t ^ sgn) - sgn;
+}
 
 // ---- 64-wide cross-lane reduction -----------------------------------------------
 // On return lane L holds the warp sums of channels c0 and c0+1 with

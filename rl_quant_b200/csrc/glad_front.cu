@@ -410,13 +410,11 @@ __global__ void __launch_bounds__(kFrontThreads, FRONT_MIN_BLOCKS) front_kernel(
               const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
               const float aa[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
               const float cc[4] = {qc4.x, qc4.y, qc4.z, qc4.w};
-              uint32_t word = 0;
+              uint32_t q4[4];
 #pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const int q = conv1_quant(__uint_as_float(r[4 * w4 + b]), bb[b], aa[b], cc[b]);
-                word |= ((uint32_t)(q & 0xFF)) << (8 * b);
-              }
-              pk[w4] = word;
+              for (int b = 0; b < 4; ++b)
+                q4[b] = conv1_qbits(__uint_as_float(r[4 * w4 + b]), bb[b], aa[b], cc[b]);
+              pk[w4] = __byte_perm(__byte_perm(q4[0], q4[1], 0x0040), __byte_perm(q4[2], q4[3], 0x0040), 0x5410);
             }
             const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             if (kConv2)
@@ -1198,13 +1196,11 @@ front_fused_kernel(const __grid_constant__ FrontParams p) {
             const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
             const float aa[4] = {qa4.x, qa4.y, qa4.z, qa4.w};
             const float cc[4] = {qc4.x, qc4.y, qc4.z, qc4.w};
-            uint32_t word = 0;
+            uint32_t q4[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int q = conv1_quant(__uint_as_float(r[4 * w4 + k]), bb[k], aa[k], cc[k]);
-              word |= ((uint32_t)(q & 0xFF)) << (8 * k);
-            }
-            pk[w4] = word;
+            for (int k = 0; k < 4; ++k)
+              q4[k] = conv1_qbits(__uint_as_float(r[4 * w4 + k]), bb[k], aa[k], cc[k]);
+            pk[w4] = __byte_perm(__byte_perm(q4[0], q4[1], 0x0040), __byte_perm(q4[2], q4[3], 0x0040), 0x5410);
           }
           const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(s.strip + ((oh + 1) * kStripCols + ow + 1) * 16) = v;
