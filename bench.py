@@ -45,8 +45,8 @@ MACS_PER_ENV = 2.55e6             # conv1 .. actor MLP (int8 2.02 M + fp16 0.53 
 OBS_BYTES_PER_ENV = 2175 * 4      # what the front kernel must read per env
 # DRAM bytes (read + write) per front_fused_kernel launch per environment, from the ncu
 # capture summarised in profiles/front_fused_kernel_glad_b4096.md (35.768 MB read +
-# 0.098 MB written at B=4096); traffic grows with the environments processed.
-FRONT_DRAM_BYTES_PER_ENV = (35.768064e6 + 0.098048e6) / 4096
+# 0.073 MB written at B=4096); traffic grows with the environments processed.
+FRONT_DRAM_BYTES_PER_ENV = (35.767552e6 + 0.072704e6) / 4096
 N_STAGES = ("absmax", "front", "tail", "actor.0", "actor.2", "actor.4", "actor.6")
 
 
