@@ -126,3 +126,26 @@ def test_conv_chain_large_batch(dw, golden_weights):
     torch.cuda.synchronize()
     assert np.array_equal(z2.cpu().numpy(), got_z8)
     assert np.array_equal(f2.cpu().numpy(), got_feat)
+
+
+def test_conv1_rounding_ties_exact(golden_weights):
+    """One unit tap per output channel makes every accumulator exact, and half-integer
+    inputs put z exactly on rounding ties of both signs and beyond both clamp bounds:
+    the kernel's round-half-away-from-zero and clamp equal the oracle's bit for bit
+    (qrt/qconv.py:96-101)."""
+    w = dict(golden_weights)
+    w1p = np.zeros((128, 16), np.float16)
+    for n in range(16):
+        w1p[2 * 16 + 2 * 3 + n % 3, n] = 1.0        # centre tap (kh = kw = 2) of input channel n % 3
+    w["map_cnn.w1p"] = w1p
+    w["map_cnn.b1f"] = np.zeros(16, np.float32)
+    w["map_cnn.qa"] = np.ones(16, np.float32)
+    w["map_cnn.qc"] = np.arange(16, dtype=np.float32) * 16.0 - 140.0   # z from below -128 to above 127
+    dev = DeviceWeights(w)
+    rng = np.random.default_rng(7)
+    x = (rng.integers(-300, 400, size=(64, 21, 33, 3)) * 0.5).astype(np.float16)
+    z8 = _conv1(dev, torch.from_numpy(x).cuda()).cpu().numpy()
+    q, z = O.conv1_fused_q(x, w1p, w["map_cnn.b1f"], w["map_cnn.qa"], w["map_cnn.qc"], return_z=True)
+    assert (np.abs(z - np.trunc(z)) == 0.5).mean() > 0.2           # many exact ties
+    assert (z < -128.5).any() and (z > 127.5).any()
+    assert np.array_equal(z8, q)
