@@ -148,6 +148,8 @@ typedef struct GladActorAux {
   void* attn_weights;    /* [B,32]    f16   head-mean attention weights         */
   void* encoded;         /* [B,224]   f16   cat(foothold, gc, proprio)          */
   float* act_scales;     /* [6]       f32   per-layer s_z used by this call     */
+  void* proprio_emb;     /* [B,64]    f16   actor_proprio_embedding output, 16-byte aligned */
+  void* query;           /* [B,64]    f16   query_projector output (qrt/encoder_opt.py:78-79) */
 } GladActorAux;
 
 /* ---- qrt operator replacements -------------------------------------------- */
@@ -301,17 +303,46 @@ int glad_actor_kernel_count(int64_t B, int act_mode);
  * most GLAD_NOALLOC_MAX_B environments (about 11.2 MiB held on every GPU that
  * loads the library until exit); larger B is rejected with
  * GLAD_ERR_INVALID_ARG. The first call on a device resolves the array's
- * address (make it before any stream capture). Calls share the array:
- * calls that overlap on the GPU race, so serialise them on one stream.
- * Arguments and results are those of glad_actor_forward.                    */
+ * address: make it before any stream capture (a first call on a capturing
+ * stream returns GLAD_ERR_INVALID_ARG); the address is kept until exit, so
+ * cudaDeviceReset is not supported together with this entry point. Calls
+ * share the array: calls that overlap on the GPU race, so serialise them on
+ * one stream. Arguments and results are those of glad_actor_forward.        */
 #define GLAD_NOALLOC_MAX_B 2048
 int glad_actor_forward_noalloc(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
                                int64_t ld_obs, int act_mode, const float* topk_noise,
                                float* mean_out, const GladActorAux* aux, void* stream);
 
-/* Device-side status word of the last launches that used `workspace`
- * (0 = fine; bits = a bounded wait ran out). Synchronises `stream`.        */
-int glad_workspace_status(const void* workspace, uint32_t* status, void* stream);
+/* Device-side status word of the last glad_actor_forward_noalloc call on the
+ * current device (the static scratch's copy of what glad_workspace_status
+ * reads from a workspace): 0 = fine, bits = a bounded wait ran out, in which
+ * case the call's outputs are not valid and GLAD_ERR_DEVICE is returned.
+ * Synchronises `stream`. Companion of the allocation-free entry point; no
+ * counterpart in the reference.                                             */
+int glad_actor_noalloc_status(uint32_t* status, void* stream);
+
+/* Device-side status word of a workspace: every bounded wait inside the
+ * kernels (mbarrier waits on the tensor core, the grid barriers of the dynamic
+ * scales) gives up after its limit, ORs a GLAD_DEVERR_* bit into this word and
+ * lets the kernel finish, so the device stays usable but that call's results
+ * are not valid. The word lives outside what each call clears: it collects
+ * every launch since the previous glad_workspace_status call on this
+ * workspace, which reads it into *status, clears it and returns
+ * GLAD_ERR_DEVICE when it was not 0. A workspace must be zeroed (at least its
+ * first 256 bytes) before its first use. Synchronises `stream`.           */
+#define GLAD_DEVERR_MMA_TIMEOUT 1u       /* a tensor-core completion wait ran out     */
+#define GLAD_DEVERR_COPY_TIMEOUT 2u      /* an asynchronous-copy completion wait ran out */
+#define GLAD_DEVERR_BAD_SHAPE 4u         /* a kernel met a shape it was not built for */
+#define GLAD_DEVERR_BARRIER_TIMEOUT 8u   /* a grid barrier ran out (CTAs not co-resident) */
+int glad_workspace_status(void* workspace, uint32_t* status, void* stream);
+
+/* Test hook of the failure path, not part of the reference interface: the
+ * fused actor MLP's grid barriers (launched after this call) wait for
+ * `extra_arrivals` CTAs more than the grid holds and give up after
+ * `limit_ns` nanoseconds (0: the normal 2 s), so a forward reports
+ * GLAD_DEVERR_BARRIER_TIMEOUT through its status word without hanging.
+ * (0, 0) restores normal operation. Process-wide.                          */
+int glad_debug_mlp_barrier(uint32_t extra_arrivals, uint64_t limit_ns);
 
 /* ---- W4A16 actor MLP (no reference implementation: INT4 is named only as
  * future work in the reference, README.md:259) ------------------------------

@@ -135,18 +135,22 @@ def conv1_fused_q(x_nhwc, w1p, b1, qa, qc, return_z=False):
 
 
 def conv2_acc(z8, w8):
-    """int32 accumulators of ``_k_conv2_int8_fused`` (qrt/qconv.py:135-153)."""
-    z = np.asarray(z8).astype(np.int64).reshape(-1, H2, W2, C2)
+    """int32 accumulators of ``_k_conv2_int8_fused`` (qrt/qconv.py:135-153).
+
+    The nine taps run as fp32 matrix products: every product of two int8 values
+    is at most 2^14 in magnitude and a sum of 144 of them stays below 2^22, so
+    every partial sum is an integer that fp32 holds exactly, in any order."""
+    z = np.asarray(z8).astype(f32).reshape(-1, H2, W2, C2)
     B = z.shape[0]
-    zp = np.zeros((B, H2 + 2, W2 + 2, C2), np.int64)
+    zp = np.zeros((B, H2 + 2, W2 + 2, C2), f32)
     zp[:, 1:1 + H2, 1:1 + W2, :] = z
-    w = np.asarray(w8).astype(np.int64)                           # [3, 64(ks), 64(n)]
-    acc = np.zeros((B, H2, W2, N2), np.int64)
+    w = np.asarray(w8).astype(f32)                                # [3, 64(ks), 64(n)]
+    acc = np.zeros((B * P, N2), f32)
     for kh in range(3):
         for kw in range(3):
-            tap = zp[:, kh:kh + H2, kw:kw + W2, :]                 # [B,11,17,16]
-            acc += np.einsum("bhwc,cn->bhwn", tap, w[kh, kw * 16:kw * 16 + 16, :])
-    return acc.reshape(B * P, N2).astype(i32)
+            tap = np.ascontiguousarray(zp[:, kh:kh + H2, kw:kw + W2, :]).reshape(B * P, C2)
+            acc += tap @ w[kh, kw * 16:kw * 16 + 16, :]
+    return acc.astype(i32)
 
 
 def conv2_epilogue(acc, dq, b2, a2, c2):
@@ -386,6 +390,25 @@ def encode(obs, Wt: GladWeights, act_mode="dynamic", proprio="actor", noise=None
     pert = topk_logits if noise is None else (topk_logits.astype(f32) + np.asarray(noise, f32)).astype(f16)
     idx = topk_lowest_index(pert, 32)
     sparse = np.take_along_axis(local, idx[..., None], axis=1)               # [B,32,D]
+    foot, attn_w = mha(query, sparse, Wt)
+    enc = np.concatenate([foot, gc, prop], axis=1)
+    if aux is not None:
+        aux.update(z8=z8, local=local, emb=emb, gc_logits=gc_logits, score_local=score_local,
+                   gc_w=gc_w, gc=gc, query=query, score_query=score_query,
+                   topk_logits=topk_logits, topk_idx=idx, foothold=foot, attn_weights=attn_w,
+                   enc=enc, s_pe=pe_aux.get("s_z"), s_qp=qp_aux.get("s_z"),
+                   q_pe=pe_aux.get("q"), acc_pe=pe_aux.get("acc"),
+                   q_qp=qp_aux.get("q"), acc_qp=qp_aux.get("acc"))
+    return enc
+
+
+def mha(query, sparse, Wt: GladWeights):
+    """The encoder's single-query cross-attention (qrt/encoder_opt.py:104-119): query
+    ``[B,64]`` over the 32 gathered tokens ``[B,32,64]`` (fp16), 16 heads of 4. Returns
+    ``foothold [B,64]`` and the head-mean attention weights ``[B,1,32]``, both fp16."""
+    query = np.asarray(query).astype(f16)
+    sparse = np.asarray(sparse).astype(f16)
+    B, D = query.shape
     Win, bin_ = Wt["mha.in_proj_weight"], Wt["mha.in_proj_bias"]
     q = linear16_2step(query, Win[:D], bin_[:D])
     k = linear16_2step(sparse.reshape(-1, D), Win[D:2 * D], bin_[D:2 * D]).reshape(B, 32, D)
@@ -399,15 +422,36 @@ def encode(obs, Wt: GladWeights, act_mode="dynamic", proprio="actor", noise=None
     oh = _mm16(attn, vh)                                                      # [B,H,1,4]
     foot = linear16_2step(oh.reshape(B, D), Wt["mha.out_proj.weight"], Wt["mha.out_proj.bias"])
     attn_w = attn[:, :, 0, :].astype(f32).mean(axis=1, keepdims=True).astype(f16)
-    enc = np.concatenate([foot, gc, prop], axis=1)
-    if aux is not None:
-        aux.update(z8=z8, local=local, emb=emb, gc_logits=gc_logits, score_local=score_local,
-                   gc_w=gc_w, gc=gc, query=query, score_query=score_query,
-                   topk_logits=topk_logits, topk_idx=idx, foothold=foot, attn_weights=attn_w,
-                   enc=enc, s_pe=pe_aux.get("s_z"), s_qp=qp_aux.get("s_z"),
-                   q_pe=pe_aux.get("q"), acc_pe=pe_aux.get("acc"),
-                   q_qp=qp_aux.get("q"), acc_qp=qp_aux.get("acc"))
-    return enc
+    return foot, attn_w
+
+
+def actor_mlp(enc, Wt: GladWeights, act_mode="dynamic", aux=None):
+    """The INT8 actor MLP of qrt full mode (``actor.0/2/4/6`` QuantLinear with ELU between,
+    rsl_rl/networks/mlp.py:59-83 with qrt/integration.py:42-43) on the fp16 ``encoded`` rows;
+    returns the fp16 head output as fp32 ``[B, 29]`` (``.float()``, qrt/integration.py:206)."""
+    h = np.asarray(enc).astype(f16)
+    for i, n in enumerate(("actor.0", "actor.2", "actor.4", "actor.6")):
+        L = Wt.ql(n)
+        la = {}
+        h = qlinear_forward(h, L, act_mode, L["out_features"], la)
+        if aux is not None:
+            aux[f"{n}.q"], aux[f"{n}.acc"], aux[f"{n}.s_z"] = la["q"], la["acc"], la["s_z"]
+        if i < 3:
+            h = _elu16(h)
+        if aux is not None:
+            aux[f"{n}.out"] = h
+    return h.astype(f32)
+
+
+def critic_mlp(enc, Wt: GladWeights):
+    """The fp16 critic MLP (``critic.0/2/4/6``, not quantised, qrt/integration.py:42-43,133-135)
+    on the fp16 critic ``encoded`` rows; returns ``[B,1]`` fp32."""
+    h = np.asarray(enc).astype(f16)
+    for i, n in enumerate(("critic.0", "critic.2", "critic.4", "critic.6")):
+        h = linear16(h, Wt[f"{n}.weight"], Wt[f"{n}.bias"])
+        if i < 3:
+            h = _elu16(h)
+    return h.astype(f32)
 
 
 def linear16_2step(x, w, b):
@@ -422,29 +466,14 @@ def actor_forward(obs, Wt: GladWeights, act_mode="dynamic", noise=None, aux=None
     INT8 actor MLP (``actor.0/2/4/6`` with ELU between, rsl_rl/networks/mlp.py:59-83).
     Returns the action mean ``[B, 29]`` in fp32 (``.float()``, integration.py:206)."""
     h = encode(obs, Wt, act_mode, "actor", noise, aux)
-    names = ("actor.0", "actor.2", "actor.4", "actor.6")
-    for i, n in enumerate(names):
-        L = Wt.ql(n)
-        la = {}
-        h = qlinear_forward(h, L, act_mode, L["out_features"], la)
-        if aux is not None:
-            aux[f"{n}.q"], aux[f"{n}.acc"], aux[f"{n}.s_z"] = la["q"], la["acc"], la["s_z"]
-        if i < 3:
-            h = _elu16(h)
-        if aux is not None:
-            aux[f"{n}.out"] = h
-    return h.astype(f32)
+    return actor_mlp(h, Wt, act_mode, aux)
 
 
 def critic_forward(obs, Wt: GladWeights, act_mode="dynamic", aux=None):
     """Compiled ``f_val`` (qrt/integration.py:133-135): same encoder with the
     fp16 critic proprio embedding, fp16 critic MLP. Returns ``[B,1]`` fp32."""
     h = encode(obs, Wt, act_mode, "critic", None, aux)
-    for i, n in enumerate(("critic.0", "critic.2", "critic.4", "critic.6")):
-        h = linear16(h, Wt[f"{n}.weight"], Wt[f"{n}.bias"])
-        if i < 3:
-            h = _elu16(h)
-    return h.astype(f32)
+    return critic_mlp(h, Wt)
 
 
 # -- W4A16 actor MLP ----------------------------------------------------------------

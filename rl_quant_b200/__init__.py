@@ -25,7 +25,7 @@ _EXPORTS = {
     "accelerate_runner": "integration", "QRTAccelerator": "integration",
     "INT8_PATHS_DEFAULT": "integration",
     "LETQuantizer": "let",
-    "FusedActor": "fused",
+    "FusedActor": "fused", "DeviceStatusError": "fused",
     "GladActorCritic": "glad_model", "build_glad": "glad_model",
 }
 _SUBMODULES = ("swap", "calib", "_native", "synthetic", "glad_model", "qconv", "qlinear", "encoder_opt",

@@ -61,7 +61,8 @@ class GladCriticWeights(Structure):
 
 class GladActorAux(Structure):
     _fields_ = [(n, c_void_p) for n in ("z8", "local", "gc_weights", "score_local", "topk_logits",
-                                        "topk_idx", "attn_weights", "encoded", "act_scales")]
+                                        "topk_idx", "attn_weights", "encoded", "act_scales",
+                                        "proprio_emb", "query")]
 
 
 class GladQLinearSrc(Structure):
@@ -122,10 +123,12 @@ SIGNATURES = {
                                     c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
     "glad_actor_forward_noalloc": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                            c_void_p, c_void_p, POINTER(GladActorAux), c_void_p]),
+    "glad_actor_noalloc_status": (c_int, [POINTER(c_uint32), c_void_p]),
     "glad_actor_stage_events": (c_int, [POINTER(c_void_p), c_int]),
     "glad_actor_mlp_fused": (c_int, [c_int64, c_int]),
     "glad_actor_kernel_count": (c_int, [c_int64, c_int]),
     "glad_workspace_status": (c_int, [c_void_p, POINTER(c_uint32), c_void_p]),
+    "glad_debug_mlp_barrier": (c_int, [c_uint32, c_uint64]),
     "glad_requant_qlinear": (c_int, [POINTER(GladQLinearSrc), c_int, c_void_p]),
     "glad_requant_qcnn": (c_int, [POINTER(GladQCNNSrc), c_void_p]),
     "glad_cast_copy": (c_int, [POINTER(GladCastCopy), c_int, c_void_p]),

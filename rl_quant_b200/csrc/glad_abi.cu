@@ -211,7 +211,7 @@ extern "C" {
 
 const char* glad_last_error(void) { return g_err; }
 
-int glad_abi_version(void) { return 101; }
+int glad_abi_version(void) { return 102; }
 
 int glad_conv1_fused_q(const void* x_nhwc, int64_t B, const GladConvWeights* w, int8_t* z8_out,
                        void* stream) {
@@ -310,7 +310,7 @@ int glad_qlinear_forward(const GladQLinear* L, int act_mode, const void* x, int 
   if ((rc = device_info(&d))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   float* slots = reinterpret_cast<float*>(workspace);
-  GLAD_CHECK_CUDA(cudaMemsetAsync(slots, 0, kSlotsBytes, st), "workspace reset");
+  GLAD_CHECK_CUDA(cudaMemsetAsync(slots, 0, kSlotsClearBytes, st), "workspace reset");
   if (act_mode == GLAD_ACT_DYNAMIC)
     GLAD_CHECK_CUDA(launch_absmax(x, x_dtype, M, ldx, L->in_features, L->alpha, L->beta, 0,
                                   &slots[0], d.sms, st),
@@ -508,11 +508,12 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   int8_t* z8 = ax.z8 ? ax.z8 : ws.z8;
   __half* score_local = ax.score_local ? reinterpret_cast<__half*>(ax.score_local) : ws.score_local;
   __half* enc = ax.encoded ? reinterpret_cast<__half*>(ax.encoded) : ws.enc;
-  if (!aligned(z8, 16) || !aligned(enc, 16))
-    return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded must be 16-byte aligned");
+  __half* pe = ax.proprio_emb ? reinterpret_cast<__half*>(ax.proprio_emb) : ws.pe;
+  if (!aligned(z8, 16) || !aligned(enc, 16) || !aligned(pe, 16) || (ax.query && !aligned(ax.query, 4)))
+    return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded / proprio_emb must be 16-byte aligned, query 4-byte");
 
   stage_mark(0, st);
-  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
+  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsClearBytes, st), "workspace reset");
   // Dynamic s_z of the proprio embedding: reduced inside the front kernel (grid
   // barrier) when its whole grid fits on the device at once, else by a separate pass.
   const int front_per_sm = front_fused_blocks_per_sm();
@@ -543,7 +544,7 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   fp.score_local = score_local;
   fp.gc_w_out = reinterpret_cast<__half*>(ax.gc_weights);
   fp.enc = enc;
-  fp.pe_out = ws.pe;
+  fp.pe_out = pe;
   fp.slots = ws.slots;
   fp.pe_absmax = pe_absmax_in_front ? 1 : 0;
   fp.norm_mean = nm.mean;
@@ -587,11 +588,12 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   tp.done_slot = kSlotTailDone;
   tp.z8 = z8;
   tp.score_local = score_local;
-  tp.pe = ws.pe;
+  tp.pe = pe;
   tp.enc = enc;
   tp.topk_logits_out = reinterpret_cast<__half*>(ax.topk_logits);
   tp.topk_idx_out = ax.topk_idx;
   tp.attn_w_out = reinterpret_cast<__half*>(ax.attn_weights);
+  tp.query_out = reinterpret_cast<__half*>(ax.query);
   tp.slots = ws.slots;
   GLAD_CHECK_CUDA(launch_tail(tp, tail_grid(B, d.sms), st, true), "tail launch");
   stage_mark(3, st);
@@ -658,6 +660,7 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
     tc.topk_logits_out = nullptr;
     tc.topk_idx_out = nullptr;
     tc.attn_w_out = nullptr;
+    tc.query_out = nullptr;
     GLAD_CHECK_CUDA(launch_tail(tc, tail_grid(B, d.sms), st, true), "critic tail launch");
     GladLinear16 L[4] = {dual->wc->mlp[0], dual->wc->mlp[1], dual->wc->mlp[2], dual->wc->mlp[3]};
     GLAD_CHECK_CUDA(launch_f16mlp(L, dual->enc_c, B, kCriticEnc, dual->value_out, 1,
@@ -735,10 +738,11 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   int8_t* z8 = ax.z8 ? ax.z8 : ws.z8;
   __half* score_local = ax.score_local ? reinterpret_cast<__half*>(ax.score_local) : ws.score_local;
   __half* enc = ax.encoded ? reinterpret_cast<__half*>(ax.encoded) : ws.enc;
-  if (!aligned(z8, 16) || !aligned(enc, 16))
-    return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded must be 16-byte aligned");
+  __half* pe = ax.proprio_emb ? reinterpret_cast<__half*>(ax.proprio_emb) : ws.pe;
+  if (!aligned(z8, 16) || !aligned(enc, 16) || !aligned(pe, 16) || (ax.query && !aligned(ax.query, 4)))
+    return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded / proprio_emb must be 16-byte aligned, query 4-byte");
 
-  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsBytes, st), "workspace reset");
+  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsClearBytes, st), "workspace reset");
   const bool front_pdl = !pe16 && act_mode == GLAD_ACT_DYNAMIC;
   if (front_pdl)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb_q.alpha,
@@ -770,7 +774,7 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   fp.score_local = score_local;
   fp.gc_w_out = reinterpret_cast<__half*>(ax.gc_weights);
   fp.enc = enc;
-  fp.pe_out = ws.pe;
+  fp.pe_out = pe;
   fp.slots = ws.slots;
   GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, front_grid(B, d, 2), st, front_pdl), "front launch");
 
@@ -792,11 +796,12 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   tp.prop_dim = P;
   tp.z8 = z8;
   tp.score_local = score_local;
-  tp.pe = ws.pe;
+  tp.pe = pe;
   tp.enc = enc;
   tp.topk_logits_out = reinterpret_cast<__half*>(ax.topk_logits);
   tp.topk_idx_out = ax.topk_idx;
   tp.attn_w_out = reinterpret_cast<__half*>(ax.attn_weights);
+  tp.query_out = reinterpret_cast<__half*>(ax.query);
   tp.slots = ws.slots;
   GLAD_CHECK_CUDA(launch_tail(tp, tail_grid(B, d.sms), st, true), "tail launch");
 
@@ -903,16 +908,20 @@ int glad_actor_stage_events(void* const* events, int n) {
   return GLAD_OK;
 }
 
-int glad_workspace_status(const void* workspace, uint32_t* status, void* stream) {
+int glad_workspace_status(void* workspace, uint32_t* status, void* stream) {
   g_err[0] = 0;
   if (!workspace || !status) return fail(GLAD_ERR_INVALID_ARG, "workspace and status must be set");
   cudaStream_t st = (cudaStream_t)stream;
-  const float* slots = reinterpret_cast<const float*>(workspace);
+  float* slots = reinterpret_cast<float*>(workspace);
   GLAD_CHECK_CUDA(cudaMemcpyAsync(status, slots + kSlotStatus, sizeof(uint32_t),
                                   cudaMemcpyDeviceToHost, st),
                   "status copy");
+  GLAD_CHECK_CUDA(cudaMemsetAsync(slots + kSlotStatus, 0, sizeof(uint32_t), st),
+                  "status clear");
   GLAD_CHECK_CUDA(cudaStreamSynchronize(st), "status sync");
-  return *status ? fail(GLAD_ERR_DEVICE, "device status 0x%x", *status) : GLAD_OK;
+  return *status ? fail(GLAD_ERR_DEVICE, "device status 0x%x (a bounded device-side wait ran out: the "
+                        "results of the launches since the last status read are not valid)", *status)
+                 : GLAD_OK;
 }
 
 int glad_requant_qlinear(const GladQLinearSrc* layers, int n, void* stream) {

@@ -24,8 +24,9 @@ constexpr int kActions = 29;
 // slots[0..5] : running absmax of each quantised layer's input z (dynamic s_z)
 //   0 actor_proprio_embedding, 1 query_projector, 2 actor.0, 3 actor.2,
 //   4 actor.4, 5 actor.6
-// slots[8]    : device status word (DeviceError bits)
-constexpr int kSlotStatus = 8;
+// slots[63]   : device status word (DeviceError bits); outside the per-call clear, so it
+//               collects every launch since glad_workspace_status last read (and cleared) it
+constexpr int kSlotStatus = 63;
 constexpr int kSlotCriticQp = 7;        // critic query projector absmax (fused actor + critic)
 // slots[16..18] : arrival counters of the fused MLP's grid barriers
 // slots[19]     : arrival counter of the front kernel's proprio-absmax grid barrier
@@ -34,6 +35,10 @@ constexpr int kSlotFrontBarrier = 19;
 constexpr int kSlotTailDone = 20;       // CTAs of the tail kernel that finished (Gumbel offset)
 constexpr int kSlotCriticTailDone = 21; // the same for the critic tail of a fused actor + critic call
 constexpr int kSlotsBytes = 256;
+constexpr int kSlotsClearBytes = kSlotStatus * 4;   // what each call zeroes: everything but the status
+static_assert(kDevErrMmaTimeout == GLAD_DEVERR_MMA_TIMEOUT && kDevErrCopyTimeout == GLAD_DEVERR_COPY_TIMEOUT &&
+                  kDevErrBadShape == GLAD_DEVERR_BAD_SHAPE && kDevErrBarrierTimeout == GLAD_DEVERR_BARRIER_TIMEOUT,
+              "device status bits and their C-ABI names agree");
 
 __device__ __forceinline__ float fp16r(float x) { return __half2float(__float2half_rn(x)); }
 
@@ -382,6 +387,7 @@ struct TailParams {
   __half* topk_logits_out; // [B,187] or null
   int64_t* topk_idx_out;   // [B,32] or null
   __half* attn_w_out;      // [B,32] or null
+  __half* query_out;       // [B,64] query projector output or null
   float* slots;
 };
 

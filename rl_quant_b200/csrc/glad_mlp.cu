@@ -72,7 +72,14 @@ struct MlpParams {
   float* mean;             // [M, ldm] = float(fp16(head output))
   int64_t ldm;
   float* slots;            // absmax slots 2..5, status, barrier counters
+  uint32_t barrier_extra;  // arrivals the grid barriers wait for beyond the grid (0; tests only)
+  uint64_t barrier_limit_ns;   // spin limit of the grid barriers
 };
+
+// Failure-path test hook (glad_debug_mlp_barrier): process-wide, read at launch.
+static uint32_t g_mlp_barrier_extra = 0;
+static uint64_t g_mlp_barrier_limit_ns = 0;
+constexpr uint64_t kMlpBarrierLimitNs = 2000000000ull;
 
 // Rows [n0, n0+ROWS) of a row-major int8 [*, K] weight -> [K/16][ROWS][16 B] (compile-time
 // shapes: the index split is a shift).
@@ -197,9 +204,9 @@ __device__ __forceinline__ __half2 elu16x2(__half2 h) {
 // Grid-wide barrier on counter `ctr` (one arrival per CTA), folded with the batch
 // absmax: the CTA's warps leave their maxima in `red`, thread 0 adds one atomic max
 // to `slot`, arrives with a release add and spins with acquire loads. The spin gives
-// up after 2 s (status bit, abort flag); an aborted CTA still arrives.
+// up after limit_ns (2 s; status bit, abort flag); an aborted CTA still arrives.
 __device__ __forceinline__ void mlp_grid_barrier(int* abort_flag, float* red, float* slot, uint32_t* ctr,
-                                                 uint32_t expected, uint32_t* status) {
+                                                 uint32_t expected, uint32_t* status, uint64_t limit_ns) {
   __syncthreads();
   if (threadIdx.x == 0) {
     float m = red[0];
@@ -209,7 +216,7 @@ __device__ __forceinline__ void mlp_grid_barrier(int* abort_flag, float* red, fl
     if (!*abort_flag) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_gpu(ctr) < expected) {
-        if (global_timer_ns() - t0 > 2000000000ull) {
+        if (global_timer_ns() - t0 > limit_ns) {
           *abort_flag = 1;
           atomicOr(status, kDevErrBarrierTimeout);
           break;
@@ -382,7 +389,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
       zmax = warp_max(zmax);
       if (lane == 0) red[warp] = zmax;
       mlp_grid_barrier(abort_flag, red, &p.slots[3 + l],
-                       reinterpret_cast<uint32_t*>(&p.slots[kSlotMlpBarrier + l]), gridDim.x, status);
+                       reinterpret_cast<uint32_t*>(&p.slots[kSlotMlpBarrier + l]), gridDim.x + p.barrier_extra, status,
+                       p.barrier_limit_ns);
       aq.let = nlet;
       aq.dyn = true;
       aq.s = dyn_scale(ld_relaxed_gpu(&p.slots[3 + l]), nlet);
@@ -508,6 +516,8 @@ cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x,
   p.mean = mean;
   p.ldm = ldm;
   p.slots = slots;
+  p.barrier_extra = g_mlp_barrier_extra;
+  p.barrier_limit_ns = g_mlp_barrier_limit_ns ? g_mlp_barrier_limit_ns : kMlpBarrierLimitNs;
   const int tiles = (int)((M + 127) / 128);
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[2];
@@ -527,3 +537,14 @@ cudaError_t launch_mlp(const GladQLinear (&L)[4], int act_mode, const __half* x,
 }
 
 }  // namespace glad
+
+namespace glad {
+int set_last_error(int code, const char* msg);   // glad_abi.cu
+}
+
+extern "C" int glad_debug_mlp_barrier(uint32_t extra_arrivals, uint64_t limit_ns) {
+  if (extra_arrivals > 1024) return glad::set_last_error(GLAD_ERR_INVALID_ARG, "extra_arrivals above 1024");
+  glad::g_mlp_barrier_extra = extra_arrivals;
+  glad::g_mlp_barrier_limit_ns = limit_ns;
+  return GLAD_OK;
+}

@@ -43,6 +43,47 @@ namespace glad {
 int set_last_error(int code, const char* msg);   // glad_abi.cu
 }
 
+namespace {
+
+// The array's device address on the current device, resolved once per device with
+// that device current. The first resolution may load the module on the device,
+// which a capturing stream does not allow, so it is refused during capture.
+// The cached address assumes the device's primary context lives until exit
+// (cudaDeviceReset is not supported together with this entry point).
+int scratch_address(void** out, cudaStream_t stream, const char* who) {
+  char msg[256];
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    snprintf(msg, sizeof(msg), "%s: cudaGetDevice: %s", who, cudaGetErrorString(e));
+    return glad::set_last_error(GLAD_ERR_CUDA, msg);
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+      snprintf(msg, sizeof(msg),
+               "%s: the first call on device %d must come before any stream capture (it resolves the "
+               "static scratch's device address)", who, dev);
+      return glad::set_last_error(GLAD_ERR_INVALID_ARG, msg);
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      snprintf(msg, sizeof(msg), "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+      return glad::set_last_error(GLAD_ERR_CUDA, msg);
+    }
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return GLAD_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int glad_actor_forward_noalloc(const GladActorWeights* w, const void* obs, int obs_dtype, int64_t B,
@@ -59,32 +100,19 @@ int glad_actor_forward_noalloc(const GladActorWeights* w, const void* obs, int o
   if (glad_actor_workspace_size(GLAD_NOALLOC_MAX_B) > kNoAllocBytes)
     return glad::set_last_error(GLAD_ERR_WORKSPACE,
                                 "glad_actor_forward_noalloc: static scratch smaller than the workspace layout");
-  // once per device, with that device current: the array's device address
-  static std::mutex mu;
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    snprintf(msg, sizeof(msg), "glad_actor_forward_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-    return glad::set_last_error(GLAD_ERR_CUDA, msg);
-  }
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess) {
-        snprintf(msg, sizeof(msg), "glad_actor_forward_noalloc: cudaGetSymbolAddress: %s",
-                 cudaGetErrorString(e));
-        return glad::set_last_error(GLAD_ERR_CUDA, msg);
-      }
-      addr[dev] = p;
-    }
-    scratch = addr[dev];
-  }
+  const int rc = scratch_address(&scratch, (cudaStream_t)stream, "glad_actor_forward_noalloc");
+  if (rc) return rc;
   return glad_actor_forward(w, obs, obs_dtype, B, ld_obs, act_mode, topk_noise, mean_out, aux, scratch,
                             kNoAllocBytes, stream);
+}
+
+int glad_actor_noalloc_status(uint32_t* status, void* stream) {
+  if (!status) return glad::set_last_error(GLAD_ERR_INVALID_ARG, "glad_actor_noalloc_status: status is NULL");
+  void* scratch = nullptr;
+  const int rc = scratch_address(&scratch, (cudaStream_t)stream, "glad_actor_noalloc_status");
+  if (rc) return rc;
+  return glad_workspace_status(scratch, status, stream);
 }
 
 }  // extern "C"

@@ -205,6 +205,8 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       const float q0 = q01.x, q1 = q01.y;
       s.qv[warp][2 * lane] = q0;
       s.qv[warp][2 * lane + 1] = q1;
+      if (p.query_out)
+        reinterpret_cast<__half2*>(p.query_out + env * kD)[lane] = __floats2half2_rn(q0, q1);
       // ---- 2. score_query = q @ w_s[:, 64:]^T + b_s (fp16 matmul then add) ----------------
       const float sqp = warp_sum(fmaf(q1, s.wsq[2 * lane + 1], q0 * s.wsq[2 * lane]));
       const float sq = fp16r(__fadd_rn(fp16r(sqp), sb));

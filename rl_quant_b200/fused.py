@@ -21,6 +21,29 @@ class FusedUnsupported(NotImplementedError):
     pass
 
 
+class DeviceStatusError(RuntimeError):
+    """A bounded device-side wait (a tensor-core completion or a grid barrier) ran out in
+    one of the launches since the last status check: their outputs are not valid."""
+
+
+def check_workspaces(workspaces, who: str) -> None:
+    """Read and clear the device status word of every workspace (one host sync). Raises
+    DeviceStatusError naming the status bits when one was set."""
+    lib = N.load()
+    bad = []
+    for key, ws in workspaces.items():
+        st = N.c_uint32(0)
+        rc = lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle(ws.device))
+        if rc == N.GLAD_ERR_DEVICE:
+            bad.append((key, st.value))
+        else:
+            N.check(rc, f"{who} status")
+    if bad:
+        raise DeviceStatusError(f"{who}: a bounded device-side wait ran out (status " +
+                                ", ".join(f"B={k[0]}: 0x{v:x}" for k, v in bad) +
+                                "); the results since the previous check are not valid")
+
+
 def _fp16(t: torch.Tensor, name: str) -> torch.Tensor:
     if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
         raise FusedUnsupported(f"{name} must be a contiguous fp16 CUDA tensor (the inference copy is .half())")
@@ -95,9 +118,14 @@ class FusedActor:
         key = (B, str(device))
         ws = self._ws.get(key)
         if ws is None:
-            ws = torch.empty(N.load().glad_actor_workspace_size(B), dtype=torch.uint8, device=device)
+            ws = torch.zeros(N.load().glad_actor_workspace_size(B), dtype=torch.uint8, device=device)
             self._ws[key] = ws
         return ws
+
+    def check_status(self) -> None:
+        """Raise DeviceStatusError if a launch since the previous check reported a
+        device-side timeout (reads and clears each workspace's status word; one sync)."""
+        check_workspaces(self._ws, "fused actor")
 
     def run(self, obs: torch.Tensor, mean: torch.Tensor | None, aux: N.GladActorAux | None = None,
             noise: torch.Tensor | None = None, gumbel: tuple | None = None, obs_norm=None) -> None:
@@ -207,6 +235,10 @@ class FusedCritic:
                                       L.in_features, L.out_features)
         return w
 
+    def check_status(self) -> None:
+        """As FusedActor.check_status, for the critic's workspaces."""
+        check_workspaces(self._ws, "fused critic")
+
     def run(self, obs: torch.Tensor, value: torch.Tensor, noise: torch.Tensor | None = None,
             obs_norm=None) -> None:
         """``obs_norm``: an EmpiricalNormalization applied to the f32 rows as they load."""
@@ -217,7 +249,7 @@ class FusedCritic:
         key = (B, str(obs.device))
         ws = self._ws.get(key)
         if ws is None:
-            ws = torch.empty(N.load().glad_critic_workspace_size(B), dtype=torch.uint8, device=obs.device)
+            ws = torch.zeros(N.load().glad_critic_workspace_size(B), dtype=torch.uint8, device=obs.device)
             self._ws[key] = ws
         rc = N.load().glad_critic_forward(
             self.weights(obs_norm), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
@@ -240,6 +272,12 @@ class FusedActorCritic:
                                    "embedding, run the two heads separately")
         self._ws: dict[tuple, torch.Tensor] = {}
 
+    def check_status(self) -> None:
+        """As FusedActor.check_status, for this call's workspaces and both heads'."""
+        check_workspaces(self._ws, "fused actor + critic")
+        self.actor.check_status()
+        self.critic.check_status()
+
     def run(self, policy_obs: torch.Tensor, critic_obs: torch.Tensor, mean: torch.Tensor,
             value: torch.Tensor, gumbel: tuple | None = None) -> None:
         """``gumbel=(seed, offset)`` (offset: int64 device tensor of one element) runs the
@@ -255,7 +293,7 @@ class FusedActorCritic:
         key = (B, str(policy_obs.device))
         ws = self._ws.get(key)
         if ws is None:
-            ws = torch.empty(N.load().glad_actor_critic_workspace_size(B), dtype=torch.uint8,
+            ws = torch.zeros(N.load().glad_actor_critic_workspace_size(B), dtype=torch.uint8,
                              device=policy_obs.device)
             self._ws[key] = ws
         dt = N.DTYPE_F32 if policy_obs.dtype == torch.float32 else N.DTYPE_F16

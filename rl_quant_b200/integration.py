@@ -11,8 +11,10 @@ What it does (qrt/integration.py:94-247):
   * ``policy.update_distribution`` / ``policy.evaluate`` are rerouted to the
     copy whenever inference mode is on (the rollout); gradient-mode calls
     (the PPO update) keep the original float path;
-  * ``alg.update`` is wrapped so every PPO iteration ends with
-    ``sync_weights_from`` (one graphed cast-copy + requantisation).
+  * ``alg.update`` is wrapped so every PPO iteration first checks the device
+    status of the rollout's fused forwards (``InferenceRunner.check_status``,
+    raising ``DeviceStatusError`` if a bounded device-side wait ran out) and
+    ends with ``sync_weights_from`` (one graphed cast-copy + requantisation).
 
 Training-side options of the reference (``accelerate_update``,
 ``update_amp``, ``cocalib``) concern the PPO update, which is outside this
@@ -155,6 +157,9 @@ class QRTAccelerator:
         self._orig_update = self.alg.update
 
         def update_qrt():
+            # the rollout this update consumes ran on the fused kernels: raise before
+            # training on it if any of their bounded device-side waits ran out
+            acc._runner.check_status()
             out = acc._orig_update()
             acc._runner.sync_weights_from(acc.policy)
             return out

@@ -287,6 +287,16 @@ class InferenceRunner:
             self._pipes[k] = pipe
         return pipe(host_obs, out)
 
+    def check_status(self) -> None:
+        """Raise ``DeviceStatusError`` if any fused forward launched since the previous
+        check (directly or by a captured graph's replay) reported that a bounded
+        device-side wait ran out; its outputs are then not valid. Reads and clears the
+        status word of every workspace (one host synchronisation): call it once per PPO
+        iteration, as ``accelerate_runner`` does before each update."""
+        for f in (self._fused, self._fused_critic, self._fused_ac):
+            if f is not None:
+                f.check_status()
+
     def _device(self):
         for t in self.model.parameters():
             return t.device

@@ -86,12 +86,16 @@ def critic_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, with_aux
     if with_aux:
         aux_t = {"topk_logits": torch.empty(B, 187, dtype=torch.float16, device=dev),
                  "topk_idx": torch.empty(B, 32, dtype=torch.int64, device=dev),
-                 "encoded": torch.empty(B, 232, dtype=torch.float16, device=dev)}
+                 "encoded": torch.empty(B, 232, dtype=torch.float16, device=dev),
+                 "local": torch.empty(B, 187, 64, dtype=torch.float16, device=dev),
+                 "attn_weights": torch.empty(B, 32, dtype=torch.float16, device=dev),
+                 "proprio_emb": torch.empty(B, 64, dtype=torch.float16, device=dev),
+                 "query": torch.empty(B, 64, dtype=torch.float16, device=dev)}
         for k, v in aux_t.items():
             setattr(aux, k, v.data_ptr())
     lib = N.load()
     nbytes = lib.glad_critic_workspace_size(B)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
     dtype = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
     N.check(lib.glad_critic_forward(critic_weights(dw), obs.data_ptr(), dtype, B, obs.stride(0),
                                     N.ACT_MODES[act_mode], None, value.data_ptr(), aux, ws.data_ptr(), nbytes,
@@ -100,6 +104,25 @@ def critic_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, with_aux
     N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
     torch.cuda.synchronize()
     return value, aux_t
+
+
+def actor_critic_forward(dw: DeviceWeights, policy_obs: torch.Tensor, critic_obs: torch.Tensor, act_mode: str):
+    """glad_actor_critic_forward (one read of the shared scan); returns (mean, value)."""
+    B, dev = policy_obs.shape[0], policy_obs.device
+    mean = torch.empty(B, 29, dtype=torch.float32, device=dev)
+    value = torch.empty(B, 1, dtype=torch.float32, device=dev)
+    lib = N.load()
+    nbytes = lib.glad_actor_critic_workspace_size(B)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    dtype = N.DTYPE_F32 if policy_obs.dtype == torch.float32 else N.DTYPE_F16
+    N.check(lib.glad_actor_critic_forward(dw.actor(), critic_weights(dw), policy_obs.data_ptr(), critic_obs.data_ptr(),
+                                          dtype, B, policy_obs.stride(0), critic_obs.stride(0),
+                                          N.ACT_MODES[act_mode], mean.data_ptr(), value.data_ptr(), ws.data_ptr(),
+                                          nbytes, N.stream_handle()), "glad_actor_critic_forward")
+    st = N.c_uint32(0)
+    N.check(lib.glad_workspace_status(ws.data_ptr(), st, N.stream_handle()), "device status")
+    torch.cuda.synchronize()
+    return mean, value
 
 
 def actor_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, noise=None, with_aux=True):
@@ -120,12 +143,14 @@ def actor_forward(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, noise=Non
             "attn_weights": torch.empty(B, 32, dtype=torch.float16, device=dev),
             "encoded": torch.empty(B, 224, dtype=torch.float16, device=dev),
             "act_scales": torch.empty(6, dtype=torch.float32, device=dev),
+            "proprio_emb": torch.empty(B, 64, dtype=torch.float16, device=dev),
+            "query": torch.empty(B, 64, dtype=torch.float16, device=dev),
         }
         for k, v in aux_t.items():
             setattr(aux, k, v.data_ptr())
     lib = N.load()
     ws_bytes = lib.glad_actor_workspace_size(B)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     w = dw.actor()
     dtype = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
     rc = lib.glad_actor_forward(w, obs.data_ptr(), dtype, B, obs.stride(0), N.ACT_MODES[act_mode],
@@ -149,7 +174,7 @@ def actor_forward_train(dw: DeviceWeights, obs: torch.Tensor, act_mode: str, see
         setattr(aux, k, v.data_ptr())
     lib = N.load()
     nbytes = lib.glad_actor_workspace_size(B)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
     dtype = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
     N.check(lib.glad_actor_forward_train(dw.actor(), obs.data_ptr(), dtype, B, obs.stride(0),
                                          N.ACT_MODES[act_mode], seed, offset.data_ptr(), mean.data_ptr(), aux,

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(N.LIB_PATH)
     for name in declared():
         assert hasattr(lib, name), name
-    assert N.load().glad_abi_version() == 101
+    assert N.load().glad_abi_version() == 102
 
 
 def test_workspace_sizes_are_host_only():

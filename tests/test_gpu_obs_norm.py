@@ -82,7 +82,7 @@ def test_obs_norm_argument_checks(infer):
         fa.run(po, m, obs_norm=_norm(100, 4))
     # the shared-scan call takes no normaliser
     w = fac.actor.weights(an)
-    ws = torch.empty(N.load().glad_actor_critic_workspace_size(4), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(N.load().glad_actor_critic_workspace_size(4), dtype=torch.uint8, device="cuda")
     v = torch.empty(4, 1, device="cuda")
     rc = N.load().glad_actor_critic_forward(w, fac.critic.weights(), po.data_ptr(), co.data_ptr(), N.DTYPE_F32, 4,
                                             po.stride(0), co.stride(0), N.ACT_MODES[fac.actor.act_mode],

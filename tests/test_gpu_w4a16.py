@@ -73,7 +73,7 @@ def _actor_w4(dw, mlp, obs, mode):
     mean = torch.empty(B, 29, dtype=torch.float32, device="cuda")
     lib = N.load()
     nbytes = lib.glad_actor_workspace_size(B)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     N.check(lib.glad_actor_forward_w4a16(dw.actor(), mlp.layers(), obs.data_ptr(), N.DTYPE_F32, B, obs.stride(0),
                                          N.ACT_MODES[mode], mean.data_ptr(), ws.data_ptr(), nbytes,
                                          N.stream_handle()), "glad_actor_forward_w4a16")
