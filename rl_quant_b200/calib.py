@@ -1,13 +1,27 @@
-"""Calibration pipeline: activation capture -> LET fit -> swap plan
-(qrt/calib.py:25-129).
+"""LET calibration of qrt's INT8 linears -> the plan ``swap.apply`` consumes.
 
-Difference from the reference: row sampling draws from an explicit
-``torch.Generator`` (seeded by ``seed``) instead of the global RNG, so a plan
-is reproducible.
+The reference builds this plan in qrt/calib.py:62-129 with quant/let.py:140-233.
+Here it is three small pieces:
+
+  * ``record_inputs``  runs the model on calibration batches and keeps, for each
+    quantised Linear, the rows of its input (at most ``max_rows // n_batches``
+    per batch, picked at random);
+  * ``fit_layer``      fits OmniQuant's learnable equivalent transformation
+    (``LETQuantizer``) of one Linear's input with Adam on the block
+    reconstruction loss, then measures the static activation scale;
+  * ``make_plan``      returns ``{path: {"s_z", "alpha", "beta", "act_mode"}}``.
+
+Random row picks come from one ``torch.Generator`` seeded by ``seed``. They are
+drawn in the order the reference draws them from torch's global generator: one
+pick per recorded input per batch (layers in forward order), then one pick per
+fitting step, layer after layer. A reference run seeded with
+``torch.manual_seed(seed)`` on the CPU therefore picks the same rows and ends
+with the same alpha, beta and s_z (tests/test_calib.py).
 """
 from __future__ import annotations
 
 import copy
+from dataclasses import dataclass, field
 
 import torch
 import torch.nn as nn
@@ -15,86 +29,104 @@ import torch.nn as nn
 from .let import LETQuantizer
 
 
+def _pick(gen: torch.Generator, n: int, k: int, device) -> torch.Tensor:
+    """k row indices in [0, n), drawn with replacement on the generator's device."""
+    return torch.randint(0, n, (k,), generator=gen, device=gen.device).to(device)
+
+
 @torch.no_grad()
-def collect_inputs(model: nn.Module, paths: list[str], obs_fn, n_batches: int = 8,
-                   max_rows: int = 16384, generator: torch.Generator | None = None) -> dict[str, torch.Tensor]:
-    """Inputs of each layer in ``paths`` over ``n_batches`` of ``obs_fn()``
-    (rows subsampled to ``max_rows``), as ``{path: [S, K] fp32}``."""
-    feats: dict[str, list[torch.Tensor]] = {p: [] for p in paths}
-    per = max(1, max_rows // n_batches)
+def record_inputs(model: nn.Module, paths: list[str], obs_fn, n_batches: int, gen: torch.Generator,
+                  max_rows: int = 16384) -> dict[str, torch.Tensor]:
+    """The fp32 input rows each module in ``paths`` sees over ``n_batches`` calls of
+    ``model.act_inference(obs_fn())`` in eval mode, ``{path: [rows, in_features]}``."""
+    budget = max_rows // n_batches
+    seen: dict[str, list[torch.Tensor]] = {p: [] for p in paths}
 
-    def hook(p):
-        def fn(mod, inp, out):
-            x = inp[0].detach().reshape(-1, inp[0].shape[-1])
-            if x.shape[0] > per:
-                idx = torch.randint(0, x.shape[0], (per,), generator=generator,
-                                    device="cpu" if generator is not None else x.device).to(x.device)
-                x = x[idx]
-            feats[p].append(x.float())
-        return fn
+    def recorder(path):
+        def record(module, args, output):
+            rows = args[0].detach().flatten(0, -2)
+            if rows.shape[0] > budget:
+                rows = rows[_pick(gen, rows.shape[0], budget, rows.device)]
+            seen[path].append(rows.float())
+        return record
 
-    hooks = [model.get_submodule(p).register_forward_hook(hook(p)) for p in paths]
-    was = model.training
+    handles = [model.get_submodule(p).register_forward_hook(recorder(p)) for p in paths]
+    training = model.training
     model.eval()
     try:
         with torch.inference_mode():
             for _ in range(n_batches):
                 model.act_inference(obs_fn())
     finally:
-        model.train(was)
-        for h in hooks:
+        for h in handles:
             h.remove()
-    return {p: torch.cat(v, dim=0) for p, v in feats.items()}
+        model.train(training)
+    return {p: torch.cat(rows, dim=0) for p, rows in seen.items()}
 
 
-def fit_let(x: torch.Tensor, linear: nn.Linear, n_steps: int = 200, lr: float = 5e-3,
-            batch_rows: int = 4096, generator: torch.Generator | None = None,
-            verbose: bool = False) -> tuple[torch.Tensor, torch.Tensor, float]:
-    """Fit LET (alpha, beta) for one layer on an fp32 copy; returns (alpha, beta, s_z)."""
-    lin32 = copy.deepcopy(linear).float()
-    for p in lin32.parameters():
-        p.requires_grad_(False)
-    x = x.float()
-    let = LETQuantizer(lin32.in_features).to(x.device)
+@dataclass
+class LetFit:
+    """Result of ``fit_layer``: the transform, the activation scale over all the
+    recorded rows, and the reconstruction loss of every step (when kept)."""
+    alpha: torch.Tensor
+    beta: torch.Tensor
+    s_z: float
+    losses: list[float] = field(default_factory=list)
+
+
+def fit_layer(rows: torch.Tensor, linear: nn.Linear, gen: torch.Generator, steps: int = 200, lr: float = 5e-3,
+              batch_rows: int = 4096, keep_losses: bool = False) -> LetFit:
+    """Fit ``z = alpha * x + beta`` for one Linear on an fp32 copy of it.
+
+    Start from the per-channel statistics of ``rows`` (alpha = 1/std, beta =
+    -mean/std), then ``steps`` Adam steps on MSE(Qw(W') Qa(z) + b', W x + b), each
+    on ``batch_rows`` rows drawn with replacement. ``s_z = absmax(alpha x + beta) / 127``
+    over every row."""
+    target = copy.deepcopy(linear).float().requires_grad_(False)
+    x = rows.float()
+    let = LETQuantizer(target.in_features).to(x.device)
     let.initialize_from_activation(x)
     opt = torch.optim.Adam(let.parameters(), lr=lr)
-    rows = min(batch_rows, x.shape[0])
-    for i in range(n_steps):
-        idx = torch.randint(0, x.shape[0], (rows,), generator=generator,
-                            device="cpu" if generator is not None else x.device).to(x.device)
+    take = min(batch_rows, x.shape[0])
+    losses = []
+    for _ in range(steps):
+        sample = x[_pick(gen, x.shape[0], take, x.device)]
         with torch.enable_grad():
-            _, loss = let.block_reconstruction_loss(x[idx], lin32)
+            loss = let.block_reconstruction_loss(sample, target)[1]
             opt.zero_grad()
             loss.backward()
         opt.step()
-        if verbose and (i + 1) % 50 == 0:
-            print(f"      step {i + 1:4d}  recon_loss={loss.item():.3e}")
-    return let.alpha.detach().clone(), let.beta.detach().clone(), let.calibrate_scale(x)
+        if keep_losses:
+            losses.append(float(loss))
+    return LetFit(let.alpha.detach().clone(), let.beta.detach().clone(), let.calibrate_scale(x), losses)
 
 
-def make_plan(model: nn.Module, paths: list[str], obs_fn=None, use_let: bool = True,
-              n_calib: int = 8, let_steps: int = 200, act_mode: str = "static",
-              verbose: bool = True, seed: int = 0) -> dict[str, dict]:
-    """Capture -> (LET) -> scale -> ``swap.apply`` plan (qrt/calib.py:93-129).
+def make_plan(model: nn.Module, paths: list[str], obs_fn=None, use_let: bool = True, n_calib: int = 8,
+              let_steps: int = 200, act_mode: str = "static", verbose: bool = True,
+              seed: int = 0) -> dict[str, dict]:
+    """The ``swap.apply`` plan for the Linears at ``paths`` (qrt/calib.py:93-129 interface).
 
-    ``use_let=False`` gives the naive PTQ plan (no alpha/beta, s_z = absmax/127);
-    ``act_mode="dynamic_full"`` needs no calibration data at all."""
+    ``use_let=True``: LET per layer (alpha, beta, the calibrated s_z); ``use_let=False``:
+    plain absmax PTQ (s_z = absmax(x) / 127, no transform); ``act_mode="dynamic_full"``
+    needs no calibration data (every scale is computed at run time). ``seed`` seeds the
+    row picks (an extension of the reference signature, whose picks are unseeded)."""
     if act_mode == "dynamic_full":
         return {p: {"s_z": None, "alpha": None, "beta": None, "act_mode": act_mode} for p in paths}
     gen = torch.Generator().manual_seed(int(seed))
-    acts = collect_inputs(model, paths, obs_fn, n_batches=n_calib, generator=gen)
+    recorded = record_inputs(model, paths, obs_fn, n_calib, gen)
     plan: dict[str, dict] = {}
-    for p in paths:
-        lin = model.get_submodule(p)
-        x = acts[p]
-        if use_let:
+    for path in paths:
+        rows = recorded[path]
+        if not use_let:
+            s_z = rows.abs().amax().item() / 127.0
+            plan[path] = {"s_z": s_z, "alpha": None, "beta": None, "act_mode": act_mode}
             if verbose:
-                print(f"  [calib/LET] {p}  (K={lin.in_features}, samples={x.shape[0]})")
-            alpha, beta, s_z = fit_let(x, lin, n_steps=let_steps, generator=gen, verbose=verbose)
-            plan[p] = {"s_z": s_z, "alpha": alpha, "beta": beta, "act_mode": act_mode}
-        else:
-            s_z = x.abs().amax().item() / 127.0
-            if verbose:
-                print(f"  [calib/naive] {p}  s_z={s_z:.4g}")
-            plan[p] = {"s_z": s_z, "alpha": None, "beta": None, "act_mode": act_mode}
+                print(f"[rl_quant_b200] absmax scale of {path}: {s_z:.4g}")
+            continue
+        fit = fit_layer(rows, model.get_submodule(path), gen, steps=let_steps, keep_losses=verbose)
+        plan[path] = {"s_z": fit.s_z, "alpha": fit.alpha, "beta": fit.beta, "act_mode": act_mode}
+        if verbose:
+            first, last = (fit.losses[0], fit.losses[-1]) if fit.losses else (float("nan"),) * 2
+            print(f"[rl_quant_b200] LET of {path}: {rows.shape[0]} rows x {rows.shape[1]}, "
+                  f"loss {first:.3e} -> {last:.3e}, s_z {fit.s_z:.4g}")
     return plan

@@ -1,9 +1,9 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE.
 
-Run in a container that has the reference checkout (default
-/root/reference, override with RLQ_REFERENCE) and no GPU:
+Run in a container that has a checkout of the reference (RLQ_REFERENCE names
+its root; nothing here needs a GPU):
 
-    python tests/golden/make_golden.py
+    RLQ_REFERENCE=<reference checkout> python tests/golden/make_golden.py [--parts ...]
 
 What runs is the reference's own code, unmodified:
   * rsl_rl ``ActorCriticEncoder`` (fp32, seed 0) -- the GLAD model;
@@ -26,6 +26,9 @@ Outputs (numpy .npz, small):
   glad_fwd_b{B}.npz     obs + qrt INT8-path outputs/intermediates (dynamic and
                         static s_z) + the fp32 eager outputs
   glad_conv_b4.npz      conv-chain op inputs/outputs from the Triton kernels
+  glad_calib.npz        qrt ``calib.make_plan`` (seeded global RNG) run on an fp16
+                        copy of this package's GLAD module: the LET alpha/beta and
+                        s_z of every INT8 path, for tests/test_calib.py
 """
 from __future__ import annotations
 
@@ -34,7 +37,9 @@ import sys
 import types
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = os.environ.get("RLQ_REFERENCE", "/root/reference")
+REF = os.environ.get("RLQ_REFERENCE")
+if not REF:
+    raise SystemExit("set RLQ_REFERENCE to the root of a checkout of the reference (RL_Quant)")
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
@@ -111,8 +116,39 @@ def to_np(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().contiguous().numpy()
 
 
-def main():
+# the calibration golden: qrt's make_plan on the package's own GLAD module
+CALIB_SEED, CALIB_OBS_SEED, CALIB_BATCHES, CALIB_ROWS, CALIB_STEPS = 77, 11, 2, 64, 25
+
+
+def calib_golden():
+    """Run qrt ``calib.make_plan`` with torch's global RNG seeded by CALIB_SEED on an
+    fp16 copy of ``build_glad(seed=0, critic_seed=2)`` (equal to the reference model,
+    checked in main), CALIB_BATCHES batches of CALIB_ROWS observations, LET with
+    CALIB_STEPS Adam steps, dynamic act mode; save every path's alpha, beta, s_z."""
+    model = build_glad(seed=0, critic_seed=2).half().eval()
+    obs = glad_obs(CALIB_BATCHES * CALIB_ROWS, seed=CALIB_OBS_SEED).half()
+    batches = [{"policy_obs": obs[i * CALIB_ROWS:(i + 1) * CALIB_ROWS]} for i in range(CALIB_BATCHES)]
+    it = iter(batches)
+    torch.manual_seed(CALIB_SEED)
+    plan = calib.make_plan(model, INT8_PATHS, obs_fn=lambda: next(it), n_calib=CALIB_BATCHES, use_let=True,
+                           let_steps=CALIB_STEPS, act_mode="dynamic", verbose=False)
+    out = {"meta.seed": np.int64(CALIB_SEED), "meta.obs_seed": np.int64(CALIB_OBS_SEED),
+           "meta.batches": np.int64(CALIB_BATCHES), "meta.rows": np.int64(CALIB_ROWS),
+           "meta.steps": np.int64(CALIB_STEPS)}
+    for p in INT8_PATHS:
+        out[f"{p}.alpha"] = to_np(plan[p]["alpha"])
+        out[f"{p}.beta"] = to_np(plan[p]["beta"])
+        out[f"{p}.s_z"] = np.float64(plan[p]["s_z"])
+    np.savez_compressed(os.path.join(HERE, "glad_calib.npz"), **out)
+    print(f"[golden] qrt make_plan (seed {CALIB_SEED}) on the package GLAD module: {list(plan)}")
+
+
+def main(parts):
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if "calib" in parts:
+        calib_golden()
+    if not parts & {"weights", "fwd", "conv"}:
+        return
     m32 = build_reference_model()
     # The package's own GLAD module must reproduce the same initialisation.
     mine = build_glad(seed=0, critic_seed=2)
@@ -212,4 +248,9 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--parts", default="weights,fwd,conv,calib",
+                    help="comma-separated subset of weights,fwd,conv,calib (weights, fwd and conv "
+                         "are written together)")
+    main(set(ap.parse_args().parts.split(",")))
