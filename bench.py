@@ -71,6 +71,78 @@ def rank_info():
 
 
 # ---------------------------------------------------------------------------------------------
+def _node_of_cpus(cpus) -> list[int]:
+    """NUMA nodes holding any of `cpus` (from /sys/devices/system/node)."""
+    nodes = []
+    base = "/sys/devices/system/node"
+    try:
+        names = sorted(n for n in os.listdir(base) if n.startswith("node") and n[4:].isdigit())
+    except OSError:
+        return nodes
+    for n in names:
+        try:
+            spec = open(os.path.join(base, n, "cpulist")).read().strip()
+        except OSError:
+            continue
+        cs = set()
+        for part in spec.split(","):
+            if "-" in part:
+                a, b = part.split("-")
+                cs.update(range(int(a), int(b) + 1))
+            elif part:
+                cs.add(int(part))
+        if cs & set(cpus):
+            nodes.append(int(n[4:]))
+    return nodes
+
+
+def host_link(device, nbytes: int, barrier, world: int, rank: int, reps: int = 10) -> dict:
+    """Where this rank's host buffers and GPU sit, and the host->device copy rate of one
+    step's observations (`nbytes` from pinned memory): with the other ranks idle (ranks
+    take turns) and with every rank copying at once."""
+    import torch.distributed as dist
+
+    info = {"rank": rank}
+    try:
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        info["gpu_pci"] = bus
+        info["gpu_numa"] = int(open(f"/sys/bus/pci/devices/{bus}/numa_node").read().strip())
+    except Exception:  # noqa: BLE001
+        pass
+    try:
+        info["cpu_numa"] = _node_of_cpus(sorted(os.sched_getaffinity(0)))
+    except Exception:  # noqa: BLE001
+        pass
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dst.copy_(src, non_blocking=True)
+
+    def rate():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        return nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9
+
+    alone = None
+    for r in range(world):
+        barrier()
+        if r == rank:
+            alone = rate()
+    barrier()
+    info["h2d_alone_gbs"] = alone
+    info["h2d_concurrent_gbs"] = rate()
+    barrier()
+    if world > 1:
+        out = [None] * world
+        dist.all_gather_object(out, info)
+        return {"ranks": out}
+    return {"ranks": [info]}
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples of one GPU while the timed work runs."""
 
@@ -436,6 +508,7 @@ def run_ours(args):
 
     e2e_value = time_e2e(2)
     e2e_serial = time_e2e(1)
+    links = host_link(device, B * OBS_BYTES_PER_ENV, barrier, world, rank)
     runner = InferenceRunner(infer, mode="manual-graph", with_critic=True)
 
     # per-iteration weight hand-over: W += 1e-3 N(0,1) on the fp32 master (rank 0,
@@ -481,6 +554,8 @@ def run_ours(args):
             pass
         hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
         peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+        tensor_peak = float(peaks.get("bf16_tflops", 1590.0))
+        tensor_src = ("measured dense bf16 burst" if "bf16_tflops" in peaks else "fallback dense bf16")
         dom = max(range(len(stage_names)), key=lambda i: stage_ms[i])
         dom_name = stage_names[dom]
         alg_bytes = {"front": OBS_BYTES_PER_ENV * B}.get(dom_name)
@@ -524,6 +599,12 @@ def run_ours(args):
             "forward_roofline": {"bytes_per_env": BYTES_PER_ENV_FWD, "achieved_gbs": fwd_gbs,
                                  "frac_hbm": fwd_gbs / hbm_peak, "macs_per_env": MACS_PER_ENV,
                                  "achieved_tops": tops},
+            # the forward's 2.55 M MAC per environment (2.02 M int8, 0.53 M fp16) as op/s against the
+            # measured dense bf16 GEMM peak (the int8 dense peak is nominally twice that)
+            "tensor_roofline": {"achieved": tops, "unit": "TOP/s", "peak": tensor_peak,
+                                "frac": tops / tensor_peak if tensor_peak else None,
+                                "peak_source": tensor_src},
+            "host_links": links["ranks"],
             "stage_ms": dict(zip(stage_names, stage_ms)),
             "actor_critic": {"value": ac_value, "unit": UNIT, "ms_per_step": ms_ac / k_ac,
                              "workload": f"actor + critic forward, B={B} per GPU, {world * B} envs" +

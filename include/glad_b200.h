@@ -272,6 +272,17 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
                         const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Train-mode glad_critic_forward: the critic head's Gumbel term of the top-k
+ * logits drawn inside the kernel (Philox4x32-10, the layout of
+ * glad_actor_forward_train) instead of read from memory, as the reference's
+ * train-mode critic draws its own (qrt/integration.py:212-216,
+ * qrt/encoder_opt.py:87-91); the call adds one to the device word
+ * *gumbel_offset. value_out NULL runs the encoder only (aux->encoded set).   */
+int glad_critic_forward_train(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
+                              int64_t ld_obs, int act_mode, uint64_t gumbel_seed,
+                              unsigned long long* gumbel_offset, float* value_out, const GladActorAux* aux,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Diagnostics: record CUDA events (cudaEvent_t, passed as void*) between the
  * stages of the following glad_actor_forward calls on this host thread:
  * events[0] before the first launch, then one after each stage (absmax, front,
@@ -407,6 +418,25 @@ typedef struct GladQCNNSrc {
   const float* beta;      /* [16] or NULL */
 } GladQCNNSrc;
 int glad_requant_qcnn(const GladQCNNSrc* src, void* stream);
+
+/* ---- weight hand-over across GPUs -------------------------------------------
+ * After the PPO update one rank refreshes its inference copy (sync_weights_from,
+ * qrt/runtime.py:224-271); the other ranks receive it in ONE collective when
+ * every tensor the forward reads lives in one contiguous device blob. An item is
+ * one tensor: its device address and size; glad_pack_layout assigns the offsets
+ * (item i at the first 256-byte boundary after item i-1, item 0 at 0) and
+ * returns the blob size. glad_pack_weights copies the tensors into the blob,
+ * glad_unpack_weights copies them back out (one launch each per 128 items);
+ * the broadcast itself is the caller's (NCCL). No counterpart in the
+ * reference, which runs on one GPU.                                         */
+typedef struct GladPackItem {
+  void* tensor;         /* device address of the tensor                     */
+  size_t nbytes;        /* its size in bytes                                */
+  size_t offset;        /* its place in the blob (set by glad_pack_layout)   */
+} GladPackItem;
+size_t glad_pack_layout(GladPackItem* items, int n);
+int glad_pack_weights(const GladPackItem* items, int n, void* blob, size_t blob_bytes, void* stream);
+int glad_unpack_weights(const GladPackItem* items, int n, const void* blob, size_t blob_bytes, void* stream);
 
 /* The cast-copy half of sync_weights_from (qrt/runtime.py:251-253): n
  * element-wise copies with dtype conversion in one launch.                  */

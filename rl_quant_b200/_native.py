@@ -85,6 +85,10 @@ class GladW4Linear(Structure):
                 ("out_features", c_int)]
 
 
+class GladPackItem(Structure):
+    _fields_ = [("tensor", c_void_p), ("nbytes", c_size_t), ("offset", c_size_t)]
+
+
 class GladCastCopy(Structure):
     _fields_ = [("src", c_void_p), ("dst", c_void_p), ("n", c_int64), ("src_dtype", c_int32),
                 ("dst_dtype", c_int32)]
@@ -119,6 +123,12 @@ SIGNATURES = {
     "glad_ppo_epilogue": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int, c_uint64, c_void_p, c_void_p,
                                   c_int64, c_void_p, c_void_p, c_void_p]),
     "glad_critic_workspace_size": (c_size_t, [c_int64]),
+    "glad_critic_forward_train": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
+                                          c_uint64, c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t,
+                                          c_void_p]),
+    "glad_pack_layout": (c_size_t, [POINTER(GladPackItem), c_int]),
+    "glad_pack_weights": (c_int, [POINTER(GladPackItem), c_int, c_void_p, c_size_t, c_void_p]),
+    "glad_unpack_weights": (c_int, [POINTER(GladPackItem), c_int, c_void_p, c_size_t, c_void_p]),
     "glad_critic_forward": (c_int, [POINTER(GladCriticWeights), c_void_p, c_int, c_int64, c_int64, c_int,
                                     c_void_p, c_void_p, POINTER(GladActorAux), c_void_p, c_size_t, c_void_p]),
     "glad_actor_forward_noalloc": (c_int, [POINTER(GladActorWeights), c_void_p, c_int, c_int64, c_int64, c_int,

@@ -19,6 +19,8 @@ size_t tail_smem_bytes();
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl = false);
 int tail_grid(int64_t B, int sms);
 int front_fused_blocks_per_sm();
+bool front_ws_usable();
+cudaError_t launch_front_ws(const FrontParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_chain(const FrontParams& p, int grid, cudaStream_t st);
 cudaError_t launch_w4mlp(const GladW4Linear (&L)[4], const __half* x, int64_t M, int64_t ldx, float* mean,
                          int64_t ldm, unsigned int* status, cudaStream_t st, bool pdl);
@@ -172,6 +174,16 @@ struct ActorWs {
 };
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// The warp-specialised front (one CTA per SM) can serve the actor forward without an
+// observation normaliser and outside the shared-scan actor + critic call; it is
+// opt-in (GLAD_FRONT_WS=1) until it beats the pipelined front kernel.
+bool use_front_ws(bool dual, bool norm) {
+  if (dual || norm) return false;
+  const char* env = getenv("GLAD_FRONT_WS");
+  if (!(env && env[0] == '1')) return false;
+  return front_ws_usable();
+}
 
 bool use_fused_mlp(int64_t B, int act_mode, cudaStream_t st) {
   const char* env = getenv("GLAD_MLP_FUSED");
@@ -516,7 +528,8 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
   GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsClearBytes, st), "workspace reset");
   // Dynamic s_z of the proprio embedding: reduced inside the front kernel (grid
   // barrier) when its whole grid fits on the device at once, else by a separate pass.
-  const int front_per_sm = front_fused_blocks_per_sm();
+  const bool ws_front = use_front_ws(dual != nullptr, nm.mean != nullptr);
+  const int front_per_sm = ws_front ? 1 : front_fused_blocks_per_sm();
   const bool pe_absmax_in_front = act_mode == GLAD_ACT_DYNAMIC && front_per_sm > 0;
   const int fgrid = front_grid(B, d, front_per_sm > 0 && front_per_sm < 2 ? front_per_sm : 2);
   const bool front_pdl = act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front;
@@ -561,7 +574,8 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
     fp.enc_c = dual->enc_c;
     fp.pe_c_out = dual->pe_c;
   }
-  GLAD_CHECK_CUDA(launch_front<kModeFront>(fp, fgrid, st, front_pdl), "front launch");
+  GLAD_CHECK_CUDA(ws_front ? launch_front_ws(fp, fgrid, st, front_pdl) : launch_front<kModeFront>(fp, fgrid, st, front_pdl),
+                  "front launch");
   stage_mark(2, st);
 
   TailParams tp{};
@@ -686,11 +700,11 @@ size_t glad_critic_workspace_size(int64_t B) {
   return actor_ws(nullptr, B < 0 ? 0 : B, kCriticEnc).bytes;
 }
 
-int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
-                        int64_t ld_obs, int act_mode, const float* topk_noise, float* value_out,
-                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
+namespace {
+int critic_forward_impl(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
+                        int64_t ld_obs, int act_mode, const float* topk_noise, const GumbelArgs* gumbel,
+                        float* value_out, const GladActorAux* aux, void* workspace, size_t workspace_bytes,
                         void* stream) {
-  g_err[0] = 0;
   if (!w) return fail(GLAD_ERR_INVALID_ARG, "weights are NULL");
   if (B < 0) return fail(GLAD_ERR_INVALID_ARG, "B must be >= 0");
   if (act_mode != GLAD_ACT_STATIC && act_mode != GLAD_ACT_DYNAMIC)
@@ -711,7 +725,9 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   if (P <= 0 || P > 104) return fail(GLAD_ERR_INVALID_ARG, "critic proprio width %d outside [1, 104]", P);
   if (ld_obs < P + kMap) return fail(GLAD_ERR_INVALID_ARG, "ld_obs %lld < %d", (long long)ld_obs, P + kMap);
   if (B == 0) return GLAD_OK;
-  if (!obs || !value_out) return fail(GLAD_ERR_INVALID_ARG, "obs and value_out must be set");
+  if (!obs) return fail(GLAD_ERR_INVALID_ARG, "obs must be set");
+  if (!value_out && !(aux && aux->encoded))
+    return fail(GLAD_ERR_INVALID_ARG, "encoder-only call (value_out NULL) needs aux->encoded");
   if (!aligned(obs, obs_dtype == GLAD_DTYPE_F32 ? 4 : 2))
     return fail(GLAD_ERR_INVALID_ARG, "obs is not element-aligned");
   if ((rc = check_conv(&w->conv, true, true))) return rc;
@@ -791,6 +807,10 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   tp.a0_absmax = 0;                 // the critic MLP is fp16: no scale to reduce
   tp.qp_slot = 1;
   tp.noise = topk_noise;
+  tp.gumbel = gumbel ? 1 : 0;
+  tp.gumbel_seed = gumbel ? gumbel->seed : 0;
+  tp.gumbel_offset = gumbel ? gumbel->offset : nullptr;
+  tp.done_slot = kSlotTailDone;
   tp.act_mode = act_mode;
   tp.ld_enc = kCriticEnc;
   tp.prop_dim = P;
@@ -806,13 +826,35 @@ int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dty
   GLAD_CHECK_CUDA(launch_tail(tp, tail_grid(B, d.sms), st, true), "tail launch");
 
   // fp16 critic MLP: one cluster kernel (fp16 activations, tcgen05 kind::f16)
-  {
+  if (value_out) {
     GladLinear16 L[4] = {w->mlp[0], w->mlp[1], w->mlp[2], w->mlp[3]};
     GLAD_CHECK_CUDA(launch_f16mlp(L, enc, B, kCriticEnc, value_out, 1,
                                   reinterpret_cast<unsigned int*>(&ws.slots[kSlotStatus]), st, true),
                     "critic MLP launch");
   }
   return GLAD_OK;
+}
+}  // namespace
+
+int glad_critic_forward(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
+                        int64_t ld_obs, int act_mode, const float* topk_noise, float* value_out,
+                        const GladActorAux* aux, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  g_err[0] = 0;
+  return critic_forward_impl(w, obs, obs_dtype, B, ld_obs, act_mode, topk_noise, nullptr, value_out, aux,
+                             workspace, workspace_bytes, stream);
+}
+
+int glad_critic_forward_train(const GladCriticWeights* w, const void* obs, int obs_dtype, int64_t B,
+                              int64_t ld_obs, int act_mode, uint64_t gumbel_seed,
+                              unsigned long long* gumbel_offset, float* value_out, const GladActorAux* aux,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!gumbel_offset) return fail(GLAD_ERR_INVALID_ARG, "gumbel_offset (device word) must be set");
+  if (!aligned(gumbel_offset, 8)) return fail(GLAD_ERR_INVALID_ARG, "gumbel_offset must be 8-byte aligned");
+  const GumbelArgs g{gumbel_seed, gumbel_offset};
+  return critic_forward_impl(w, obs, obs_dtype, B, ld_obs, act_mode, nullptr, &g, value_out, aux, workspace,
+                             workspace_bytes, stream);
 }
 
 namespace {
@@ -895,7 +937,8 @@ int glad_actor_kernel_count(int64_t B, int act_mode) {
   int rc = device_info(&d);
   if (rc) return rc;
   if (B == 0) return 0;
-  const bool absmax_pass = act_mode == GLAD_ACT_DYNAMIC && front_fused_blocks_per_sm() <= 0;
+  const bool absmax_pass =
+      act_mode == GLAD_ACT_DYNAMIC && !use_front_ws(false, false) && front_fused_blocks_per_sm() <= 0;
   return 2 + (absmax_pass ? 1 : 0) + (use_fused_mlp(B, act_mode, 0) ? 1 : 4);
 }
 

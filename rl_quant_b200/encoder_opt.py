@@ -6,9 +6,9 @@ The patched ``_encode_terrain`` is the reference's algebraic rewrite
     product over the local features; the query half is a per-env scalar;
   * the multi-head attention is a single-query attention written out.
 
-Without autograd it runs the fused sm_100a encoder (glad_actor_forward in
-encoder-only mode): conv chain, pooling, query, top-32, attention, in three
-kernels. With autograd (PPO update) it runs the same rewrite in float torch
+Without autograd it runs the fused sm_100a encoder in encoder-only mode
+(glad_actor_forward for the actor observation group, glad_critic_forward for
+the critic group): conv chain, pooling, query, top-32, attention. With autograd (PPO update) it runs the same rewrite in float torch
 ops on the model's own parameters, as the reference does.
 """
 from __future__ import annotations
@@ -19,7 +19,7 @@ import warnings
 import torch
 import torch.nn.functional as F
 
-from .fused import FusedActor
+from .fused import FusedActor, FusedCritic
 
 
 def _encode_terrain_float(self, obs):
@@ -74,13 +74,20 @@ def _encode_terrain_opt(self, obs):
     if torch.is_grad_enabled():
         return _encode_terrain_float(self, obs)
     n_map = self.L * self.W * self.coord_dim
-    if obs.shape[1] - n_map != self.actor_proprio_dim:
-        # critic-width observations: not on the fused path yet
-        raise NotImplementedError("the fused encoder handles the actor observation group")
-    fused = self.__dict__.get("_glad_fused")
+    P = obs.shape[1] - n_map
+    # the group picks its embedding by its proprio width (qrt/encoder_opt.py:57-66;
+    # the actor's when both widths agree, rsl_rl actor_critic_encoder.py:226-229)
+    if P == self.actor_proprio_dim:
+        key, make = "_glad_fused", lambda: FusedActor(self, need_mlp=False)
+    elif P == self.critic_proprio_dim:
+        key, make = "_glad_fused_critic", lambda: FusedCritic(self, need_mlp=False)
+    else:
+        raise ValueError(f"proprio dim {P} matches neither actor({self.actor_proprio_dim}) "
+                         f"nor critic({self.critic_proprio_dim})")
+    fused = self.__dict__.get(key)
     if fused is None:
-        fused = FusedActor(self, need_mlp=False)
-        self.__dict__["_glad_fused"] = fused
+        fused = make()
+        self.__dict__[key] = fused
     noise = _gumbel_noise((obs.shape[0], 187), obs.device) if self.training else None
     return fused.encode(obs, noise)
 

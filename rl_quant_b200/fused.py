@@ -187,13 +187,14 @@ class FusedCritic:
     """The fused critic forward (``glad_critic_forward``) of one GLAD inference
     copy: shared encoder, critic proprio embedding, fp16 critic MLP."""
 
-    def __init__(self, model: nn.Module):
+    def __init__(self, model: nn.Module, need_mlp: bool = True):
         self.model = model
+        self.need_mlp = need_mlp
         if not isinstance(model.map_cnn, QuantCNN):
             raise FusedUnsupported("map_cnn is not a QuantCNN (swap_cnn first)")
         if not isinstance(model.query_projector, QuantLinear):
             raise FusedUnsupported("query_projector is not a QuantLinear")
-        for p in ("critic.0", "critic.2", "critic.4", "critic.6"):
+        for p in ("critic.0", "critic.2", "critic.4", "critic.6") if need_mlp else ():
             layer = model.get_submodule(p)
             if type(layer) is not nn.Linear:
                 raise FusedUnsupported(f"{p} must be an fp16 nn.Linear (the critic MLP is not quantised)")
@@ -230,6 +231,10 @@ class FusedCritic:
         w.mha_out_b = _fp16(m.mha.out_proj.bias, "mha.out_proj.bias").data_ptr()
         for i, p in enumerate(("critic.0", "critic.2", "critic.4", "critic.6")):
             L = m.get_submodule(p)
+            if not isinstance(L, nn.Linear):
+                if self.need_mlp:
+                    raise FusedUnsupported(f"{p} must be an fp16 nn.Linear")
+                continue
             w.mlp[i] = N.GladLinear16(_fp16(L.weight, f"{p}.weight").data_ptr(),
                                       N.ptr(_fp16(L.bias, f"{p}.bias")) if L.bias is not None else None,
                                       L.in_features, L.out_features)
@@ -239,23 +244,56 @@ class FusedCritic:
         """As FusedActor.check_status, for the critic's workspaces."""
         check_workspaces(self._ws, "fused critic")
 
-    def run(self, obs: torch.Tensor, value: torch.Tensor, noise: torch.Tensor | None = None,
-            obs_norm=None) -> None:
-        """``obs_norm``: an EmpiricalNormalization applied to the f32 rows as they load."""
+    def run(self, obs: torch.Tensor, value: torch.Tensor | None, noise: torch.Tensor | None = None,
+            obs_norm=None, gumbel: tuple | None = None, aux: N.GladActorAux | None = None) -> None:
+        """Launch the fused critic forward on the current stream (no host sync).
+
+        ``noise``: f32 [B,187] added to the top-k logits; ``gumbel = (seed, offset)`` instead
+        draws the train-mode Gumbel term inside the kernel (``offset``: one-element int64
+        device tensor, advanced by one per call). ``obs_norm``: an EmpiricalNormalization
+        applied to the f32 rows as they load. ``value`` None runs the encoder only (``aux``
+        must then receive ``encoded``)."""
         N.require_cuda(obs)
         if obs.dim() != 2 or obs.stride(1) != 1:
             raise ValueError("obs must be a row-major [B, P+2079] tensor")
+        if noise is not None and gumbel is not None:
+            raise ValueError("pass either noise or gumbel")
         B = obs.shape[0]
         key = (B, str(obs.device))
         ws = self._ws.get(key)
         if ws is None:
             ws = torch.zeros(N.load().glad_critic_workspace_size(B), dtype=torch.uint8, device=obs.device)
             self._ws[key] = ws
+        dt = N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16
+        if gumbel is not None:
+            seed, offset = gumbel
+            N.require_cuda(offset)
+            if offset.dtype != torch.int64 or offset.numel() != 1:
+                raise ValueError("gumbel offset must be a one-element int64 CUDA tensor")
+            rc = N.load().glad_critic_forward_train(
+                self.weights(obs_norm), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode],
+                int(seed) & 0xFFFFFFFFFFFFFFFF, offset.data_ptr(), N.ptr(value), aux, ws.data_ptr(), ws.numel(),
+                N.stream_handle(obs.device))
+            N.check(rc, "glad_critic_forward_train")
+            return
         rc = N.load().glad_critic_forward(
-            self.weights(obs_norm), obs.data_ptr(), N.DTYPE_F32 if obs.dtype == torch.float32 else N.DTYPE_F16,
-            B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise), value.data_ptr(), None,
-            ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
+            self.weights(obs_norm), obs.data_ptr(), dt, B, obs.stride(0), N.ACT_MODES[self.act_mode], N.ptr(noise),
+            N.ptr(value), aux, ws.data_ptr(), ws.numel(), N.stream_handle(obs.device))
         N.check(rc, "glad_critic_forward")
+
+    def encode(self, obs: torch.Tensor, noise: torch.Tensor | None = None):
+        """``_encode_terrain`` outputs for critic-width observations: (encoded [B,128+P]
+        fp16, attn_weights [B,1,32], topk_indices [B,32] int64, gc_weights [B,187,1])."""
+        B, dev = obs.shape[0], obs.device
+        enc = torch.empty(B, 232, dtype=torch.float16, device=dev)
+        attn = torch.empty(B, 1, 32, dtype=torch.float16, device=dev)
+        idx = torch.empty(B, 32, dtype=torch.int64, device=dev)
+        gcw = torch.empty(B, 187, 1, dtype=torch.float16, device=dev)
+        aux = N.GladActorAux()
+        aux.encoded, aux.attn_weights, aux.topk_idx, aux.gc_weights = (
+            enc.data_ptr(), attn.data_ptr(), idx.data_ptr(), gcw.data_ptr())
+        self.run(obs, None, noise, aux=aux)
+        return enc[:, :128 + self.P].contiguous(), attn, idx, gcw
 
 
 class FusedActorCritic:

@@ -23,7 +23,6 @@ import torch
 import torch.nn as nn
 
 from . import _native as N
-from .encoder_opt import _gumbel_noise
 from .fused import FusedActor, FusedActorCritic, FusedCritic, FusedUnsupported, ppo_epilogue
 from .qconv import QuantCNN
 from .qlinear import QuantLinear
@@ -174,8 +173,8 @@ class InferenceRunner:
         c = self._apply_norm(getattr(m, "critic_obs_normalizer", None), co) if self.normalize else co
         if self._fused_critic is not None and co.shape[1] == self._fused_critic.P + 2079:
             value = torch.empty(co.shape[0], 1, dtype=torch.float32, device=co.device)
-            noise = _gumbel_noise((co.shape[0], 187), co.device) if m.training else None
-            self._fused_critic.run(c, value, noise)
+            # train-mode rollouts: the critic's Gumbel term is drawn in the kernel too
+            self._fused_critic.run(c, value, gumbel=self._gumbel_state(co.device) if m.training else None)
             return value
         enc_fn = getattr(m, "_encode_terrain_orig", None) if co.shape[1] - 2079 != getattr(
             m, "actor_proprio_dim", -1) else None
@@ -236,8 +235,7 @@ class InferenceRunner:
         else:
             # normalised groups differ in their scans: each head loads (and normalises) its own
             self._fused.run(po, mean, gumbel=self._gumbel_state(dev) if train else None, obs_norm=an)
-            noise = _gumbel_noise((B, 187), dev) if train else None
-            self._fused_critic.run(co, value, noise, obs_norm=cn)
+            self._fused_critic.run(co, value, obs_norm=cn, gumbel=self._gumbel_state(dev) if train else None)
         if self._ppo_rng is None or self._ppo_rng.device != dev:
             self._ppo_rng = torch.zeros(2, dtype=torch.int64, device=dev)
         ppo_epilogue(mean, std_fn(), self._ppo_seed, self._ppo_rng, actions, log_prob, sigma)

@@ -31,22 +31,32 @@ def _tensors(model: nn.Module, include_params: bool):
             yield mod, n, b, False
 
 
+def pack_layout(sizes: list[int]) -> tuple[list[int], int]:
+    """Offsets of tensors of `sizes` bytes in the blob and its size: each tensor at the
+    first 256-byte boundary after the previous one (the rule of glad_pack_layout)."""
+    offs, off = [], 0
+    for n in sizes:
+        offs.append(off)
+        off += (n + _ALIGN - 1) // _ALIGN * _ALIGN
+    return offs, max(off, _ALIGN)
+
+
 class PackedWeights:
     def __init__(self, model: nn.Module, include_params: bool = True):
         items = []
         seen = set()
-        off = 0
         for mod, name, t, is_param in _tensors(model, include_params):
             if t.data_ptr() in seen:
                 continue
             seen.add(t.data_ptr())
-            nbytes = t.numel() * t.element_size()
-            items.append((mod, name, t, is_param, off, nbytes))
-            off += (nbytes + _ALIGN - 1) // _ALIGN * _ALIGN
+            items.append((mod, name, t, is_param))
+        offs, off = pack_layout([t.numel() * t.element_size() for _, _, t, _ in items])
+        items = [(mod, name, t, is_param, o, t.numel() * t.element_size())
+                 for (mod, name, t, is_param), o in zip(items, offs)]
         if not items:
             raise ValueError("nothing to pack")
         device = items[0][2].device
-        self.blob = torch.zeros(max(off, _ALIGN), dtype=torch.uint8, device=device)
+        self.blob = torch.zeros(off, dtype=torch.uint8, device=device)
         self.entries = []
         with torch.no_grad():
             for mod, name, t, is_param, o, nbytes in items:

@@ -76,3 +76,22 @@ def test_packing_single_process_keeps_values():
                                 if not k.endswith("num_batches_tracked"))
     y = m.act_inference(torch.randn(2, 2175))[0]   # the module still runs on the packed storage
     assert y.shape == (2, 29)
+
+
+def test_pack_layout_matches_the_c_abi():
+    """The blob layout the Python packer uses is the one glad_pack_layout computes."""
+    from rl_quant_b200 import _native as N
+    from rl_quant_b200.weight_sync import pack_layout
+
+    sizes = [1, 255, 256, 257, 0, 4096, 3, 512 * 224]
+    items = (N.GladPackItem * len(sizes))(*[N.GladPackItem(None, n, 7) for n in sizes])
+    total = N.load().glad_pack_layout(items, len(sizes))
+    offs, tot = pack_layout(sizes)
+    assert [it.offset for it in items] == offs and total == tot
+    assert all(o % 256 == 0 for o in offs)
+    # a rejected item: off the layout (the tensor addresses are never dereferenced here)
+    for it in items:
+        it.tensor = 0x1000
+    items[1].offset = 100
+    rc = N.load().glad_pack_weights(items, len(sizes), None, total, None)
+    assert rc == N.GLAD_ERR_INVALID_ARG and b"256-byte layout" in N.load().glad_last_error()
