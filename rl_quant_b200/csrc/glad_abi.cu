@@ -175,13 +175,13 @@ struct ActorWs {
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// The warp-specialised front (one CTA per SM) can serve the actor forward without an
-// observation normaliser and outside the shared-scan actor + critic call; it is
-// opt-in (GLAD_FRONT_WS=1) until it beats the pipelined front kernel.
+// The warp-specialised front (one CTA per SM) serves the actor forward without an
+// observation normaliser and outside the shared-scan actor + critic call; both fronts
+// give identical results. GLAD_FRONT_WS=0 selects the pipelined front kernel.
 bool use_front_ws(bool dual, bool norm) {
   if (dual || norm) return false;
   const char* env = getenv("GLAD_FRONT_WS");
-  if (!(env && env[0] == '1')) return false;
+  if (env && env[0] == '0') return false;
   return front_ws_usable();
 }
 

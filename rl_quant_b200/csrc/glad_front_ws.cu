@@ -14,12 +14,14 @@
 //   warp 0      observation rows -> stage ring (one bulk copy per row body)
 //   warps 1-2   conv1 MMAs (tile 0 / tile 1)           warp 3  conv2 MMAs
 //   warp 4      logits MMAs                            warp 5  pooling MMAs
-//   warps 6-7   stage -> fp16 conv1 planes (ragged row ends from global memory)
+//   warps 6-7   stage -> fp16 conv1 planes
 //   warps 8-11  conv1 epilogue: TMEM -> z8 -> conv2 strip and z8 (global)
 //   warps 12-19 conv2 epilogue: TMEM -> fp16 local-feature tiles
-//   warps 20-23 int8 proprio embedding of all the CTA's environments (one batched
-//               GEMM after the proprio-absmax grid barrier), then per environment
-//               the logits -> softmax -> pooling weights, and the pooled gc
+//   warps 20-27 two groups of four; group g takes the environments i = g, g+2, ...:
+//               per step the logits -> softmax -> pooling weights of i and the pooled
+//               gc of i-2 (whose pooling MMAs ran meanwhile); group 0 first computes
+//               the int8 proprio embedding of all the CTA's environments (one batched
+//               GEMM after the proprio-absmax grid barrier)
 //
 // The operand layouts, descriptors and epilogue arithmetic are those of the
 // pipelined front kernel (front_layout.cuh, glad_front.cu): identical integers and
@@ -34,14 +36,15 @@
 namespace glad {
 
 namespace ws {
-constexpr int kWarps = 24;
+constexpr int kWarps = 28;
 constexpr int kThreads = kWarps * 32;
 constexpr int kLoad = 0, kMma1 = 1, kMma2 = 3, kMmaLg = 4, kMmaPl = 5;
-constexpr int kCvt = 6, kCvtThreads = 64;     // warps 6-7
+constexpr int kCvt = 6, kCvtWarps = 2, kCvtThreads = 32 * kCvtWarps;   // warps 6-7
+constexpr int kNLocal = 3;                    // local-feature tiles in flight
 constexpr int kEpi1 = 8;                      // warps 8-11
 constexpr int kEpi2 = 12;                     // warps 12-19
-constexpr int kSoft = 20;                     // warps 20-23
-constexpr int kBarSoft = 2;                   // named barrier of the softmax warps
+constexpr int kSoft = 20;                     // warps 20-27: two groups of four, alternate environments
+constexpr int kBarSoft = 2;                   // named barriers 2 and 3: one per softmax group
 // TMEM columns (512 allocated): conv2 [0,256) buffer b at 128b, tile t at +64t; conv1
 // [256,320) buffer b at +32b, tile t at +16t; logits [320,384) likewise; pooling
 // [384,448) buffer b at +32b, K half h at +16h; batched proprio embedding [448,512)
@@ -52,7 +55,7 @@ constexpr int kPeABytes = 8 * 2048;               // proprio A tile [16-byte K c
 }  // namespace ws
 
 struct __align__(128) WsSmem {
-  alignas(128) uint8_t local16[2][ws::kLocalBytes];
+  alignas(128) uint8_t local16[ws::kNLocal][ws::kLocalBytes];
   alignas(128) uint8_t pe_a[ws::kPeABytes];   // also the raw conv weights during the set-up
   alignas(128) uint8_t bpool[2][16 * 16 * 16];
   alignas(128) uint8_t blog[8 * 16 * 16];
@@ -72,19 +75,20 @@ struct __align__(128) WsSmem {
   float pe_la[kMaxProp], pe_lb[kMaxProp];     // proprio embedding LET alpha / beta
   float pe_scale[64], pe_bp[64];
   float qp_a[128], qp_b[128];                 // query projector LET (absmax of its input)
-  float poolv[128];
-  float red[8];                               // softmax warps: maxima [0,4), sums [4,8)
+  float poolv[2][128];                        // [softmax group]
+  float red[2][12];                           // [softmax group]: maxima [0,4), sums of tile 0 [4,8), tile 1 [8,12)
   float wmax[ws::kWarps];
   uint64_t c1_adesc[2][16];                   // [planes buffer][tile*8 + K-step]
   uint64_t c1_bdesc[8];
   uint64_t c2_adesc[2][10];                   // [strip buffer][tile*5 + K-step]
   uint64_t c2_bdesc[5];
-  uint64_t lg_adesc[2][2][4];                 // [local buffer][tile][K-step]
+  uint64_t lg_adesc[ws::kNLocal][2][4];       // [local buffer][tile][K-step]
   uint64_t lg_bdesc[4];
-  uint64_t pl_adesc[2][8];                    // [local buffer][K-step]
+  uint64_t pl_adesc[ws::kNLocal][8];          // [local buffer][K-step]
   uint64_t pl_bdesc[2][8];                    // [pooling-weight buffer][K-step]
   uint64_t stage_full[2], stage_empty[2], planes_full[2], c1_full[2], c1_empty[2], strip_full[2];
-  uint64_t c2_full[2], c2_empty[2], local_full[2], lg_full[2], lg_empty[2], pw_full[2];
+  uint64_t c2_full[2], c2_empty[2], lg_full[2], lg_empty[2], pw_full[2];
+  uint64_t local_full[ws::kNLocal], local_empty[ws::kNLocal];   // [local buffer]
   uint64_t pool_full[2], pool_empty[2], pe_done;
   uint32_t tmem_base;
   int abort;
@@ -157,11 +161,15 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
   if (warp == 0) tmem_alloc(&s.tmem_base, ws::kTmemCols);
   if (tid == 0) {
     uint64_t* full2[] = {s.stage_full, s.c1_full, s.c1_empty, s.strip_full, s.c2_full, s.c2_empty,
-                         s.local_full, s.lg_full, s.lg_empty, s.pw_full, s.pool_full, s.pool_empty,
+                         s.lg_full, s.lg_empty, s.pw_full, s.pool_full, s.pool_empty,
                          s.stage_empty, s.planes_full};
-    const uint32_t cnt[] = {7, 2, 4, 4, 1, 8, 8, 1, 4, 4, 1, 4, 2, 2};
-    for (int k = 0; k < 14; ++k)
+    const uint32_t cnt[] = {7, 2, 4, 4, 1, 8, 1, 4, 4, 1, 4, ws::kCvtWarps, ws::kCvtWarps};
+    for (int k = 0; k < 13; ++k)
       for (int b = 0; b < 2; ++b) mbar_init(&full2[k][b], cnt[k]);
+    for (int b = 0; b < ws::kNLocal; ++b) {
+      mbar_init(&s.local_full[b], 8);              // the eight conv2-epilogue warps
+      mbar_init(&s.local_empty[b], 1);             // the pooling MMAs' commit
+    }
     mbar_init(&s.pe_done, 1);
     fence_mbar_init();
     s.abort = 0;
@@ -229,7 +237,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
 #pragma unroll 1
     for (int i = tid; i < 2 * kStripBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.strip[0][0])[i] = z;
 #pragma unroll 1
-    for (int i = tid; i < 2 * ws::kLocalBytes / 16; i += NT) reinterpret_cast<uint4*>(&s.local16[0][0])[i] = z;
+    for (int i = tid; i < ws::kNLocal * ws::kLocalBytes / 16; i += NT)
+      reinterpret_cast<uint4*>(&s.local16[0][0])[i] = z;
 #pragma unroll 1
     for (int i = tid; i < 2 * 16 * 16 * 16 / 16; i += NT) reinterpret_cast<uint4*>(&s.bpool[0][0])[i] = z;
 #pragma unroll 1
@@ -301,20 +310,20 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
     } else if (tid < 65) {
       const int pr = tid - 60;
       s.c2_bdesc[pr] = smem_desc(smem_u32(s.w2s) + pr * 2048, 1024, 128);
-    } else if (tid < 81) {
+    } else if (tid < 65 + 8 * ws::kNLocal) {
       // logits: A = local tile t, K-major (8-channel chunks 2048 B apart, 8-row groups 128 B)
       const int bb = (tid - 65) >> 3, t = ((tid - 65) >> 2) & 1, kk = (tid - 65) & 3;
       s.lg_adesc[bb][t][kk] = smem_desc(smem_u32(s.local16[bb]) + t * 16384 + kk * 2 * 2048, 2048, 128);
-    } else if (tid < 85) {
-      const int kk = tid - 81;
+    } else if (tid < 69 + 8 * ws::kNLocal) {
+      const int kk = tid - 65 - 8 * ws::kNLocal;
       s.lg_bdesc[kk] = smem_desc(smem_u32(s.blog) + kk * 2 * 256, 256, 128);
-    } else if (tid < 101) {
+    } else if (tid < 69 + 16 * ws::kNLocal) {
       // pooling: A = the local tile read M-major (M = tile*64 + channel: 8-channel blocks
       // 2048 B apart; K = row: 8-row blocks 128 B apart), B = softmax weights, K-major
-      const int bb = (tid - 85) >> 3, kk = (tid - 85) & 7;
+      const int x = tid - 69 - 8 * ws::kNLocal, bb = x >> 3, kk = x & 7;
       s.pl_adesc[bb][kk] = smem_desc(smem_u32(s.local16[bb]) + kk * 256, 128, 2048);
-    } else if (tid < 117) {
-      const int bb = (tid - 101) >> 3, kk = (tid - 101) & 7;
+    } else if (tid < 85 + 16 * ws::kNLocal) {
+      const int x = tid - 69 - 16 * ws::kNLocal, bb = x >> 3, kk = x & 7;
       s.pl_bdesc[bb][kk] = smem_desc(smem_u32(s.bpool[bb]) + kk * 2 * 256, 256, 128);
     }
   }
@@ -377,15 +386,15 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
     constexpr uint32_t idesc = idesc_f16(128, 16);
     int issued = -1;
     for (int i = 0; i < n_env; ++i) {
-      const int b = i & 1, k = i >> 1;
-      if (!warp_wait(s, &s.local_full[b], k & 1, p.slots)) break;
+      const int b = i & 1, k = i >> 1, lb = i % ws::kNLocal;
+      if (!warp_wait(s, &s.local_full[lb], (i / ws::kNLocal) & 1, p.slots)) break;
       if (i >= 2 && !warp_wait(s, &s.lg_empty[b], (k - 1) & 1, p.slots)) break;
       tc_fence_after();
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16_warp(tmem + ws::kColLg + 32 * b + 16 * t, s.lg_adesc[b][t][kk], s.lg_bdesc[kk], idesc,
+          mma_f16_warp(tmem + ws::kColLg + 32 * b + 16 * t, s.lg_adesc[lb][t][kk], s.lg_bdesc[kk], idesc,
                        kk > 0 ? 1u : 0u);
       mma_commit_warp(&s.lg_full[b]);
       issued = i;
@@ -396,7 +405,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
     constexpr uint32_t idesc = idesc_f16_amajor_m(128, 16);
     int issued = -1;
     for (int i = 0; i < n_env; ++i) {
-      const int b = i & 1, k = i >> 1;
+      const int b = i & 1, k = i >> 1, lb = i % ws::kNLocal;
       if (!warp_wait(s, &s.pw_full[b], k & 1, p.slots)) break;
       if (i >= 2 && !warp_wait(s, &s.pool_empty[b], (k - 1) & 1, p.slots)) break;
       tc_fence_after();
@@ -406,9 +415,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16_warp(tmem + ws::kColPl + 32 * b + 16 * h, s.pl_adesc[b][4 * h + kk], s.pl_bdesc[b][4 * h + kk],
+          mma_f16_warp(tmem + ws::kColPl + 32 * b + 16 * h, s.pl_adesc[lb][4 * h + kk], s.pl_bdesc[b][4 * h + kk],
                        idesc, kk > 0 ? 1u : 0u);
       mma_commit_warp(&s.pool_full[b]);
+      mma_commit_warp(&s.local_empty[lb]);    // the last reader of local tile lb is done
       issued = i;
     }
     if (ws_aborted(s) && issued >= 0) mbar_wait_bounded(&s.pool_full[issued & 1], (issued >> 1) & 1);
@@ -521,7 +531,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
     for (int i = 0; i < n_env; ++i) {
       const int b = i & 1, k = i >> 1;
       if (!warp_wait(s, &s.c2_full[b], k & 1, p.slots)) break;
-      if (i >= 2 && !warp_wait(s, &s.pool_full[b], (k - 1) & 1, p.slots)) break;   // local16[b] free
+      const int lb = i % ws::kNLocal;
+      if (i >= ws::kNLocal && !warp_wait(s, &s.local_empty[lb], (i / ws::kNLocal - 1) & 1, p.slots))
+        break;                                                  // local tile lb free
       tc_fence_after();
       const int64_t e = env_of(i);
       const int nchunk = live1 ? 4 : 2;             // (tile 0, 16 channels) x 2, then tile 1
@@ -553,7 +565,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
         }
         const uint4 v0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         const uint4 v1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-        uint8_t* lrow = s.local16[b] + 16384 * t + ri * 16 + (cc >> 3) * 2048;
+        uint8_t* lrow = s.local16[lb] + 16384 * t + ri * 16 + (cc >> 3) * 2048;
         *reinterpret_cast<uint4*>(lrow) = v0;
         *reinterpret_cast<uint4*>(lrow + 2048) = v1;
         if (p.feat_out && (t ? valid1 : valid0)) {
@@ -565,165 +577,180 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.local_full[b]);
+      if (lane == 0) mbar_arrive(&s.local_full[lb]);
     }
   } else {
     // ---- proprio embedding, then softmax / pooled gc per environment ---------------------------
-    const int sid = tid - ws::kSoft * 32;                     // 0..127 = 32 * quarter + lane
+    const int sid = (tid - ws::kSoft * 32) & 127;             // 32 * quarter + lane within the group
+    const int wg = (warp - ws::kSoft) >> 2;
+    const int sbar = ws::kBarSoft + wg;
     float zmax_qp = 0.0f;
     ActQuant aq_qp{};
     aq_qp.let = p.qp.alpha != nullptr;
     bool fail = false;
-    // (1) the batch scale of the embedding's input
-    ActQuant aq_pe{};
-    if (grid_absmax) {
-      bool ok = true;
-      if (sid == 0) {                   // every CTA has added its part (bounded spin, 2 s)
-        const uint32_t* ctr = reinterpret_cast<const uint32_t*>(&p.slots[kSlotFrontBarrier]);
-        const uint64_t t0 = global_timer_ns();
-        while (ld_acquire_gpu(ctr) < (uint32_t)G) {
-          if (global_timer_ns() - t0 > 2000000000ull) {
-            ok = false;
-            *reinterpret_cast<volatile int*>(&s.abort) = 1;
-            atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrBarrierTimeout);
-            break;
-          }
-        }
-      }
-      fail = named_bar_or(ws::kBarSoft, 128, !ok);
-      aq_pe.let = p.pe.alpha != nullptr;
-      aq_pe.dyn = true;
-      aq_pe.s = dyn_scale(ld_relaxed_gpu(&p.slots[0]), aq_pe.let);
-      aq_pe.rcp = __fdiv_rn(1.0f, aq_pe.s);
-      aq_pe.inv = 0.0f;
-    } else {
-      aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
-    }
-    if (dyn && sid < kD) s.pe_scale[sid] = __fmul_rn(s.pe_scale[sid], aq_pe.s);   // s_w * s_z
-    named_bar_sync(ws::kBarSoft, 128);
-    // (2) the int8 embedding of all this CTA's environments in batches of 128 rows: the
-    // quantised rows are the A operand, w8 the B operand, the int32 products land in TMEM
-    // columns [448, 512); the fp16 proprio goes to `enc`
-    const int pe_q = pe_kc * 4;                                // 4-value items per row
-    uint32_t ph_pe = 0;
-    for (int j0 = 0; j0 < n_env && !fail; j0 += 128) {
-      const int nb = n_env - j0 < 128 ? n_env - j0 : 128;
-      for (int item = sid; item < nb * pe_q; item += 128) {
-        const int r = item / pe_q, k0 = 4 * (item - r * pe_q);
-        const int64_t e = env_of(j0 + r);
-        auto ld = [&](int kk) -> __half {
-          if (kk >= P) return __float2half(0.0f);
-          return esz == 4 ? __float2half_rn(reinterpret_cast<const float*>(p.in)[e * p.ld + kk])
-                          : reinterpret_cast<const __half*>(p.in)[e * p.ld + kk];
-        };
-        const __half h0 = ld(k0), h1 = ld(k0 + 1), h2 = ld(k0 + 2), h3 = ld(k0 + 3);
-        auto qz = [&](__half h, int kk) {
-          return kk < P ? ((uint32_t)aq_pe.quant(__half2float(h), s.pe_la[kk], s.pe_lb[kk]) & 0xFFu) : 0u;
-        };
-        *reinterpret_cast<uint32_t*>(s.pe_a + (k0 >> 4) * 2048 + r * 16 + (k0 & 15)) =
-            qz(h0, k0) | (qz(h1, k0 + 1) << 8) | (qz(h2, k0 + 2) << 16) | (qz(h3, k0 + 3) << 24);
-        __half* er = p.enc + e * p.ld_enc + 128 + k0;
-        if (k0 + 4 <= P && (reinterpret_cast<uintptr_t>(er) & 7) == 0) {
-          const __half2 a01 = __halves2half2(h0, h1), a23 = __halves2half2(h2, h3);
-          *reinterpret_cast<uint2*>(er) = make_uint2(*reinterpret_cast<const uint32_t*>(&a01),
-                                                     *reinterpret_cast<const uint32_t*>(&a23));
-        } else {
-          if (k0 < P) er[0] = h0;
-          if (k0 + 1 < P) er[1] = h1;
-          if (k0 + 2 < P) er[2] = h2;
-          if (k0 + 3 < P) er[3] = h3;
-        }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      named_bar_sync(ws::kBarSoft, 128);
-      if (warp == ws::kSoft) {
-        tc_fence_after();
-        constexpr uint32_t idesc = idesc_i8(128, 64);
-        for (int kk = 0; kk < pe_kc / 2; ++kk)
-          mma_i8_warp(tmem + ws::kColPe, smem_desc(smem_u32(s.pe_a) + kk * 4096, 2048, 128),
-                      smem_desc(smem_u32(s.pe_w) + kk * 2048, 1024, 128), idesc, kk > 0 ? 1u : 0u);
-        mma_commit_warp(&s.pe_done);
-      }
-      const bool ok = ws_wait(s, &s.pe_done, ph_pe, p.slots);
-      ph_pe ^= 1;
-      if (named_bar_or(ws::kBarSoft, 128, !ok)) {
-        fail = true;
-        break;
-      }
-      tc_fence_after();
-      if (32 * quarter < nb) {
-        const int r = 32 * quarter + lane;
-        const int64_t e = env_of(j0 + r);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t acc[16];
-          tmem_ld16(tmem + lane_base + ws::kColPe + 16 * c, acc);
-          tmem_ld_wait();
-          if (r < nb) {
-            uint32_t hw[8];
-#pragma unroll
-            for (int t = 0; t < 16; t += 2) {
-              const int n = 16 * c + t;
-              const __half y0 = qlinear_out((int32_t)acc[t], s.pe_scale[n], s.pe_bp[n]);
-              const __half y1 = qlinear_out((int32_t)acc[t + 1], s.pe_scale[n + 1], s.pe_bp[n + 1]);
-              if (dyn) {
-                zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(y0), s.qp_a[kD + n], s.qp_b[kD + n]));
-                zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(y1), s.qp_a[kD + n + 1], s.qp_b[kD + n + 1]));
-              }
-              const __half2 h2 = __halves2half2(y0, y1);
-              hw[t >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+    if (wg == 0) {
+      // (1) the batch scale of the embedding's input
+      ActQuant aq_pe{};
+      if (grid_absmax) {
+        bool ok = true;
+        if (sid == 0) {                   // every CTA has added its part (bounded spin, 2 s)
+          const uint32_t* ctr = reinterpret_cast<const uint32_t*>(&p.slots[kSlotFrontBarrier]);
+          const uint64_t t0 = global_timer_ns();
+          while (ld_acquire_gpu(ctr) < (uint32_t)G) {
+            if (global_timer_ns() - t0 > 2000000000ull) {
+              ok = false;
+              *reinterpret_cast<volatile int*>(&s.abort) = 1;
+              atomicOr(reinterpret_cast<unsigned int*>(&p.slots[kSlotStatus]), kDevErrBarrierTimeout);
+              break;
             }
-            uint4* dst = reinterpret_cast<uint4*>(p.pe_out + e * kD + 16 * c);
-            dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
           }
         }
+        fail = named_bar_or(sbar, 128, !ok);
+        aq_pe.let = p.pe.alpha != nullptr;
+        aq_pe.dyn = true;
+        aq_pe.s = dyn_scale(ld_relaxed_gpu(&p.slots[0]), aq_pe.let);
+        aq_pe.rcp = __fdiv_rn(1.0f, aq_pe.s);
+        aq_pe.inv = 0.0f;
+      } else {
+        aq_pe = make_act_quant(p.pe, p.act_mode, p.slots, 0);
       }
-      tc_fence_before();
-      named_bar_sync(ws::kBarSoft, 128);   // the A tile and the TMEM columns serve the next batch
+      if (dyn && sid < kD) s.pe_scale[sid] = __fmul_rn(s.pe_scale[sid], aq_pe.s);   // s_w * s_z
+      named_bar_sync(sbar, 128);
+      // (2) the int8 embedding of all this CTA's environments in batches of 128 rows: the
+      // quantised rows are the A operand, w8 the B operand, the int32 products land in TMEM
+      // columns [448, 512); the fp16 proprio goes to `enc`
+      const int pe_q = pe_kc * 4;                                // 4-value items per row
+      uint32_t ph_pe = 0;
+      for (int j0 = 0; j0 < n_env && !fail; j0 += 128) {
+        const int nb = n_env - j0 < 128 ? n_env - j0 : 128;
+        for (int item = sid; item < nb * pe_q; item += 128) {
+          const int r = item / pe_q, k0 = 4 * (item - r * pe_q);
+          const int64_t e = env_of(j0 + r);
+          auto ld = [&](int kk) -> __half {
+            if (kk >= P) return __float2half(0.0f);
+            return esz == 4 ? __float2half_rn(reinterpret_cast<const float*>(p.in)[e * p.ld + kk])
+                            : reinterpret_cast<const __half*>(p.in)[e * p.ld + kk];
+          };
+          const __half h0 = ld(k0), h1 = ld(k0 + 1), h2 = ld(k0 + 2), h3 = ld(k0 + 3);
+          auto qz = [&](__half h, int kk) {
+            return kk < P ? ((uint32_t)aq_pe.quant(__half2float(h), s.pe_la[kk], s.pe_lb[kk]) & 0xFFu) : 0u;
+          };
+          *reinterpret_cast<uint32_t*>(s.pe_a + (k0 >> 4) * 2048 + r * 16 + (k0 & 15)) =
+              qz(h0, k0) | (qz(h1, k0 + 1) << 8) | (qz(h2, k0 + 2) << 16) | (qz(h3, k0 + 3) << 24);
+          __half* er = p.enc + e * p.ld_enc + 128 + k0;
+          if (k0 + 4 <= P && (reinterpret_cast<uintptr_t>(er) & 7) == 0) {
+            const __half2 a01 = __halves2half2(h0, h1), a23 = __halves2half2(h2, h3);
+            *reinterpret_cast<uint2*>(er) = make_uint2(*reinterpret_cast<const uint32_t*>(&a01),
+                                                       *reinterpret_cast<const uint32_t*>(&a23));
+          } else {
+            if (k0 < P) er[0] = h0;
+            if (k0 + 1 < P) er[1] = h1;
+            if (k0 + 2 < P) er[2] = h2;
+            if (k0 + 3 < P) er[3] = h3;
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_bar_sync(sbar, 128);
+        if (warp == ws::kSoft) {
+          tc_fence_after();
+          constexpr uint32_t idesc = idesc_i8(128, 64);
+          for (int kk = 0; kk < pe_kc / 2; ++kk)
+            mma_i8_warp(tmem + ws::kColPe, smem_desc(smem_u32(s.pe_a) + kk * 4096, 2048, 128),
+                        smem_desc(smem_u32(s.pe_w) + kk * 2048, 1024, 128), idesc, kk > 0 ? 1u : 0u);
+          mma_commit_warp(&s.pe_done);
+        }
+        const bool ok = ws_wait(s, &s.pe_done, ph_pe, p.slots);
+        ph_pe ^= 1;
+        if (named_bar_or(sbar, 128, !ok)) {
+          fail = true;
+          break;
+        }
+        tc_fence_after();
+        if (32 * quarter < nb) {
+          const int r = 32 * quarter + lane;
+          const int64_t e = env_of(j0 + r);
+  #pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t acc[16];
+            tmem_ld16(tmem + lane_base + ws::kColPe + 16 * c, acc);
+            tmem_ld_wait();
+            if (r < nb) {
+              uint32_t hw[8];
+  #pragma unroll
+              for (int t = 0; t < 16; t += 2) {
+                const int n = 16 * c + t;
+                const __half y0 = qlinear_out((int32_t)acc[t], s.pe_scale[n], s.pe_bp[n]);
+                const __half y1 = qlinear_out((int32_t)acc[t + 1], s.pe_scale[n + 1], s.pe_bp[n + 1]);
+                if (dyn) {
+                  zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(y0), s.qp_a[kD + n], s.qp_b[kD + n]));
+                  zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(y1), s.qp_a[kD + n + 1], s.qp_b[kD + n + 1]));
+                }
+                const __half2 h2 = __halves2half2(y0, y1);
+                hw[t >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(p.pe_out + e * kD + 16 * c);
+              dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+              dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            }
+          }
+        }
+        tc_fence_before();
+        named_bar_sync(sbar, 128);   // the A tile and the TMEM columns serve the next batch
+      }
     }
-    // (3) per environment: logits -> softmax -> pooling weights; pooled partials -> gc
+    // (3) per step i: logits -> softmax -> pooling weights of environment i, then the pooled
+    //     gc of environment i-2 (its pooling MMAs ran while the softmax of i was computed)
     const int ri = sid;                                       // row of tile 0; tile 1 row 128 + ri
     const bool live1 = 128 + 32 * quarter < 11 * kStripCols;
     const int oh0 = ri / kStripCols, ow0 = ri - oh0 * kStripCols;
     const int m1 = 128 + ri, oh1 = m1 / kStripCols, ow1 = m1 - oh1 * kStripCols;
     const int tok0 = oh0 < kH2 && ow0 < kW2 ? oh0 * kW2 + ow0 : -1;
     const int tok1 = oh1 < kH2 && ow1 < kW2 ? oh1 * kW2 + ow1 : -1;
-    for (int i = 0; i < n_env && !fail; ++i) {
-      const int b = i & 1, k = i >> 1;
-      const int64_t e = env_of(i);
-      bool ok = ws_wait(s, &s.lg_full[b], k & 1, p.slots);
-      if (named_bar_or(ws::kBarSoft, 128, !ok)) break;
-      tc_fence_after();
-      uint32_t la0, la1, lb0 = 0, lb1 = 0;
-      tmem_ld2(tmem + lane_base + ws::kColLg + 32 * b, la0, la1);
-      if (live1) tmem_ld2(tmem + lane_base + ws::kColLg + 32 * b + 16, lb0, lb1);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.lg_empty[b]);
-      // logits (qrt/encoder_opt.py:69-73) and the softmax over the 187 tokens (:75)
-      float g0 = -INFINITY, g1 = -INFINITY;
-      if (tok0 >= 0) {
-        g0 = fp16r(__fadd_rn(fp16r(__uint_as_float(la0)), gb));
-        p.score_local[e * kTok + tok0] = __float2half_rn(__uint_as_float(la1));
-      }
-      if (tok1 >= 0) {
-        g1 = fp16r(__fadd_rn(fp16r(__uint_as_float(lb0)), gb));
-        p.score_local[e * kTok + tok1] = __float2half_rn(__uint_as_float(lb1));
-      }
-      float mx = warp_max(fmaxf(g0, g1));
-      if (lane == 0) s.red[quarter] = mx;
-      named_bar_sync(ws::kBarSoft, 128);
-      mx = fmaxf(fmaxf(s.red[0], s.red[1]), fmaxf(s.red[2], s.red[3]));
-      const float ex0 = tok0 < 0 ? 0.0f : expf(g0 - mx);
-      const float ex1 = tok1 < 0 ? 0.0f : expf(g1 - mx);
-      float sm = warp_sum(ex0 + ex1);
-      if (lane == 0) s.red[4 + quarter] = sm;
-      named_bar_sync(ws::kBarSoft, 128);
-      sm = (s.red[4] + s.red[5]) + (s.red[6] + s.red[7]);
-      {
+    for (int i = wg; i < n_env + 2 && !fail; i += 2) {
+      if (i < n_env) {
+        const int b = i & 1, k = i >> 1;
+        const int64_t e = env_of(i);
+        const bool ok = ws_wait(s, &s.lg_full[b], k & 1, p.slots);
+        if (named_bar_or(sbar, 128, !ok)) break;
+        tc_fence_after();
+        uint32_t la0, la1, lb0 = 0, lb1 = 0;
+        tmem_ld2(tmem + lane_base + ws::kColLg + 32 * b, la0, la1);
+        if (live1) tmem_ld2(tmem + lane_base + ws::kColLg + 32 * b + 16, lb0, lb1);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.lg_empty[b]);
+        // logits (qrt/encoder_opt.py:69-73) and the softmax over the 187 tokens (:75)
+        float g0 = -INFINITY, g1 = -INFINITY;
+        if (tok0 >= 0) {
+          g0 = fp16r(__fadd_rn(fp16r(__uint_as_float(la0)), gb));
+          p.score_local[e * kTok + tok0] = __float2half_rn(__uint_as_float(la1));
+        }
+        if (tok1 >= 0) {
+          g1 = fp16r(__fadd_rn(fp16r(__uint_as_float(lb0)), gb));
+          p.score_local[e * kTok + tok1] = __float2half_rn(__uint_as_float(lb1));
+        }
+        float mx = warp_max(fmaxf(g0, g1));
+        if (lane == 0) s.red[wg][quarter] = mx;
+        named_bar_sync(sbar, 128);
+        mx = fmaxf(fmaxf(s.red[wg][0], s.red[wg][1]), fmaxf(s.red[wg][2], s.red[wg][3]));
+        const float ex0 = tok0 < 0 ? 0.0f : expf(g0 - mx);
+        const float ex1 = tok1 < 0 ? 0.0f : expf(g1 - mx);
+        // the pipelined front's order: one warp sum per (tile, quarter), then those sums in
+        // sequence (tile 0 quarters 0-3, tile 1 quarters 0-2; tile 1's last quarter is past
+        // the grid), so both fronts give the same weights
+        const float s0 = warp_sum(ex0), s1 = warp_sum(ex1);
+        if (lane == 0) {
+          s.red[wg][4 + quarter] = s0;
+          s.red[wg][8 + quarter] = s1;
+        }
+        named_bar_sync(sbar, 128);
+        float sm = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sm += s.red[wg][4 + q];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) sm += s.red[wg][8 + q];
         // pooling B: column n = tile, K = row within the tile
         const __half w0 = __float2half_rn(__fdiv_rn(ex0, sm)), w1 = __float2half_rn(__fdiv_rn(ex1, sm));
         __half* bp = reinterpret_cast<__half*>(s.bpool[b] + (ri >> 3) * 256);
@@ -733,38 +760,42 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
           if (tok0 >= 0) p.gc_w_out[e * kTok + tok0] = w0;
           if (tok1 >= 0) p.gc_w_out[e * kTok + tok1] = w1;
         }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.pw_full[b]);
       }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.pw_full[b]);
-      // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77): row
-      // tile*64 + c of the pooling accumulator, column `tile`
-      ok = ws_wait(s, &s.pool_full[b], k & 1, p.slots);
-      if (named_bar_or(ws::kBarSoft, 128, !ok)) break;
-      tc_fence_after();
-      uint32_t d0, d1, f0, f1;
-      tmem_ld2(tmem + lane_base + ws::kColPl + 32 * b, d0, d1);
-      tmem_ld2(tmem + lane_base + ws::kColPl + 32 * b + 16, f0, f1);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.pool_empty[b]);
-      s.poolv[sid] = __fadd_rn(__uint_as_float(sid < 64 ? d0 : d1), __uint_as_float(sid < 64 ? f0 : f1));
-      named_bar_sync(ws::kBarSoft, 128);
-      if (sid < kD) {
-        const __half gh = __float2half_rn(s.poolv[sid] + s.poolv[64 + sid]);
-        p.enc[e * p.ld_enc + 64 + sid] = gh;
-        if (dyn) zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(gh), s.qp_a[sid], s.qp_b[sid]));
+      if (i >= 2 && i - 2 < n_env) {
+        // pooled global context gc = sum_i w_i local_i (qrt/encoder_opt.py:76-77) of j = i-2:
+        // row tile*64 + c of the pooling accumulator, column `tile`
+        const int j = i - 2, b = j & 1, k = j >> 1;
+        const int64_t e = env_of(j);
+        const bool ok = ws_wait(s, &s.pool_full[b], k & 1, p.slots);
+        if (named_bar_or(sbar, 128, !ok)) break;
+        tc_fence_after();
+        uint32_t d0, d1, f0, f1;
+        tmem_ld2(tmem + lane_base + ws::kColPl + 32 * b, d0, d1);
+        tmem_ld2(tmem + lane_base + ws::kColPl + 32 * b + 16, f0, f1);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.pool_empty[b]);
+        s.poolv[wg][sid] = __fadd_rn(__uint_as_float(sid < 64 ? d0 : d1), __uint_as_float(sid < 64 ? f0 : f1));
+        named_bar_sync(sbar, 128);
+        if (sid < kD) {
+          const __half gh = __float2half_rn(s.poolv[wg][sid] + s.poolv[wg][64 + sid]);
+          p.enc[e * p.ld_enc + 64 + sid] = gh;
+          if (dyn) zmax_qp = fmaxf(zmax_qp, aq_qp.absz(__half2float(gh), s.qp_a[sid], s.qp_b[sid]));
+        }
       }
     }
     // one atomic per CTA on the query projector's absmax slot
     if (dyn) {
       const float m = warp_max(zmax_qp);
-      named_bar_sync(ws::kBarSoft, 128);
-      if (lane == 0) s.red[quarter] = m;
-      named_bar_sync(ws::kBarSoft, 128);
+      named_bar_sync(sbar, 128);
+      if (lane == 0) s.red[wg][quarter] = m;
+      named_bar_sync(sbar, 128);
       if (sid == 0) {
-        const float mm = fmaxf(fmaxf(s.red[0], s.red[1]), fmaxf(s.red[2], s.red[3]));
+        const float mm = fmaxf(fmaxf(s.red[wg][0], s.red[wg][1]), fmaxf(s.red[wg][2], s.red[wg][3]));
         if (mm > 0.0f) atomic_max_nonneg(&p.slots[1], mm);
       }
     }
