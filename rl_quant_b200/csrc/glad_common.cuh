@@ -251,6 +251,43 @@ __device__ __forceinline__ float warp_reduce16(float (&v)[16], int lane) {
   return r + __shfl_xor_sync(0xffffffffu, r, 16);
 }
 
+// 16 per-lane values v[h] -> every lane gets op over the 32 lanes of each h, combined in
+// the butterfly order (partners L^16, L^8, L^4, L^2, L^1) and so bit-identical to 16
+// separate xor-butterflies, in 32 shuffles instead of 80: each step hands half of the
+// still-open values to the partner (after step k a lane holds 16 >> k of them), the last
+// step leaves value h on lanes 2h and 2h+1, and 16 shuffles broadcast the results.
+template <bool kMax>
+__device__ __forceinline__ void warp_allreduce16(float (&v)[16], int lane) {
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+  float w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool up = lane & 16;
+    w[i] = op(up ? v[i + 8] : v[i], __shfl_xor_sync(0xffffffffu, up ? v[i] : v[i + 8], 16));
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 8;
+    w[i] = op(up ? w[i + 4] : w[i], __shfl_xor_sync(0xffffffffu, up ? w[i] : w[i + 4], 8));
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 4;
+    w[i] = op(up ? w[i + 2] : w[i], __shfl_xor_sync(0xffffffffu, up ? w[i] : w[i + 2], 4));
+  }
+  {
+    const bool up = lane & 2;
+    w[0] = op(up ? w[1] : w[0], __shfl_xor_sync(0xffffffffu, up ? w[0] : w[1], 2));
+  }
+  w[0] = op(w[0], __shfl_xor_sync(0xffffffffu, w[0], 1));
+  // lane L now holds the result of h = 8*b4 + 4*b3 + 2*b2 + b1 (bk = bit k of L)
+#pragma unroll
+  for (int h = 0; h < 16; ++h) {
+    const int src = ((h >> 3) & 1) << 4 | ((h >> 2) & 1) << 3 | ((h >> 1) & 1) << 2 | (h & 1) << 1;
+    v[h] = __shfl_sync(0xffffffffu, w[0], src);
+  }
+}
+
 // conv2 weights w8 [3][64 (kw*16 + c)][64 n] (qrt/qconv.py:270-284) -> the MMA B operand
 // [5 K-steps][2 taps][64 n][16 c] (tap q = kh*3 + kw; tap 9 is zero filler). One thread
 // builds one 4-byte word; a warp reads 32 consecutive n (no bank conflicts in shared

@@ -24,6 +24,15 @@ constexpr int kTailRows = 32 * kTailWarps;   // GEMM rows per CTA
 // groups = two per resident CTA (2 per SM x 148) with no third wave; slot 7 is idle.
 constexpr int kTailEnvs = 7;
 constexpr int kTailTmemCols = 256;           // tile t: columns [128t, 128t+128): conv2, then K|V
+constexpr int kTailMaxProp = 104;            // proprio columns of an encoded row
+// Inputs of one environment, copied one group ahead: the proprio embedding (64 halves),
+// then enc[64, 128 + P) (gc and the proprio columns), so that stage half k >= 64 is enc[k].
+constexpr int kTailStageBytes = 2 * kD + 2 * (kD + kTailMaxProp);
+
+// The [k pair c][n pair np] weight tables are read by lane np at a fixed c; element
+// (c, np) sits at c*32 + (np ^ (c & 15)), so that the set-up's writes (32 consecutive c
+// at a fixed np) take 2 shared-memory wavefronts per warp instead of 32.
+__device__ __forceinline__ int swz(int c, int np) { return c * 32 + (np ^ (c & 15)); }
 
 struct __align__(128) TailSmem {
   uint8_t w2s[5 * 2048];          // conv2 B operand (same layout as the front kernel)
@@ -31,9 +40,10 @@ struct __align__(128) TailSmem {
   // same bytes hold the local features (fp16) [k8 chunk][row][16 B]
   uint8_t a12[10 * kTailRows * 16];
   uint8_t bkv[8 * 2048];          // in_proj rows 64..191 fp16: [k8 chunk][n][16B]
-  uint2 wqT[32 * 32];             // in_proj rows 0..63: [k pair][n pair] -> half2 (n even), half2 (n odd)
+  uint2 wqT[32 * 32];             // in_proj rows 0..63: [k pair][n pair] -> half2 (n even), half2 (n odd) (swz)
   uint2 woT[32 * 32];             // out_proj, same layout
-  int2 w8qpT[32 * 32];            // query_projector int8: [k quad][n pair]
+  int2 w8qpT[32 * 32];            // query_projector int8: [k quad][n pair] (swz)
+  alignas(16) uint8_t stage[2][kTailWarps][kTailStageBytes];   // [group parity][warp]
   float qp_a[128], qp_b[128];
   float qp_scale[64], qp_bp[64];
   alignas(16) float dq[64];
@@ -130,31 +140,51 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     r_wsq = __half2float(p.scorer_w[64 + tid]);
   }
   float r_bin = tid < 192 ? __half2float(p.in_b[tid]) : 0.0f;
-  grid_dep_wait();                      // outputs of the front kernel are visible from here
-  const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, p.qp_slot);
+  const float sb = __half2float(p.scorer_b[0]);
+  // the weight tables need nothing of the front kernel: built before the dependency wait
   cp_async_wait_all();
   __syncthreads();
   conv2_b_relayout(s.w2s, scratch, tid, NT);
   for (int idx = tid; idx < 32 * 32; idx += NT) {
-    // [k pair c2][n pair np]: (W[2np][2c2..], W[2np+1][2c2..]) as two half2
-    const int c2 = idx >> 5, np = idx & 31;
+    // [k pair c][n pair np]: (W[2np][2c..], W[2np+1][2c..]) as two half2 (int8: two 4-byte
+    // words); a warp reads 32 consecutive c of one row pair
+    const int c = idx & 31, np = idx >> 5;
     const uint32_t* wi = reinterpret_cast<const uint32_t*>(scratch + 12288);
     const uint32_t* wo = reinterpret_cast<const uint32_t*>(scratch + 20480);
     const int* w8 = reinterpret_cast<const int*>(scratch + 28672);
-    s.wqT[idx] = make_uint2(wi[(2 * np) * 32 + c2], wi[(2 * np + 1) * 32 + c2]);
-    s.woT[idx] = make_uint2(wo[(2 * np) * 32 + c2], wo[(2 * np + 1) * 32 + c2]);
-    s.w8qpT[idx] = make_int2(w8[(2 * np) * 32 + c2], w8[(2 * np + 1) * 32 + c2]);
+    const int d = swz(c, np);
+    s.wqT[d] = make_uint2(wi[(2 * np) * 32 + c], wi[(2 * np + 1) * 32 + c]);
+    s.woT[d] = make_uint2(wo[(2 * np) * 32 + c], wo[(2 * np + 1) * 32 + c]);
+    s.w8qpT[d] = make_int2(w8[(2 * np) * 32 + c], w8[(2 * np + 1) * 32 + c]);
   }
   if (tid < 64) {
-    if (dyn) s.qp_scale[tid] = __fmul_rn(s.qp_scale[tid], aq.s);      // s_w * s_z
     s.bout[tid] = r_bout;
     s.wsq[tid] = r_wsq;
   }
   if (tid < 192) s.bin[tid] = r_bin;
-  __syncthreads();                      // scratch is the im2col buffer again from here
-  for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9
+  for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9 (past the raw weights)
     reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
-  const float sb = __half2float(p.scorer_b[0]);
+  const int64_t ngroups = (p.B + kTailEnvs - 1) / kTailEnvs;
+  // this warp's inputs of group g -> stage[b]: the proprio embedding row, then enc[64, 128 + P)
+  // in 8-byte copies (rows start on 8-byte boundaries; the last copy may take up to three
+  // halves of the row's padding, never read)
+  auto prefetch = [&](int64_t g, int b) {
+    const int64_t e = g * kTailEnvs + warp;
+    if (warp >= kTailEnvs || g >= ngroups || e >= p.B) return;
+    uint8_t* st = s.stage[b][warp];
+    const uint8_t* pe_row = reinterpret_cast<const uint8_t*>(p.pe + e * kD);
+    const uint8_t* enc_row = reinterpret_cast<const uint8_t*>(p.enc + e * p.ld_enc + kD);
+    const int n_pe = 2 * kD / 8, n_all = n_pe + (2 * (kD + p.prop_dim) + 7) / 8;
+    for (int c = lane; c < n_all; c += 32) {
+      if (c < n_pe) cp_async8(st + 8 * c, pe_row + 8 * c);
+      else cp_async8(st + 8 * c, enc_row + 8 * (c - n_pe));
+    }
+  };
+  grid_dep_wait();                      // outputs of the front kernel are visible from here
+  prefetch(blockIdx.x, 0);
+  cp_async_commit();
+  const ActQuant aq = make_act_quant(p.qp, p.act_mode, p.slots, p.qp_slot);
+  if (tid < 64 && dyn) s.qp_scale[tid] = __fmul_rn(s.qp_scale[tid], aq.s);      // s_w * s_z
   const uint64_t g_offset = p.gumbel ? (uint64_t)*p.gumbel_offset : 0ull;
   fence_async_smem();
   tc_fence_before();
@@ -168,11 +198,15 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   ActQuant aq_a0{};
   aq_a0.let = a0_let;
 
-  const int64_t ngroups = (p.B + kTailEnvs - 1) / kTailEnvs;
-  for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x) {
+  int buf = 0;
+  for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, buf ^= 1) {
     const int64_t env = g * kTailEnvs + warp;
     const bool have = warp < kTailEnvs && env < p.B;
     const int r = 32 * warp + lane;              // GEMM row of this thread
+    cp_async_wait_all();                         // this group's stage: the only copies in flight
+    __syncwarp();
+    const __half* stg = reinterpret_cast<const __half*>(s.stage[buf][warp]);   // pe | enc[64..]
+    float zm_enc = 0.0f;                         // actor.0 absmax over enc[64, 128 + P)
     if (have) {
       // this environment's local scores, loaded first (used after the two GEMVs)
       __half sl[6];
@@ -181,21 +215,22 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         const int i = lane + 32 * j;
         sl[j] = i < kTok ? p.score_local[env * kTok + i] : __float2half(0.0f);
       }
-      // ---- 1. query projector: W8A8 over cat(gc, pe) ---------------------------------
-      const __half* gc = p.enc + env * p.ld_enc + 64;
-      const __half* pe = p.pe + env * kD;
+      // ---- 1. query projector: W8A8 over cat(gc, pe) (gc = enc[64, 128)) -------------
       uint32_t qword = 0;
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const int k = 4 * lane + b;
-        const float x = __half2float(k < 64 ? gc[k] : pe[k - 64]);
+        const float x = __half2float(k < 64 ? stg[64 + k] : stg[k - 64]);
         qword |= (uint32_t)(aq.quant(x, s.qp_a[k], s.qp_b[k]) & 0xFF) << (8 * b);
       }
+      if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax)
+        for (int k = 64 + lane; k < enc_w; k += 32)    // |alpha*enc + beta| for actor.0's s_z
+          zm_enc = fmaxf(zm_enc, aq_a0.absz(__half2float(stg[k]), s.a0_a[k], s.a0_b[k]));
       int acc0 = 0, acc1 = 0;
 #pragma unroll
       for (int w = 0; w < 32; ++w) {
         const int qw = (int)__shfl_sync(0xffffffffu, qword, w);
-        const int2 wv = s.w8qpT[w * 32 + lane];
+        const int2 wv = s.w8qpT[swz(w, lane)];
         acc0 = __dp4a(qw, wv.x, acc0);
         acc1 = __dp4a(qw, wv.y, acc1);
       }
@@ -294,7 +329,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
         for (int c2 = 0; c2 < 32; ++c2) {
-          const uint2 wv = s.wqT[c2 * 32 + lane];
+          const uint2 wv = s.wqT[swz(c2, lane)];
           const float x0 = s.qv[warp][2 * c2], x1 = s.qv[warp][2 * c2 + 1];
           const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
           const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
@@ -318,6 +353,10 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+
+    // the next group's inputs land while this one finishes
+    prefetch(g + gridDim.x, buf ^ 1);
+    cp_async_commit();
 
     // ---- 5. conv2 recompute for the 256 selected rows (two M=128 tiles) -------------------
     if (tid == 0) {
@@ -426,19 +465,13 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     float red[kHeads];
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) red[h] = sc[h];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h) red[h] = fmaxf(red[h], __shfl_xor_sync(0xffffffffu, red[h], o));
+    warp_allreduce16<true>(red, lane);
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) {
       sc[h] = expf(sc[h] - red[h]);
       red[h] = sc[h];
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h) red[h] += __shfl_xor_sync(0xffffffffu, red[h], o);
+    warp_allreduce16<false>(red, lane);
     float asum = 0.0f;
 #pragma unroll
     for (int h = 0; h < kHeads; h += 2) {
@@ -473,7 +506,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
       for (int c2 = 0; c2 < 32; ++c2) {
-        const uint2 wv = s.woT[c2 * 32 + lane];
+        const uint2 wv = s.woT[swz(c2, lane)];
         const float x0 = s.om[warp][2 * c2], x1 = s.om[warp][2 * c2 + 1];
         const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
         const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
@@ -488,15 +521,14 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       reinterpret_cast<__half2*>(p.enc + env * p.ld_enc)[lane] = __floats2half2_rn(f0, f1);
       if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
         // |alpha*encoded + beta| for actor.0's dynamic s_z
-        float zm = fmaxf(aq_a0.absz(f0, s.a0_a[2 * lane], s.a0_b[2 * lane]),
-                         aq_a0.absz(f1, s.a0_a[2 * lane + 1], s.a0_b[2 * lane + 1]));
-        for (int k = 64 + lane; k < enc_w; k += 32)
-          zm = fmaxf(zm, aq_a0.absz(__half2float(p.enc[env * p.ld_enc + k]), s.a0_a[k], s.a0_b[k]));
-        zmax_a0 = fmaxf(zmax_a0, zm);
+        const float zm = fmaxf(aq_a0.absz(f0, s.a0_a[2 * lane], s.a0_b[2 * lane]),
+                               aq_a0.absz(f1, s.a0_a[2 * lane + 1], s.a0_b[2 * lane + 1]));
+        zmax_a0 = fmaxf(zmax_a0, fmaxf(zm, zm_enc));
       }
     }
     __syncthreads();
   }
+  cp_async_wait_all();                           // a prefetch left in flight by an abort
 
   if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
     // one atomic per CTA on actor.0's absmax slot
@@ -529,6 +561,8 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
 }
 
 size_t tail_smem_bytes() { return sizeof(TailSmem) + 128; }
+// two CTAs per SM (228 KB of shared memory, 1 KB of it reserved per CTA)
+static_assert(2 * (sizeof(TailSmem) + 128 + 1024) <= 228 * 1024, "tail shared memory");
 
 // Persistent grid: one CTA per group of environments, at most two per SM.
 int tail_grid(int64_t B, int sms) {
@@ -537,6 +571,10 @@ int tail_grid(int64_t B, int sms) {
 }
 
 cudaError_t launch_tail(const TailParams& p, int grid, cudaStream_t st, bool pdl) {
+  // the staged copies of an encoded row need 8-byte row starts, P <= kTailMaxProp and the
+  // row's columns up to the next multiple of 4 inside its stride
+  if (p.ld_enc % 4 || p.prop_dim < 0 || p.prop_dim > kTailMaxProp || 128 + ((p.prop_dim + 3) & ~3) > p.ld_enc)
+    return cudaErrorInvalidValue;
   const size_t smem = tail_smem_bytes();
   static bool done[64] = {false};
   cudaError_t e = allow_max_smem((const void*)tail_kernel, done);
