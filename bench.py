@@ -62,6 +62,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-conv-chain", action="store_true", help="skip the conv-only (QuantCNN chain) measurement")
     p.add_argument("--no-w4a16", action="store_true", help="skip the W4A16 large-batch measurement")
+    p.add_argument("--profile-case", choices=("actor", "chain"), default=None,
+                   help="run only this workload for a profiler (warm-up + steps forwards of --batch, "
+                        "no graphs, no timing, no JSON line): 'actor' = the fused actor forward, "
+                        "'chain' = the QuantCNN chain alone (glad_conv_chain)")
     return p.parse_args()
 
 
@@ -308,6 +312,30 @@ def bench_w4a16(device, hbm_peak, fused, infer, reps=20):
     return out
 
 
+def profile_case(args, device, fused):
+    """One workload alone, for an ncu capture: --warmup + --steps calls on rotating inputs
+    (two buffers), plainly launched so that each kernel is one launch in the list."""
+    from rl_quant_b200 import _native as N
+    from rl_quant_b200.synthetic import glad_obs
+    B, n = args.batch, args.warmup + args.steps
+    if args.profile_case == "actor":
+        obs = [glad_obs(B, seed=1000 + i).to(device) for i in range(2)]
+        mean = torch.empty(B, 29, dtype=torch.float32, device=device)
+        for k in range(n):
+            fused.run(obs[k % 2], mean)
+    else:
+        lib = N.load()
+        xs = [glad_obs(B, seed=77 + i)[:, 96:].half().reshape(B, 21, 33, 3).contiguous().to(device)
+              for i in range(2)]
+        feat = torch.empty(B * 187, 64, dtype=torch.float16, device=device)
+        z8 = torch.empty(B * 187, 16, dtype=torch.int8, device=device)
+        for k in range(n):
+            N.check(lib.glad_conv_chain(xs[k % 2].data_ptr(), B, fused.weights().conv, feat.data_ptr(),
+                                        z8.data_ptr(), N.stream_handle(device)), "conv chain")
+    torch.cuda.synchronize(device)
+    print(f"profile case {args.profile_case}: {n} calls at B={B}")
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -332,6 +360,9 @@ def run_ours(args):
     if fused.act_mode != args.act_mode:
         raise RuntimeError("calibrated model has the wrong act_mode")
 
+    if args.profile_case:
+        profile_case(args, device, fused)
+        return
     # inputs resident in HBM, rotated so successive steps miss L2
     obs = [glad_obs(B, seed=1000 + 97 * rank + i).to(device) for i in range(args.nbuf)]
     means = [torch.empty(B, 29, dtype=torch.float32, device=device) for _ in range(args.nbuf)]
