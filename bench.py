@@ -616,7 +616,7 @@ def run_ours(args):
                        "batch_per_gpu": B, "act_mode": args.act_mode, "obs_dtype": "fp32",
                        "weights": "seed-0 default init, LET calibrated 200 Adam steps on 512 obs (seed 1)",
                        "l2": f"{args.nbuf} rotating obs buffers ({args.nbuf * B * OBS_BYTES_PER_ENV / 1e6:.0f} MB) > 126 MB L2",
-                       "launch": f"CUDA graph per step (memset + {n_kernels} kernels)"},
+                       "launch": f"CUDA graph per step ({n_kernels} kernels: slot clear, front, tail, MLP)"},
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * 2175 * 4,

@@ -160,6 +160,20 @@ int front_grid(int64_t B, const DeviceInfo& d, int per_sm) {
   return (int)(B < g ? B : g);
 }
 
+// Per-call reset of the slot block (everything but the sticky status word) as a
+// one-CTA kernel rather than a memset node: it lets the next kernel launch at once
+// (programmatic dependent launch), so the front kernel's set-up (weights, first rows,
+// TMEM, mbarriers) overlaps it; the front reads no slot before griddepcontrol.wait.
+__global__ void slots_clear_kernel(float* slots) {
+  grid_dep_launch();
+  if (threadIdx.x < kSlotStatus) slots[threadIdx.x] = 0.0f;
+}
+static_assert(kSlotStatus <= 64, "one thread per cleared slot");
+cudaError_t clear_slots(float* slots, cudaStream_t st) {
+  slots_clear_kernel<<<1, 64, 0, st>>>(slots);
+  return cudaGetLastError();
+}
+
 // Fused-forward workspace layout.
 struct ActorWs {
   float* slots;
@@ -525,14 +539,16 @@ int actor_forward_impl(const GladActorWeights* w, const void* obs, int obs_dtype
     return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded / proprio_emb must be 16-byte aligned, query 4-byte");
 
   stage_mark(0, st);
-  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsClearBytes, st), "workspace reset");
+  GLAD_CHECK_CUDA(clear_slots(ws.slots, st), "workspace reset");
   // Dynamic s_z of the proprio embedding: reduced inside the front kernel (grid
   // barrier) when its whole grid fits on the device at once, else by a separate pass.
   const bool ws_front = use_front_ws(dual != nullptr, nm.mean != nullptr);
   const int front_per_sm = ws_front ? 1 : front_fused_blocks_per_sm();
   const bool pe_absmax_in_front = act_mode == GLAD_ACT_DYNAMIC && front_per_sm > 0;
   const int fgrid = front_grid(B, d, front_per_sm > 0 && front_per_sm < 2 ? front_per_sm : 2);
-  const bool front_pdl = act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front;
+  // the front follows the clear kernel or the absmax pass and waits for it before its
+  // first slot access, so it may always launch early
+  const bool front_pdl = true;
   if (act_mode == GLAD_ACT_DYNAMIC && !pe_absmax_in_front)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb.alpha,
                                   w->proprio_emb.beta, 1, &ws.slots[0], d.sms, st, nm.mean, nm.var, nm.eps),
@@ -758,9 +774,10 @@ int critic_forward_impl(const GladCriticWeights* w, const void* obs, int obs_dty
   if (!aligned(z8, 16) || !aligned(enc, 16) || !aligned(pe, 16) || (ax.query && !aligned(ax.query, 4)))
     return fail(GLAD_ERR_INVALID_ARG, "aux z8 / encoded / proprio_emb must be 16-byte aligned, query 4-byte");
 
-  GLAD_CHECK_CUDA(cudaMemsetAsync(ws.slots, 0, kSlotsClearBytes, st), "workspace reset");
-  const bool front_pdl = !pe16 && act_mode == GLAD_ACT_DYNAMIC;
-  if (front_pdl)
+  GLAD_CHECK_CUDA(clear_slots(ws.slots, st), "workspace reset");
+  const bool absmax_pass = !pe16 && act_mode == GLAD_ACT_DYNAMIC;
+  const bool front_pdl = true;          // after the clear kernel or the absmax pass (both kernels)
+  if (absmax_pass)
     GLAD_CHECK_CUDA(launch_absmax(obs, obs_dtype, B, ld_obs, P, w->proprio_emb_q.alpha,
                                   w->proprio_emb_q.beta, 1, &ws.slots[0], d.sms, st, w->obs_norm.mean,
                                   w->obs_norm.var, w->obs_norm.eps),
@@ -939,7 +956,7 @@ int glad_actor_kernel_count(int64_t B, int act_mode) {
   if (B == 0) return 0;
   const bool absmax_pass =
       act_mode == GLAD_ACT_DYNAMIC && !use_front_ws(false, false) && front_fused_blocks_per_sm() <= 0;
-  return 2 + (absmax_pass ? 1 : 0) + (use_fused_mlp(B, act_mode, 0) ? 1 : 4);
+  return 3 + (absmax_pass ? 1 : 0) + (use_fused_mlp(B, act_mode, 0) ? 1 : 4);   // clear + front + tail + MLP
 }
 
 int glad_actor_stage_events(void* const* events, int n) {

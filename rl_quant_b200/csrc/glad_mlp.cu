@@ -163,20 +163,17 @@ __device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mb
 }
 
 // 16 accumulator columns at `taddr`: the sum of the kMlpChains partial chains (int32,
-// exact), chain c at column offset c * nj.
+// exact), chain c at column offset c * nj; all chains' loads are in flight before one wait.
 __device__ __forceinline__ void mlp_ld_acc(uint32_t taddr, int nj, uint32_t (&r)[16]) {
-  static_assert(kMlpChains == 4, "two loads per wait");
-  uint32_t t[16], u[16];
+  uint32_t t[kMlpChains - 1][16];
   tmem_ld16(taddr, r);
-  tmem_ld16(taddr + (uint32_t)nj, t);
+#pragma unroll
+  for (int c = 1; c < kMlpChains; ++c) tmem_ld16(taddr + (uint32_t)(c * nj), t[c - 1]);
   tmem_ld_wait();
 #pragma unroll
-  for (int j = 0; j < 16; ++j) r[j] += t[j];
-  tmem_ld16(taddr + (uint32_t)(2 * nj), t);
-  tmem_ld16(taddr + (uint32_t)(3 * nj), u);
-  tmem_ld_wait();
+  for (int c = 1; c < kMlpChains; ++c)
 #pragma unroll
-  for (int j = 0; j < 16; ++j) r[j] += t[j] + u[j];
+    for (int j = 0; j < 16; ++j) r[j] += t[c - 1][j];
 }
 
 // 16 int32 accumulators -> fp32, exactly: through the mantissa of 1.5*2^23 (two ALU
