@@ -301,8 +301,8 @@ int glad_actor_stage_events(void* const* events, int n);
 int glad_actor_mlp_fused(int64_t B, int act_mode);
 
 /* Number of kernels one glad_actor_forward call with mean_out set launches for
- * a B-row batch on the current device (after a 256-byte memset), aux outputs
- * aside; < 0 on error. Not part of the reference interface.                */
+ * a B-row batch on the current device (the slot-reset kernel included), aux
+ * outputs aside; < 0 on error. Not part of the reference interface.         */
 int glad_actor_kernel_count(int64_t B, int act_mode);
 
 /* Allocation-free variant of glad_actor_forward. No counterpart in the
