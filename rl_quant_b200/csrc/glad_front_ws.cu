@@ -72,6 +72,7 @@ struct __align__(128) WsSmem {
   alignas(16) float b2[64];
   alignas(16) float a2[64];
   alignas(16) float c2[64];
+  float4 ck[64];                              // conv2 epilogue constants per channel {dq, b2, a2, c2}
   float pe_la[kMaxProp], pe_lb[kMaxProp];     // proprio embedding LET alpha / beta
   float pe_scale[64], pe_bp[64];
   float qp_a[128], qp_b[128];                 // query projector LET (absmax of its input)
@@ -291,6 +292,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
       dst[idx] = v;
     }
     conv2_b_relayout(s.w2s, scratch, tid, NT);
+    if (tid < 64) s.ck[tid] = make_float4(s.dq[tid], s.b2[tid], s.a2[tid], s.c2[tid]);
     if (tid < 2 * kD) {                  // logits B: row 0 = GPS weight, row 1 = scorer (local half)
       const int n = tid >> 6, c = (tid & 63) >> 3, e = tid & 7;
       reinterpret_cast<__half*>(s.blog)[(c * 16 + n) * 8 + e] = lgw;
@@ -522,12 +524,13 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
     }
   } else if (warp < ws::kSoft) {
     // ---- conv2 epilogue: TMEM -> fp16 local features (operand of the logits and pooling GEMMs) --
+    // TMEM is read in the 16x256b shape: per 16-channel chunk a thread holds 4 rows x 4
+    // channels (rows g, g+8, g+16, g+24 of the warp's quarter; channels 2q, 2q+1, 8+2q,
+    // 9+2q), so it loads the constants of 4 channels instead of 16 broadcast loads (the
+    // shared-memory pipe bounds this kernel); each warp store covers 8 rows x 16 bytes.
     const int c0 = 32 * ((warp - ws::kEpi2) >> 2);
-    const int ri = 32 * quarter + lane;                       // row of tile 0; tile 1 row 128 + ri
+    const int q = lane & 3, g = lane >> 2;
     const bool live1 = 128 + 32 * quarter < 11 * kStripCols;
-    const int oh0 = ri / kStripCols, ow0 = ri - oh0 * kStripCols;
-    const int m1 = 128 + ri, oh1 = m1 / kStripCols, ow1 = m1 - oh1 * kStripCols;
-    const bool valid0 = oh0 < kH2 && ow0 < kW2, valid1 = oh1 < kH2 && ow1 < kW2;
     for (int i = 0; i < n_env; ++i) {
       const int b = i & 1, k = i >> 1;
       if (!warp_wait(s, &s.c2_full[b], k & 1, p.slots)) break;
@@ -540,39 +543,47 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
 #pragma unroll 1
       for (int c4 = 0; c4 < nchunk; ++c4) {
         const int t = c4 >> 1, cc = c0 + 16 * (c4 & 1);
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + ws::kColC2 + 128 * b + 64 * t + cc, r);
+        uint32_t ra[8], rb[8];
+        const uint32_t ta = tmem + lane_base + ws::kColC2 + 128 * b + 64 * t + cc;
+        tmem_ld16x256b_x2(ta, ra);                  // rows g, g+8 of the quarter
+        tmem_ld16x256b_x2(ta + (16u << 16), rb);    // rows 16+g, 24+g
         tmem_ld_wait();
         if (c4 == nchunk - 1) {            // the accumulators are read: conv2 of i+2 may start
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s.c2_empty[b]);
         }
-        uint32_t hw[8];
+        const float4 k0 = s.ck[cc + 2 * q], k1 = s.ck[cc + 2 * q + 1];
+        const float4 k2 = s.ck[cc + 8 + 2 * q], k3 = s.ck[cc + 9 + 2 * q];
+        uint8_t* tile = s.local16[lb] + 16384 * t + (cc >> 3) * 2048 + 4 * q;
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const int c = cc + j;
-          const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
-          const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
-          const float4 a24 = *reinterpret_cast<const float4*>(&s.a2[c]);
-          const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
-          const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)r[j], dq4.x, b24.x, a24.x, c24.x),
-                                                conv2_val((int32_t)r[j + 1], dq4.y, b24.y, a24.y, c24.y));
-          const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)r[j + 2], dq4.z, b24.z, a24.z, c24.z),
-                                                conv2_val((int32_t)r[j + 3], dq4.w, b24.w, a24.w, c24.w));
-          hw[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
-          hw[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
-        }
-        const uint4 v0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        const uint4 v1 = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-        uint8_t* lrow = s.local16[lb] + 16384 * t + ri * 16 + (cc >> 3) * 2048;
-        *reinterpret_cast<uint4*>(lrow) = v0;
-        *reinterpret_cast<uint4*>(lrow + 2048) = v1;
-        if (p.feat_out && (t ? valid1 : valid0)) {
-          const int tok = t ? oh1 * kW2 + ow1 : oh0 * kW2 + ow0;
-          uint4* dst = reinterpret_cast<uint4*>(p.feat_out + (e * kTok + tok) * kD + cc);
-          dst[0] = v0;
-          dst[1] = v1;
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t (&r)[8] = hh ? rb : ra;
+          const int row = 32 * quarter + 16 * hh + g;   // and row + 8
+          const __half2 h0 = __floats2half2_rn(conv2_val((int32_t)r[0], k0.x, k0.y, k0.z, k0.w),
+                                               conv2_val((int32_t)r[1], k1.x, k1.y, k1.z, k1.w));
+          const __half2 h1 = __floats2half2_rn(conv2_val((int32_t)r[2], k0.x, k0.y, k0.z, k0.w),
+                                               conv2_val((int32_t)r[3], k1.x, k1.y, k1.z, k1.w));
+          const __half2 h2 = __floats2half2_rn(conv2_val((int32_t)r[4], k2.x, k2.y, k2.z, k2.w),
+                                               conv2_val((int32_t)r[5], k3.x, k3.y, k3.z, k3.w));
+          const __half2 h3 = __floats2half2_rn(conv2_val((int32_t)r[6], k2.x, k2.y, k2.z, k2.w),
+                                               conv2_val((int32_t)r[7], k3.x, k3.y, k3.z, k3.w));
+          *reinterpret_cast<__half2*>(tile + row * 16) = h0;
+          *reinterpret_cast<__half2*>(tile + (row + 8) * 16) = h1;
+          *reinterpret_cast<__half2*>(tile + 2048 + row * 16) = h2;
+          *reinterpret_cast<__half2*>(tile + 2048 + (row + 8) * 16) = h3;
+          if (p.feat_out) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int m = 128 * t + row + 8 * j;
+              const int oh = m / kStripCols, ow = m - oh * kStripCols;
+              if (oh < kH2 && ow < kW2) {
+                __half2* dst = reinterpret_cast<__half2*>(p.feat_out + (e * kTok + oh * kW2 + ow) * kD + cc + 2 * q);
+                dst[0] = j ? h1 : h0;
+                dst[4] = j ? h3 : h2;
+              }
+            }
+          }
         }
       }
       fence_async_smem();

@@ -72,9 +72,8 @@ __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// GLAD_PDL=1 in the environment turns programmatic dependent launch on for the
-// fused forwards' kernel chains (read once per process; off by default).
-// On by default; GLAD_PDL=0 launches every kernel after its predecessor completes.
+// Programmatic dependent launch of the fused forwards' kernel chains is on by default
+// (read once per process); GLAD_PDL=0 launches every kernel after its predecessor completes.
 inline bool pdl_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("GLAD_PDL");
@@ -272,6 +271,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // Warp-collective: 2 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+// Whole warp: 16 lanes x 16 columns from TMEM (16x256b shape, two 8-column blocks). Thread
+// t = 4*g + q receives, for the 16 lanes starting at the address's lane field: r[0..1] =
+// lane g, columns 2q, 2q+1; r[2..3] = lane g+8, same columns; r[4..7] = the same for
+// columns 8+2q, 9+2q. Only the lane quarter of the executing warp is accessible.
+__device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t& r0, uint32_t& r1) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
                : "=r"(r0), "=r"(r1)
