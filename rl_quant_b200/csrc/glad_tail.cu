@@ -49,6 +49,7 @@ struct __align__(128) TailSmem {
   alignas(16) float dq[64];
   alignas(16) float b2[64];
   alignas(16) float a2c[64];
+  float4 ck[64];                  // conv2 epilogue constants per channel {dq, b2, a2, c2}
   alignas(16) float c2[64];
   float bin[192], bout[64];
   float wsq[64];                  // scorer weight, query half
@@ -160,6 +161,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   if (tid < 64) {
     s.bout[tid] = r_bout;
     s.wsq[tid] = r_wsq;
+    s.ck[tid] = make_float4(s.dq[tid], s.b2[tid], s.a2c[tid], s.c2[tid]);
   }
   if (tid < 192) s.bin[tid] = r_bin;
   for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9 (past the raw weights)
@@ -381,30 +383,39 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     if (s.abort_flag) break;
 
     // ---- 6. local features (fp16) -> A operand of the K|V projection (over the im2col bytes)
+    // TMEM read in the 16x256b shape: a thread holds rows g, g+8, g+16, g+24 of its warp and
+    // channels 2q, 2q+1, 8+2q, 9+2q of each 16-channel chunk, so it loads 4 channels'
+    // constants per chunk instead of 16
+    {
+      const int q = lane & 3, g = lane >> 2;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t ra[8], rb[8];
+        tmem_ld16x256b_x2(tcol + cb * 16, ra);
+        tmem_ld16x256b_x2(tcol + cb * 16 + (16u << 16), rb);
+        tmem_ld_wait();
+        const int cc = cb * 16;
+        const float4 k0 = s.ck[cc + 2 * q], k1 = s.ck[cc + 2 * q + 1];
+        const float4 k2 = s.ck[cc + 8 + 2 * q], k3 = s.ck[cc + 9 + 2 * q];
+        uint8_t* chunk = s.a12 + (2 * cb) * (kTailRows * 16) + 4 * q;
 #pragma unroll
-    for (int cb = 0; cb < 4; ++cb) {
-      uint32_t rr[16];
-      tmem_ld16(tcol + cb * 16, rr);
-      tmem_ld_wait();
-      uint32_t hw[8];
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        const int c = cb * 16 + j;
-        const float4 dq4 = *reinterpret_cast<const float4*>(&s.dq[c]);
-        const float4 b24 = *reinterpret_cast<const float4*>(&s.b2[c]);
-        const float4 a24 = *reinterpret_cast<const float4*>(&s.a2c[c]);
-        const float4 c24 = *reinterpret_cast<const float4*>(&s.c2[c]);
-        const __half2 h01 = __floats2half2_rn(conv2_val((int32_t)rr[j], dq4.x, b24.x, a24.x, c24.x),
-                                              conv2_val((int32_t)rr[j + 1], dq4.y, b24.y, a24.y, c24.y));
-        const __half2 h23 = __floats2half2_rn(conv2_val((int32_t)rr[j + 2], dq4.z, b24.z, a24.z, c24.z),
-                                              conv2_val((int32_t)rr[j + 3], dq4.w, b24.w, a24.w, c24.w));
-        hw[j >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
-        hw[(j >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t (&v)[8] = hh ? rb : ra;
+          const int row = 32 * warp + 16 * hh + g;      // and row + 8
+          const __half2 h0 = __floats2half2_rn(conv2_val((int32_t)v[0], k0.x, k0.y, k0.z, k0.w),
+                                               conv2_val((int32_t)v[1], k1.x, k1.y, k1.z, k1.w));
+          const __half2 h1 = __floats2half2_rn(conv2_val((int32_t)v[2], k0.x, k0.y, k0.z, k0.w),
+                                               conv2_val((int32_t)v[3], k1.x, k1.y, k1.z, k1.w));
+          const __half2 h2 = __floats2half2_rn(conv2_val((int32_t)v[4], k2.x, k2.y, k2.z, k2.w),
+                                               conv2_val((int32_t)v[5], k3.x, k3.y, k3.z, k3.w));
+          const __half2 h3 = __floats2half2_rn(conv2_val((int32_t)v[6], k2.x, k2.y, k2.z, k2.w),
+                                               conv2_val((int32_t)v[7], k3.x, k3.y, k3.z, k3.w));
+          *reinterpret_cast<__half2*>(chunk + row * 16) = h0;
+          *reinterpret_cast<__half2*>(chunk + (row + 8) * 16) = h1;
+          *reinterpret_cast<__half2*>(chunk + kTailRows * 16 + row * 16) = h2;
+          *reinterpret_cast<__half2*>(chunk + kTailRows * 16 + (row + 8) * 16) = h3;
+        }
       }
-      *reinterpret_cast<uint4*>(s.a12 + (2 * cb) * (kTailRows * 16) + r * 16) =
-          make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(s.a12 + (2 * cb + 1) * (kTailRows * 16) + r * 16) =
-          make_uint4(hw[4], hw[5], hw[6], hw[7]);
     }
     tc_fence_before();
     fence_async_smem();
