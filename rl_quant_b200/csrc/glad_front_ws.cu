@@ -539,48 +539,52 @@ __global__ void __launch_bounds__(ws::kThreads, 1) front_ws_kernel(const __grid_
         break;                                                  // local tile lb free
       tc_fence_after();
       const int64_t e = env_of(i);
-      const int nchunk = live1 ? 4 : 2;             // (tile 0, 16 channels) x 2, then tile 1
+      const int nt = live1 ? 2 : 1;
+      // per 16-channel chunk its constants are loaded once and serve both tiles
 #pragma unroll 1
-      for (int c4 = 0; c4 < nchunk; ++c4) {
-        const int t = c4 >> 1, cc = c0 + 16 * (c4 & 1);
-        uint32_t ra[8], rb[8];
-        const uint32_t ta = tmem + lane_base + ws::kColC2 + 128 * b + 64 * t + cc;
-        tmem_ld16x256b_x2(ta, ra);                  // rows g, g+8 of the quarter
-        tmem_ld16x256b_x2(ta + (16u << 16), rb);    // rows 16+g, 24+g
-        tmem_ld_wait();
-        if (c4 == nchunk - 1) {            // the accumulators are read: conv2 of i+2 may start
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.c2_empty[b]);
-        }
+      for (int hc = 0; hc < 2; ++hc) {
+        const int cc = c0 + 16 * hc;
         const float4 k0 = s.ck[cc + 2 * q], k1 = s.ck[cc + 2 * q + 1];
         const float4 k2 = s.ck[cc + 8 + 2 * q], k3 = s.ck[cc + 9 + 2 * q];
-        uint8_t* tile = s.local16[lb] + 16384 * t + (cc >> 3) * 2048 + 4 * q;
+#pragma unroll 1
+        for (int t = 0; t < nt; ++t) {
+          uint32_t ra[8], rb[8];
+          const uint32_t ta = tmem + lane_base + ws::kColC2 + 128 * b + 64 * t + cc;
+          tmem_ld16x256b_x2(ta, ra);                  // rows g, g+8 of the quarter
+          tmem_ld16x256b_x2(ta + (16u << 16), rb);    // rows 16+g, 24+g
+          tmem_ld_wait();
+          if (hc == 1 && t == nt - 1) {      // the accumulators are read: conv2 of i+2 may start
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.c2_empty[b]);
+          }
+          uint8_t* tile = s.local16[lb] + 16384 * t + (cc >> 3) * 2048 + 4 * q;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t (&r)[8] = hh ? rb : ra;
-          const int row = 32 * quarter + 16 * hh + g;   // and row + 8
-          const __half2 h0 = __floats2half2_rn(conv2_val((int32_t)r[0], k0.x, k0.y, k0.z, k0.w),
-                                               conv2_val((int32_t)r[1], k1.x, k1.y, k1.z, k1.w));
-          const __half2 h1 = __floats2half2_rn(conv2_val((int32_t)r[2], k0.x, k0.y, k0.z, k0.w),
-                                               conv2_val((int32_t)r[3], k1.x, k1.y, k1.z, k1.w));
-          const __half2 h2 = __floats2half2_rn(conv2_val((int32_t)r[4], k2.x, k2.y, k2.z, k2.w),
-                                               conv2_val((int32_t)r[5], k3.x, k3.y, k3.z, k3.w));
-          const __half2 h3 = __floats2half2_rn(conv2_val((int32_t)r[6], k2.x, k2.y, k2.z, k2.w),
-                                               conv2_val((int32_t)r[7], k3.x, k3.y, k3.z, k3.w));
-          *reinterpret_cast<__half2*>(tile + row * 16) = h0;
-          *reinterpret_cast<__half2*>(tile + (row + 8) * 16) = h1;
-          *reinterpret_cast<__half2*>(tile + 2048 + row * 16) = h2;
-          *reinterpret_cast<__half2*>(tile + 2048 + (row + 8) * 16) = h3;
-          if (p.feat_out) {
+          for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t (&r)[8] = hh ? rb : ra;
+            const int row = 32 * quarter + 16 * hh + g;   // and row + 8
+            const __half2 h0 = __floats2half2_rn(conv2_val((int32_t)r[0], k0.x, k0.y, k0.z, k0.w),
+                                                 conv2_val((int32_t)r[1], k1.x, k1.y, k1.z, k1.w));
+            const __half2 h1 = __floats2half2_rn(conv2_val((int32_t)r[2], k0.x, k0.y, k0.z, k0.w),
+                                                 conv2_val((int32_t)r[3], k1.x, k1.y, k1.z, k1.w));
+            const __half2 h2 = __floats2half2_rn(conv2_val((int32_t)r[4], k2.x, k2.y, k2.z, k2.w),
+                                                 conv2_val((int32_t)r[5], k3.x, k3.y, k3.z, k3.w));
+            const __half2 h3 = __floats2half2_rn(conv2_val((int32_t)r[6], k2.x, k2.y, k2.z, k2.w),
+                                                 conv2_val((int32_t)r[7], k3.x, k3.y, k3.z, k3.w));
+            *reinterpret_cast<__half2*>(tile + row * 16) = h0;
+            *reinterpret_cast<__half2*>(tile + (row + 8) * 16) = h1;
+            *reinterpret_cast<__half2*>(tile + 2048 + row * 16) = h2;
+            *reinterpret_cast<__half2*>(tile + 2048 + (row + 8) * 16) = h3;
+            if (p.feat_out) {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int m = 128 * t + row + 8 * j;
-              const int oh = m / kStripCols, ow = m - oh * kStripCols;
-              if (oh < kH2 && ow < kW2) {
-                __half2* dst = reinterpret_cast<__half2*>(p.feat_out + (e * kTok + oh * kW2 + ow) * kD + cc + 2 * q);
-                dst[0] = j ? h1 : h0;
-                dst[4] = j ? h3 : h2;
+              for (int j = 0; j < 2; ++j) {
+                const int m = 128 * t + row + 8 * j;
+                const int oh = m / kStripCols, ow = m - oh * kStripCols;
+                if (oh < kH2 && ow < kW2) {
+                  __half2* dst = reinterpret_cast<__half2*>(p.feat_out + (e * kTok + oh * kW2 + ow) * kD + cc + 2 * q);
+                  dst[0] = j ? h1 : h0;
+                  dst[4] = j ? h3 : h2;
+                }
               }
             }
           }
