@@ -52,6 +52,7 @@ struct __align__(128) TailSmem {
   float4 ck[64];                  // conv2 epilogue constants per channel {dq, b2, a2, c2}
   alignas(16) float c2[64];
   float bin[192], bout[64];
+  __half2 binh[64];              // in_proj bias of K (pairs 0-31) and V (32-63) as half2
   float wsq[64];                  // scorer weight, query half
   float a0_a[232], a0_b[232];
   float qv[kTailWarps][64];        // query (fp16 values)
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
     s.ck[tid] = make_float4(s.dq[tid], s.b2[tid], s.a2c[tid], s.c2[tid]);
   }
   if (tid < 192) s.bin[tid] = r_bin;
+  if (tid < 64) s.binh[tid] = __halves2half2(p.in_b[64 + 2 * tid], p.in_b[65 + 2 * tid]);
   for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9 (past the raw weights)
     reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
   const int64_t ngroups = (p.B + kTailEnvs - 1) / kTailEnvs;
@@ -457,8 +459,10 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           const int c = 16 * cb + 4 * hh + e;
-          const float2 k0 = fp16r2(__uint_as_float(rr[4 * hh + e]), __uint_as_float(rr[4 * hh + e + 1]));
-          const float2 kv = fp16r2(__fadd_rn(k0.x, s.bin[64 + c]), __fadd_rn(k0.y, s.bin[64 + c + 1]));
+          // fp16(fp16(k) + b): one half2 add (the fp32 sum of two fp16 values rounds to the
+          // same fp16 as the exact sum, which is what the half add returns)
+          const __half2 k0 = __floats2half2_rn(__uint_as_float(rr[4 * hh + e]), __uint_as_float(rr[4 * hh + e + 1]));
+          const float2 kv = __half22float2(__hadd2(k0, s.binh[c >> 1]));
           d = fmaf(s.qm[warp][c], kv.x, d);
           d = fmaf(s.qm[warp][c + 1], kv.y, d);
         }
@@ -502,8 +506,8 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {
         const int c = 16 * cb + j;
-        const float2 v0 = fp16r2(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]));
-        const float2 vb = fp16r2(__fadd_rn(v0.x, s.bin[128 + c]), __fadd_rn(v0.y, s.bin[128 + c + 1]));
+        const __half2 v0 = __floats2half2_rn(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]));
+        const float2 vb = __half22float2(__hadd2(v0, s.binh[32 + (c >> 1)]));
         v[j] = sc[4 * cb + (j >> 2)] * vb.x;
         v[j + 1] = sc[4 * cb + (j >> 2)] * vb.y;
       }
