@@ -53,6 +53,7 @@ struct __align__(128) TailSmem {
   alignas(16) float c2[64];
   float bin[192], bout[64];
   __half2 binh[64];              // in_proj bias of K (pairs 0-31) and V (32-63) as half2
+  __half2 bqh[32], bouth[32];    // in_proj bias of Q and out_proj bias as half2 pairs
   float wsq[64];                  // scorer weight, query half
   float a0_a[232], a0_b[232];
   float qv[kTailWarps][64];        // query (fp16 values)
@@ -166,6 +167,10 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
   }
   if (tid < 192) s.bin[tid] = r_bin;
   if (tid < 64) s.binh[tid] = __halves2half2(p.in_b[64 + 2 * tid], p.in_b[65 + 2 * tid]);
+  if (tid < 32) {
+    s.bqh[tid] = __halves2half2(p.in_b[2 * tid], p.in_b[2 * tid + 1]);
+    s.bouth[tid] = __halves2half2(p.out_b[2 * tid], p.out_b[2 * tid + 1]);
+  }
   for (int idx = tid; idx < kTailRows; idx += NT)      // zero filler tap 9 (past the raw weights)
     reinterpret_cast<uint4*>(s.a12 + 9 * kTailRows * 16)[idx] = make_uint4(0, 0, 0, 0);
   const int64_t ngroups = (p.B + kTailEnvs - 1) / kTailEnvs;
@@ -251,16 +256,18 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       const float sq = fp16r(__fadd_rn(fp16r(sqp), sb));
       __syncwarp();
       // ---- 3. top-32 over 187 logits, value desc / index asc ------------------------------
+      // fp16 logit = fp16(score_local + score_query): a half add (the fp32 sum of two fp16
+      // values rounds to the same fp16 as the exact sum); the Gumbel term is fp16-valued too
       uint32_t key[6];
+      const __half sqh = __float2half_rn(sq);
 #pragma unroll
       for (int j = 0; j < 6; ++j) {
         const int i = lane + 32 * j;
         key[j] = 0;
         if (i < kTok) {
-          float lg = fp16r(__fadd_rn(__half2float(sl[j]), sq));
-          if (p.gumbel) lg = fp16r(__fadd_rn(lg, gumbel16(p.gumbel_seed, g_offset, env, i)));
-          else if (p.noise) lg = fp16r(__fadd_rn(lg, p.noise[env * kTok + i]));
-          const __half lh = __float2half_rn(lg);
+          __half lh = __hadd_rn(sl[j], sqh);
+          if (p.gumbel) lh = __hadd_rn(lh, __float2half_rn(gumbel16(p.gumbel_seed, g_offset, env, i)));
+          else if (p.noise) lh = __float2half_rn(__fadd_rn(__half2float(lh), p.noise[env * kTok + i]));
           if (p.topk_logits_out) p.topk_logits_out[env * kTok + i] = lh;
           key[j] = (ord16(lh) << 16) | (uint32_t)(0xFFFF - i);
         }
@@ -342,8 +349,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
           a1 = fmaf(x0, w1.x, a1);
           a1 = fmaf(x1, w1.y, a1);
         }
-        const float2 a01 = fp16r2(a0, a1);
-        const float2 qm = fp16r2(__fadd_rn(a01.x, s.bin[2 * lane]), __fadd_rn(a01.y, s.bin[2 * lane + 1]));
+        const float2 qm = __half22float2(__hadd2_rn(__floats2half2_rn(a0, a1), s.bqh[lane]));
         s.qm[warp][2 * lane] = qm.x;
         s.qm[warp][2 * lane + 1] = qm.y;
       }
@@ -462,7 +468,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
           // fp16(fp16(k) + b): one half2 add (the fp32 sum of two fp16 values rounds to the
           // same fp16 as the exact sum, which is what the half add returns)
           const __half2 k0 = __floats2half2_rn(__uint_as_float(rr[4 * hh + e]), __uint_as_float(rr[4 * hh + e + 1]));
-          const float2 kv = __half22float2(__hadd2(k0, s.binh[c >> 1]));
+          const float2 kv = __half22float2(__hadd2_rn(k0, s.binh[c >> 1]));
           d = fmaf(s.qm[warp][c], kv.x, d);
           d = fmaf(s.qm[warp][c + 1], kv.y, d);
         }
@@ -470,8 +476,8 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       }
 #pragma unroll
       for (int hh = 0; hh < 4; hh += 2) {
-        const float2 d01 = fp16r2(dd[hh], dd[hh + 1]);
-        const float2 s01 = fp16r2(__fmul_rn(d01.x, 0.5f), __fmul_rn(d01.y, 0.5f));
+        // fp16(fp16(d) * 0.5): a half multiply by 0.5 rounds the same exact product
+        const float2 s01 = __half22float2(__hmul2_rn(__floats2half2_rn(dd[hh], dd[hh + 1]), __float2half2_rn(0.5f)));
         sc[4 * cb + hh] = s01.x;
         sc[4 * cb + hh + 1] = s01.y;
       }
@@ -507,7 +513,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
       for (int j = 0; j < 16; j += 2) {
         const int c = 16 * cb + j;
         const __half2 v0 = __floats2half2_rn(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]));
-        const float2 vb = __half22float2(__hadd2(v0, s.binh[32 + (c >> 1)]));
+        const float2 vb = __half22float2(__hadd2_rn(v0, s.binh[32 + (c >> 1)]));
         v[j] = sc[4 * cb + (j >> 2)] * vb.x;
         v[j + 1] = sc[4 * cb + (j >> 2)] * vb.y;
       }
@@ -530,8 +536,7 @@ __global__ void __launch_bounds__(kTailThreads, 2) tail_kernel(const __grid_cons
         a1 = fmaf(x0, w1.x, a1);
         a1 = fmaf(x1, w1.y, a1);
       }
-      const float2 a01 = fp16r2(a0, a1);
-      const float2 f01 = fp16r2(__fadd_rn(a01.x, s.bout[2 * lane]), __fadd_rn(a01.y, s.bout[2 * lane + 1]));
+      const float2 f01 = __half22float2(__hadd2_rn(__floats2half2_rn(a0, a1), s.bouth[lane]));
       const float f0 = f01.x, f1 = f01.y;
       reinterpret_cast<__half2*>(p.enc + env * p.ld_enc)[lane] = __floats2half2_rn(f0, f1);
       if (p.act_mode == GLAD_ACT_DYNAMIC && p.a0_absmax) {
