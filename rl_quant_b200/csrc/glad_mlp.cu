@@ -286,8 +286,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     }
   }
   cp_async_commit();
-  // weight slices of all four layers, in flight while the input is quantised
+  // weight slices of all four layers, in flight while the input is quantised; layer 0's
+  // are a group of their own, so its MMA waits for those alone
   mlp_load_w<224, 128>(sm + kOffW0, p.L[0].w8, (int)rank * 128, tid);
+  cp_async_commit();
   mlp_load_w<512, 64>(sm + kOffW1, p.L[1].w8, (int)rank * 64, tid);
   mlp_load_w<256, 32>(sm + kOffW2, p.L[2].w8, (int)rank * 32, tid);
   if (rank == 0) mlp_load_w<128, 32>(sm + kOffW3, p.L[3].w8, 0, tid);
@@ -307,7 +309,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     in1 = src[1];
   }
   ActQuant aq = make_act_quant(p.L[0], p.act_mode, p.slots, 2);   // input of the running layer
-  cp_async_wait_group<1>();             // constants landed; the weights may still be in flight
+  cp_async_wait_group<2>();             // constants landed; the weights may still be in flight
   __syncthreads();
   tc_fence_before();
   cluster_sync_all();                            // every CTA of the cluster runs before DSMEM stores
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
 #pragma unroll
     for (int r = 0; r < kMlpCluster; ++r) st_cluster_v4(mapa_shared(off, r), q);
   }
-  cp_async_wait_all();
+  cp_async_wait_group<1>();             // layer 0's weight slice (the later layers' may still land)
   fence_async_smem();
   fence_async_cluster();
   cluster_sync_all();
@@ -409,6 +411,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
 #pragma unroll
         for (int r = 0; r < kMlpCluster; ++r) st_cluster_v4(mapa_shared(off, r), q);
       }
+    }
+    if (l == 0) {                          // the later layers' weight slices, before layer 1's MMA
+      cp_async_wait_all();
+      fence_async_smem();
     }
     fence_async_cluster();
     cluster_sync_all();
