@@ -19,6 +19,8 @@
 // after 2 s, set a status bit and let the kernel finish.
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "glad_common.cuh"
 
 namespace glad {
@@ -164,31 +166,40 @@ __device__ __forceinline__ void mlp_mma(uint8_t* sm, uint32_t tmem, uint64_t* mb
 
 // 16 accumulator columns at `taddr`: the sum of the kMlpChains partial chains (int32,
 // exact), chain c at column offset c * nj; all chains' loads are in flight before one wait.
-__device__ __forceinline__ void mlp_ld_acc(uint32_t taddr, int nj, uint32_t (&r)[16]) {
-  uint32_t t[kMlpChains - 1][16];
-  tmem_ld16(taddr, r);
+template <int W>
+__device__ __forceinline__ void mlp_ld_acc(uint32_t taddr, int nj, uint32_t (&r)[W]) {
+  static_assert(W == 8 || W == 16, "8 or 16 columns");
+  uint32_t t[kMlpChains - 1][W];
+  if constexpr (W == 16) {
+    tmem_ld16(taddr, r);
 #pragma unroll
-  for (int c = 1; c < kMlpChains; ++c) tmem_ld16(taddr + (uint32_t)(c * nj), t[c - 1]);
+    for (int c = 1; c < kMlpChains; ++c) tmem_ld16(taddr + (uint32_t)(c * nj), t[c - 1]);
+  } else {
+    tmem_ld8(taddr, r);
+#pragma unroll
+    for (int c = 1; c < kMlpChains; ++c) tmem_ld8(taddr + (uint32_t)(c * nj), t[c - 1]);
+  }
   tmem_ld_wait();
 #pragma unroll
   for (int c = 1; c < kMlpChains; ++c)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) r[j] += t[c - 1][j];
+    for (int j = 0; j < W; ++j) r[j] += t[c - 1][j];
 }
 
 // 16 int32 accumulators -> fp32, exactly: through the mantissa of 1.5*2^23 (two ALU
 // operations) when every |acc| < 2^22, which the OR of the offset values shows, else
 // by the conversion instruction.
-__device__ __forceinline__ void mlp_acc_f32(const uint32_t (&r)[16], float (&a)[16]) {
+template <int W>
+__device__ __forceinline__ void mlp_acc_f32(const uint32_t (&r)[W], float (&a)[W]) {
   uint32_t span = 0;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) span |= r[j] + (1u << 22);
+  for (int j = 0; j < W; ++j) span |= r[j] + (1u << 22);
   if (span < (1u << 23)) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) a[j] = i2f_small((int32_t)r[j]);
+    for (int j = 0; j < W; ++j) a[j] = i2f_small((int32_t)r[j]);
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) a[j] = (float)(int32_t)r[j];
+    for (int j = 0; j < W; ++j) a[j] = (float)(int32_t)r[j];
   }
 }
 
@@ -347,15 +358,18 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     float zmax = 0.0f;
     if (!*abort_flag) {
 #pragma unroll 1
-      for (int ch = part; ch < nch; ch += 4) {
-        uint32_t r[16];
-        mlp_ld_acc(tmem + lane_base + ch * 16, NJ, r);
-        float a[16];
-        mlp_acc_f32(r, a);
-        uint32_t h[8];
+      // work units of 16 columns; a layer with only two 16-column chunks (actor.4) is cut
+      // into 8-column halves so that all four warps of each lane quarter take part
+      auto unit = [&](auto wc, int c0) {
+        constexpr int W = decltype(wc)::value;
+        uint32_t r[W];
+        mlp_ld_acc<W>(tmem + lane_base + c0, NJ, r);
+        float a[W];
+        mlp_acc_f32<W>(r, a);
+        uint32_t h[W / 2];
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const int c = CB + ch * 16 + j;
+        for (int j = 0; j < W; j += 4) {
+          const int c = CB + c0 + j;
           const float4 sc = *reinterpret_cast<const float4*>(&F[kFSc + c]);
           const float4 bp = *reinterpret_cast<const float4*>(&F[kFBp + c]);
           // y = fp16(acc*scale + b') (qlinear_out32), then ELU in fp32 rounded to fp16
@@ -379,8 +393,17 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
             }
           }
         }
-        H[(ch * 2) * 128 + row] = make_uint4(h[0], h[1], h[2], h[3]);
-        H[(ch * 2 + 1) * 128 + row] = make_uint4(h[4], h[5], h[6], h[7]);
+        // H: [16-column chunk][8-column half][128 rows][8 halves]; c0 / 8 indexes the halves
+#pragma unroll
+        for (int u = 0; u < W / 8; ++u)
+          H[(c0 / 8 + u) * 128 + row] = make_uint4(h[4 * u], h[4 * u + 1], h[4 * u + 2], h[4 * u + 3]);
+      };
+      if (nch >= 4) {
+#pragma unroll 1
+        for (int ch = part; ch < nch; ch += 4) unit(std::integral_constant<int, 16>{}, ch * 16);
+      } else {
+#pragma unroll 1
+        for (int u8 = part; u8 < 2 * nch; u8 += 4) unit(std::integral_constant<int, 8>{}, u8 * 8);
       }
     }
     tc_fence_before();
