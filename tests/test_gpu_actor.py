@@ -1,6 +1,6 @@
 """Fused actor forward (glad_actor_forward) vs the oracle and the reference goldens.
 
-Tolerances: action means within max-abs 1e-2 and
+Tolerances of this path's accuracy target: action means within max-abs 1e-2 and
 cosine >= 0.99999 of qrt's INT8 path; integer results bit-exact; top-32 index
 sets exact on the logits the kernel selected from (value desc, lower index
 first on ties).

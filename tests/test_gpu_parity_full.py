@@ -10,7 +10,7 @@ groups. Every comparison is against the oracle (the reference's INT8 path
 restated on the CPU, qrt/encoder_opt.py:41-123, qrt/qlinear.py:111-138,
 qrt/qconv.py:54-163), computed over the whole batch.
 
-Tiers (north star: int32 accumulators and top-32 indices bit-exact, means and
+Tiers (the accuracy target: int32 accumulators and top-32 indices bit-exact, means and
 values within max-abs 1e-2 and cosine >= 0.99999):
 - z8 equal except rounding ties (one step, the oracle's pre-rounding value
   within 1e-3 of a half-integer);
